@@ -1,0 +1,348 @@
+"""Benchmark of the Palu decode-attention hot path on B200 (one JSON line on rank 0).
+
+Workload (the north star's target): one Llama-3.1-8B-shaped attention layer, M-LRD rank_k = rank_v = 64,
+32 query / 8 KV heads, head_dim 128, batch 32, cached context 8192 (every row attends all 8192
+positions), bf16 latents ~ N(0,1), U ~ N(0, 1/64), llama3 RoPE table. Synthetic, seeded, created on
+the device. A step is one decode-attention call (fused kernel + split merge) over the whole cache.
+
+Multi-GPU (torchrun, one rank per GPU): KV heads are sharded, 8/N per rank, over a global batch of
+32*N rows, so every rank holds the same latent bytes (weak scaling; no collective inside the op).
+
+Also reported: e2e (the same op through the C ABI with host buffers: the step's query and new latents
+copied in from pinned memory, the latents appended, the output copied back, all inside the timed
+region), the roofline of the decode kernel against MEASURED_PEAKS.json, and the CPU oracle timed on a
+bounded sample on this host. ``--impl reference`` times the reference's CPU implementation of the path
+(the oracle restatement of palu_tt/fused.py:reference_decode) on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "tt-cadlab_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import torch  # noqa: E402
+
+METRIC = "decode-attn µs/layer & latent HBM GB/s vs 8 TB/s; tokens/s at 1/2/4/8 B200"
+B_PER_GPU, N_Q, N_KV, S, R = 32, 32, 8, 8192, 64
+THETA = 500000.0
+LLAMA3 = {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+          "original_max_position_embeddings": 8192}
+L2_BYTES = 126 * 1024 * 1024
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_record():
+    """dram read+write bytes per launch of the decode kernel, from the committed ncu summary."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text())
+    except ValueError:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons, sampled every 200 ms while the timed region runs."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_layer(dev, B, n_q, n_kv, seed):
+    from palu_b200 import fused
+    g = torch.Generator(device=dev).manual_seed(seed)
+    k = torch.randn(B, n_kv, S, R, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    v = torch.randn(B, n_kv, S, R, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    u = (torch.randn(n_kv, R, 128, generator=g, device=dev) / R ** 0.5).to(torch.bfloat16)
+    q = torch.randn(B, n_q, 128, generator=g, device=dev).to(torch.bfloat16)
+    pos = torch.full((B,), S - 1, dtype=torch.int32, device=dev)
+    cos, sin = fused.cos_sin_tables(128, S, THETA, LLAMA3)
+    cs = fused.pack_cs_table(fused.cs_table(cos, sin, S).to(dev, torch.bfloat16))
+    return dict(k=k, v=v, u=u, q=q, pos=pos, cs=cs)
+
+
+def cpu_oracle_rate(budget_s: float, rows_per_sample: int = 1):
+    """Time the oracle (reference_decode restated) on whole batch rows of the workload until the
+    budget is spent; returns (rows/s, threads, description)."""
+    import oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(5)
+    bf = lambda t: t.to(torch.bfloat16).float()
+    q = bf(torch.randn(1, rows_per_sample, N_Q, 128, generator=g))
+    k = bf(torch.randn(rows_per_sample, N_KV, S, R, generator=g))
+    v = bf(torch.randn(rows_per_sample, N_KV, S, R, generator=g))
+    u = bf(torch.randn(N_KV, R, 128, generator=g) / R ** 0.5)
+    cos, sin = oracle.cos_sin_tables(128, S, THETA, LLAMA3)
+    cos, sin = bf(cos[:S]), bf(sin[:S])
+    pos = torch.full((rows_per_sample,), S - 1)
+    oracle.reference_decode(q, k, u, v, pos, cos, sin, 128 ** -0.5)   # warm-up
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        oracle.reference_decode(q, k, u, v, pos, cos, sin, 128 ** -0.5)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return rows_per_sample / med, threads, (f"{rows_per_sample} of {B_PER_GPU} batch rows (all {N_KV} KV heads, "
+                                            f"S={S}, r=64) per sample, median of {len(times)} samples, "
+                                            f"reference_decode (fp32 torch) on {threads} threads")
+
+
+def run_reference(args, ws, rank):
+    """--impl reference: the reference's CPU implementation on the same workload, rank 0 only."""
+    if rank != 0:
+        return
+    rows = 1
+    import oracle
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(5)
+    bf = lambda t: t.to(torch.bfloat16).float()
+    q = bf(torch.randn(1, rows, N_Q, 128, generator=g))
+    k = bf(torch.randn(rows, N_KV, S, R, generator=g))
+    v = bf(torch.randn(rows, N_KV, S, R, generator=g))
+    u = bf(torch.randn(N_KV, R, 128, generator=g) / R ** 0.5)
+    cos, sin = oracle.cos_sin_tables(128, S, THETA, LLAMA3)
+    cos, sin = bf(cos[:S]), bf(sin[:S])
+    pos = torch.full((rows,), S - 1)
+    for _ in range(args.warmup):
+        oracle.reference_decode(q, k, u, v, pos, cos, sin, 128 ** -0.5)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.reference_decode(q, k, u, v, pos, cos, sin, 128 ** -0.5)
+        times.append(time.perf_counter() - t0)
+    t_row = statistics.median(times) / rows
+    # whole-job rate on the bench's workload: global batch rows / time, extrapolated per row
+    rows_total = B_PER_GPU * ws
+    value = rows_total / (t_row * rows_total)
+    cores = torch.get_num_threads()
+    sample = (f"{rows} of {B_PER_GPU} batch rows per step (all {N_KV} KV heads, S={S}, r=64); "
+              f"palu_tt/fused.py:reference_decode restated in fp32 torch on {cores} threads")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_row * B_PER_GPU * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": workload_config(ws),
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(ws):
+    return {"workload": "mlrd_r64_b32_s8192", "model": "Llama-3.1-8B attention layer (M-LRD, absorbed V)",
+            "global_batch": B_PER_GPU * ws, "seq_len": S, "rank_k": R, "rank_v": R, "n_q_heads": N_Q,
+            "n_kv_heads": N_KV, "kv_heads_per_gpu": N_KV // ws, "parallelism": f"kv-head shard x{ws}",
+            "l2": "no flush: each step reads 537 MB of latents (> 126 MB L2)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    args = ap.parse_args()
+    ws, rank, local = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, ws, rank)
+
+    from palu_b200 import _lib, fused
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    if N_KV % ws:
+        raise SystemExit(f"{N_KV} KV heads do not shard over {ws} GPUs")
+    B = B_PER_GPU * ws
+    n_kv = N_KV // ws
+    n_q = N_Q // ws
+    L = make_layer(dev, B, n_q, n_kv, seed=1234 + rank)
+    out = torch.empty(B, n_q, R, dtype=torch.bfloat16, device=dev)
+    d = _lib.dims(B, n_q, n_kv, n_kv, R, R, S)
+    ws_buf = torch.empty(_lib.workspace_bytes(d), dtype=torch.uint8, device=dev)
+
+    def step():
+        fused.decode(L["q"], L["k"], L["v"], L["u"], L["cs"], L["pos"], out=out, workspace=ws_buf)
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if ws > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    # ---- device-resident timing -------------------------------------------------------------------
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+    barrier()
+    with ClockSampler(local) as clk:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(args.steps):
+            evs[2 * i].record(stream)
+            step()
+            evs[2 * i + 1].record(stream)
+        t1.record(stream)
+        barrier()
+    total_ms = t0.elapsed_time(t1)
+    per_launch = [evs[2 * i].elapsed_time(evs[2 * i + 1]) for i in range(args.steps)]
+    if ws > 1:
+        tt = torch.tensor([total_ms], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        total_ms = float(tt.item())
+    ms = total_ms / args.steps
+    value = B / (ms * 1e-3)   # global batch rows per second (each rank does the same per-rank work)
+
+    # ---- e2e through the C ABI with host buffers ---------------------------------------------------
+    q_h = torch.randn(B, n_q, 128).to(torch.bfloat16).pin_memory()
+    nk_h = torch.randn(B, n_kv, R).to(torch.bfloat16).pin_memory()
+    nv_h = torch.randn(B, n_kv, R).to(torch.bfloat16).pin_memory()
+    pos_h = torch.full((B,), S - 1, dtype=torch.int32).pin_memory()
+    out_h = torch.empty(B, n_q, R, dtype=torch.bfloat16).pin_memory()
+    q_d, nk_d, nv_d, pos_d = (torch.empty_like(t, device=dev) for t in (q_h, nk_h, nv_h, pos_h))
+
+    def e2e_step():
+        q_d.copy_(q_h, non_blocking=True)
+        nk_d.copy_(nk_h, non_blocking=True)
+        nv_d.copy_(nv_h, non_blocking=True)
+        pos_d.copy_(pos_h, non_blocking=True)
+        fused.append_latents(nk_d, nv_d, pos_d, L["k"], L["v"])
+        fused.decode(q_d, L["k"], L["v"], L["u"], L["cs"], pos_d, out=out, workspace=ws_buf)
+        out_h.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if ws > 1:
+        tt = torch.tensor([e2e_ms], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+    h2d = sum(t.numel() * t.element_size() for t in (q_h, nk_h, nv_h, pos_h))
+    d2h = out_h.numel() * out_h.element_size()
+
+    # ---- roofline of the op on this rank -----------------------------------------------------------
+    per_launch_ms = statistics.mean(per_launch)
+    latent_bytes = B * n_kv * S * (R + R) * 2
+    u_bytes = n_kv * R * 128 * 2
+    alg_bytes = latent_bytes + u_bytes
+    achieved = alg_bytes / (per_launch_ms * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+    tr = traffic_record()
+
+    if rank == 0:
+        cpu = None
+        if ws == 1:
+            rate, cores, sample = cpu_oracle_rate(args.cpu_budget)
+            cpu = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, on device)",
+            "config": workload_config(ws),
+            "us_per_layer": ms * 1e3, "latent_GBps": achieved,
+            "e2e": {"value": B / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": (tr or {}).get("bytes_per_launch"),
+                         "kernel": "palu_decode_mma_kernel + palu_combine_kernel (one op)",
+                         "algorithmic_bytes": alg_bytes},
+            "cpu_baseline": cpu,
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

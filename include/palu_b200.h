@@ -1,0 +1,124 @@
+/*
+ * palu_b200.h -- C ABI of the B200 (sm_100a) Palu compressed-KV decode-attention library.
+ *
+ * Conventions for every entry point:
+ *   - all tensor pointers are device pointers, owned by the caller, row-major and contiguous in the
+ *     layouts stated below; bf16 means IEEE bfloat16 (cuda_bf16.h __nv_bfloat16);
+ *   - work is enqueued on `stream` (NULL = the legacy default stream) and the call returns without
+ *     synchronising; errors found before launch return a nonzero status and launch nothing;
+ *   - the return value is PALU_OK (0) or a PALU_ERR_* code; palu_last_error() then describes the
+ *     failure in the calling thread (thread-local). The messages reuse the substrings of the
+ *     reference op's validation errors ("r_k", "cs_tab", "heads_per_group", "u_v", "head_dim_v", ...).
+ *   - head_dim is 128 throughout (the reference envelope).
+ *
+ * Reference interfaces replaced (paths inside the ryankert01/tt-cadlab tree):
+ *   palu_decode_attn       <- ttnn.transformer.palu_sdpa_decode, called at palu_tt/attention.py:633-639,
+ *                             CPU model palu_tt/fused.py:82-107
+ *   palu_workspace_bytes   <- (no reference counterpart: the Tensix op sizes its own circular buffers,
+ *                             palu_tt/fused.py:145-201); the split-K partials live in caller memory here
+ *   palu_append_latents    <- ttnn.experimental.paged_update_cache x2, palu_tt/attention.py:612-625
+ *   palu_plain_gqa_decode  <- ttnn.transformer.flash_multi_latent_attention_decode / stock
+ *                             scaled_dot_product_attention_decode on full K, palu_tt/attention.py:703-706,
+ *                             tests/test_palu_sdpa_device.py:58-65, 238-241
+ *   palu_pack_cs_table     <- the cs_tab upload of palu_tt/attention.py:70-72 (fused.py:62-73 layout)
+ */
+#ifndef PALU_B200_H
+#define PALU_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* palu_stream_t; /* the same handle type as cudaStream_t */
+
+enum palu_status {
+  PALU_OK = 0,
+  PALU_ERR_INVALID = 1,   /* shapes / envelope / null pointers */
+  PALU_ERR_WORKSPACE = 2, /* workspace missing or smaller than palu_workspace_bytes() */
+  PALU_ERR_CUDA = 3       /* a CUDA runtime error (launch failure, no device, ...) */
+};
+
+enum palu_dtype { PALU_BF16 = 0, PALU_F32 = 1 };
+
+/* Shapes of one decode-attention call (the local shard on this GPU). */
+typedef struct palu_decode_dims {
+  int32_t batch;      /* B */
+  int32_t n_q_heads;  /* query heads; n_q_heads / n_kv_heads query heads share a KV head */
+  int32_t n_kv_heads; /* KV heads */
+  int32_t n_groups;   /* latent heads in the caches: n_kv_heads (M-LRD) or n_kv_heads / group size (G-LRD) */
+  int32_t head_dim;   /* must be 128 */
+  int32_t r_k;        /* K latent width (multiple of 16) */
+  int32_t r_v;        /* V latent width (multiple of 16) */
+  int32_t max_seq;    /* cache rows per (batch row, latent head) */
+  int32_t splits;     /* split-K partitions per (batch row, KV head); 0 = choose for this GPU */
+} palu_decode_dims;
+
+/*
+ * Fused decode attention over latent caches (replaces palu_sdpa_decode).
+ *
+ *   q        [B][n_q_heads][128] bf16, already rotated (RoPE at the query position)
+ *   k_lat    [B][n_groups][max_seq][r_k] bf16 latent K cache
+ *   v_lat    [B][n_groups][max_seq][r_v] bf16 latent V cache
+ *   u_k      [n_kv_heads][r_k] rows of u_k_ld bf16 elements; the first 128 of a row are U_k in Meta
+ *            (interleaved-pair) order. u_k_ld = 128 for u_k itself, 256 for w_rot = [u_k | u_k T].
+ *   u_v      NULL: absorbed V (M-LRD) -- the output is the attention-weighted V latent, r_v wide;
+ *            else [n_kv_heads][r_v][128] bf16 -- V rebuilt per head (G-LRD), the output is 128 wide.
+ *   cs_pairs [>= max_seq][64] packed rows from palu_pack_cs_table: (cos, sin) of frequency j at
+ *            position s as a bf16 pair (cos in the low half)
+ *   cur_pos  [B] int32: last visible position of each row (inclusive); < 0 skips the row (zeros out)
+ *   out      [B][n_q_heads][r_v or 128], out_dtype PALU_BF16 or PALU_F32
+ *   workspace / workspace_bytes: >= palu_workspace_bytes(dims) bytes of device memory
+ *   scale    softmax scale (the reference passes head_dim ** -0.5)
+ * Query head h attends KV head h / (n_q_heads / n_kv_heads), which reads latent head
+ * kv / (n_kv_heads / n_groups). Positions above cur_pos[b] are masked; cur_pos[b] >= max_seq is
+ * clamped to max_seq - 1.
+ */
+int palu_decode_attn(const void* q, const void* k_lat, const void* v_lat, const void* u_k, int64_t u_k_ld,
+                     const void* u_v, const void* cs_pairs, const int32_t* cur_pos, void* out, int32_t out_dtype,
+                     void* workspace, size_t workspace_bytes, const palu_decode_dims* dims, float scale,
+                     palu_stream_t stream);
+
+/* Device bytes palu_decode_attn / palu_plain_gqa_decode need for their split-K partials. */
+size_t palu_workspace_bytes(const palu_decode_dims* dims);
+
+/* The split count a call with dims->splits == 0 uses on the current device. */
+int32_t palu_choose_splits(const palu_decode_dims* dims);
+
+/*
+ * Append one decode step's latents at cur_pos[b] (replaces the two paged_update_cache calls).
+ *   new_k [B][n_groups][r_k] bf16, new_v [B][n_groups][r_v] bf16; rows with cur_pos outside
+ *   [0, max_seq) are skipped. Caches as in palu_decode_attn.
+ */
+int palu_append_latents(const void* new_k, const void* new_v, const int32_t* cur_pos, void* k_cache, void* v_cache,
+                        const palu_decode_dims* dims, palu_stream_t stream);
+
+/*
+ * Plain GQA flash-decode over full, already-rotated K (the identity comparison path).
+ *   k [B][n_kv_heads][max_seq][128] bf16, v [B][n_kv_heads][max_seq][dims->r_v] bf16,
+ *   out [B][n_q_heads][r_v]. dims->n_groups must equal n_kv_heads and dims->r_k must be 128.
+ */
+int palu_plain_gqa_decode(const void* q, const void* k, const void* v, const int32_t* cur_pos, void* out,
+                          int32_t out_dtype, void* workspace, size_t workspace_bytes, const palu_decode_dims* dims,
+                          float scale, palu_stream_t stream);
+
+/*
+ * Pack the reference's [rows][ld] [cos | sin] table (bf16 or fp32, pair-duplicated frequency
+ * columns: cos_j at column 2j, sin_j at 128 + 2j) into [rows][64] bf16 (cos, sin) pairs.
+ */
+int palu_pack_cs_table(const void* cs_tab, int64_t ld, int32_t in_dtype, void* cs_pairs, int32_t rows,
+                       palu_stream_t stream);
+
+/* Description of the last failure in this thread ("" if none). */
+const char* palu_last_error(void);
+
+/* Library version string. */
+const char* palu_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PALU_B200_H */

@@ -1,0 +1,62 @@
+// Small bandwidth kernels around the decode op:
+//  * palu_append_kernel: write one decode step's latents into the caches at cur_pos[b]
+//    (the reference's paged_update_cache calls, attention.py:612-625);
+//  * palu_pack_cs_kernel: turn the reference's [S, 256] [cos | sin] table (pair-duplicated,
+//    Meta-interleaved, fused.py:62-73) into the packed [S, 64] (cos, sin) bf16x2 rows the decode
+//    kernels read (half the bytes, one 4-byte load per frequency pair).
+#pragma once
+#include "palu_common.cuh"
+
+namespace palu {
+
+struct AppendParams {
+  const __nv_bfloat16* new_k;  // [B][n_groups][r_k]
+  const __nv_bfloat16* new_v;  // [B][n_groups][r_v]
+  const int32_t* cur_pos;      // [B]
+  __nv_bfloat16* k_cache;      // [B][n_groups][max_seq][r_k]
+  __nv_bfloat16* v_cache;      // [B][n_groups][max_seq][r_v]
+  int batch, n_groups, r_k, r_v, max_seq;
+};
+
+// One thread per 16-byte chunk of the step's K and V latents.
+__global__ void palu_append_kernel(const AppendParams p) {
+  const int kc = p.r_k / 8, vc = p.r_v / 8, per = kc + vc;
+  const long total = (long)p.batch * p.n_groups * per;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % per);
+    const long bg = i / per;
+    const int b = (int)(bg / p.n_groups);
+    const int pos = p.cur_pos[b];
+    if (pos < 0 || pos >= p.max_seq) continue;
+    if (c < kc) {
+      const uint4 v = reinterpret_cast<const uint4*>(p.new_k + bg * p.r_k)[c];
+      reinterpret_cast<uint4*>(p.k_cache + (bg * p.max_seq + pos) * p.r_k)[c] = v;
+    } else {
+      const uint4 v = reinterpret_cast<const uint4*>(p.new_v + bg * p.r_v)[c - kc];
+      reinterpret_cast<uint4*>(p.v_cache + (bg * p.max_seq + pos) * p.r_v)[c - kc] = v;
+    }
+  }
+}
+
+// cs_tab row s: cos at columns 2j (== 2j+1), sin at 128 + 2j. in_f32 selects an fp32 table
+// (rounded to bf16 here) instead of bf16.
+__global__ void palu_pack_cs_kernel(const void* cs_tab, long ld, int in_f32, uint32_t* out, int rows) {
+  const long total = (long)rows * 64;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long s = i >> 6;
+    const int j = (int)(i & 63);
+    float c, sn;
+    if (in_f32) {
+      const float* r = reinterpret_cast<const float*>(cs_tab) + s * ld;
+      c = r[2 * j];
+      sn = r[kHeadDim + 2 * j];
+    } else {
+      const __nv_bfloat16* r = reinterpret_cast<const __nv_bfloat16*>(cs_tab) + s * ld;
+      c = __bfloat162float(r[2 * j]);
+      sn = __bfloat162float(r[kHeadDim + 2 * j]);
+    }
+    out[i] = pack_bf16(c, sn);
+  }
+}
+
+}  // namespace palu

@@ -1,0 +1,264 @@
+// C ABI of libpalu_b200 (declared in include/palu_b200.h): envelope validation, split planning,
+// workspace layout and kernel dispatch. Everything here runs on the host; the kernels live in the
+// .cuh files next to it.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/palu_b200.h"
+#include "append.cuh"
+#include "combine.cuh"
+#include "decode_mma.cuh"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_check(const char* where) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(PALU_ERR_CUDA, "%s: %s", where, cudaGetErrorString(e));
+  return PALU_OK;
+}
+
+int device_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+int rep_of(const palu_decode_dims* d) { return d->n_q_heads / d->n_kv_heads; }
+
+// Shape envelope shared by every decode entry point. `latent` = latent caches (palu_decode_attn).
+int validate(const palu_decode_dims* d, bool latent, bool has_uv) {
+  if (!d) return fail(PALU_ERR_INVALID, "dims is NULL");
+  if (d->batch <= 0 || d->n_q_heads <= 0 || d->n_kv_heads <= 0 || d->n_groups <= 0 || d->max_seq <= 0)
+    return fail(PALU_ERR_INVALID, "batch, head counts and max_seq must be positive (got B=%d n_q=%d n_kv=%d "
+                "n_groups=%d max_seq=%d)", d->batch, d->n_q_heads, d->n_kv_heads, d->n_groups, d->max_seq);
+  if (d->head_dim != 128) return fail(PALU_ERR_INVALID, "head_dim must be 128, got %d", d->head_dim);
+  if (d->n_q_heads % d->n_kv_heads != 0)
+    return fail(PALU_ERR_INVALID, "KV head count %d must divide the %d query heads", d->n_kv_heads, d->n_q_heads);
+  if (rep_of(d) > 4)
+    return fail(PALU_ERR_INVALID, "at most 4 query heads per KV head are supported, got %d", rep_of(d));
+  if (d->n_kv_heads % d->n_groups != 0)
+    return fail(PALU_ERR_INVALID, "heads_per_group: %d latent heads do not divide %d KV heads", d->n_groups,
+                d->n_kv_heads);
+  if (d->r_v % 16 != 0 || d->r_v < 16 || d->r_v > 128)
+    return fail(PALU_ERR_INVALID, "r_v must be a multiple of 16 in [16, 128], got %d", d->r_v);
+  if (latent) {
+    if (d->r_k % 16 != 0 || d->r_k < 16 || d->r_k > 128)
+      return fail(PALU_ERR_INVALID, "r_k must be a multiple of 16 in [16, 128], got %d", d->r_k);
+    if (d->n_groups != d->n_kv_heads && !has_uv)
+      return fail(PALU_ERR_INVALID, "grouped latents (%d groups for %d KV heads) need u_v", d->n_groups,
+                  d->n_kv_heads);
+  } else {
+    if (d->n_groups != d->n_kv_heads) return fail(PALU_ERR_INVALID, "plain decode needs n_groups == n_kv_heads");
+    if (d->r_k != 128) return fail(PALU_ERR_INVALID, "plain decode needs r_k == head_dim == 128");
+  }
+  if (d->splits < 0) return fail(PALU_ERR_INVALID, "splits must be >= 0");
+  return PALU_OK;
+}
+
+int choose_splits(const palu_decode_dims* d) {
+  if (d->splits > 0) return d->splits < palu::kMaxSplits ? d->splits : palu::kMaxSplits;
+  const long items = (long)d->batch * d->n_kv_heads;
+  const int tiles = (d->max_seq + palu::kMmaTile - 1) / palu::kMmaTile;
+  const long target = 16L * device_sms();  // ~8 waves at 2 CTAs per SM
+  long s = (target + items - 1) / items;
+  const long cap = tiles / 4 > 1 ? tiles / 4 : 1;  // keep >= 4 tiles per split
+  if (s > cap) s = cap;
+  if (s < 1) s = 1;
+  if (s > palu::kMaxSplits) s = palu::kMaxSplits;
+  return (int)s;
+}
+
+size_t ws_floats_o(const palu_decode_dims* d, int splits) {
+  return (size_t)d->batch * d->n_kv_heads * splits * rep_of(d) * d->r_v;
+}
+size_t ws_floats_ml(const palu_decode_dims* d, int splits) {
+  return (size_t)d->batch * d->n_kv_heads * splits * rep_of(d) * 2;
+}
+size_t ws_bytes(const palu_decode_dims* d, int splits) {
+  const size_t o = (ws_floats_o(d, splits) * 4 + 255) / 256 * 256;
+  return o + ws_floats_ml(d, splits) * 4 + 256;
+}
+
+template <int RV16, bool RECON>
+int launch_mma(const palu::DecodeParams& p, cudaStream_t stream) {
+  constexpr int NS = 2;
+  const palu::MmaSmem<RV16, RECON> lay(p.rk);
+  const int bytes = lay.total(NS);
+  auto kern = palu::palu_decode_mma_kernel<RV16, RECON, NS>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return cuda_check("cudaFuncSetAttribute(decode)");
+  kern<<<dim3(p.splits, p.n_kv, p.batch), palu::kMmaThreads, bytes, stream>>>(p);
+  return cuda_check("decode kernel launch");
+}
+
+template <bool RECON>
+int dispatch_rv(const palu::DecodeParams& p, cudaStream_t s) {
+  switch (p.rv / 16) {
+    case 1: return launch_mma<1, RECON>(p, s);
+    case 2: return launch_mma<2, RECON>(p, s);
+    case 3: return launch_mma<3, RECON>(p, s);
+    case 4: return launch_mma<4, RECON>(p, s);
+    case 5: return launch_mma<5, RECON>(p, s);
+    case 6: return launch_mma<6, RECON>(p, s);
+    case 7: return launch_mma<7, RECON>(p, s);
+    case 8: return launch_mma<8, RECON>(p, s);
+  }
+  return fail(PALU_ERR_INVALID, "r_v %d unsupported", p.rv);
+}
+
+int run_decode(bool recon, const void* q, const void* k, const void* v, const void* u_k, int64_t u_k_ld,
+               const void* u_v, const void* cs_pairs, const int32_t* cur_pos, void* out, int32_t out_dtype,
+               void* workspace, size_t workspace_bytes, const palu_decode_dims* d, float scale,
+               cudaStream_t stream) {
+  int st = validate(d, recon, u_v != nullptr);
+  if (st) return st;
+  if (!q || !k || !v || !cur_pos || !out) return fail(PALU_ERR_INVALID, "q, caches, cur_pos and out must be set");
+  if (recon && (!u_k || !cs_pairs)) return fail(PALU_ERR_INVALID, "u_k (w_rot) and cs_tab must be set");
+  if (recon && (u_k_ld < 128 || u_k_ld % 8 != 0))
+    return fail(PALU_ERR_INVALID, "w_rot/u_k row length %lld must be >= 128 and a multiple of 8", (long long)u_k_ld);
+  if (out_dtype != PALU_BF16 && out_dtype != PALU_F32) return fail(PALU_ERR_INVALID, "out_dtype must be bf16 or f32");
+  const int splits = choose_splits(d);
+  if (!workspace || workspace_bytes < ws_bytes(d, splits))
+    return fail(PALU_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu bytes needed", workspace_bytes,
+                ws_bytes(d, splits));
+  float* ws_o = static_cast<float*>(workspace);
+  float* ws_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + (ws_floats_o(d, splits) * 4 + 255) / 256 * 256);
+
+  palu::DecodeParams p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.u_k = static_cast<const __nv_bfloat16*>(u_k);
+  p.cs = static_cast<const uint32_t*>(cs_pairs);
+  p.cur_pos = cur_pos;
+  p.ws_o = ws_o;
+  p.ws_ml = ws_ml;
+  p.batch = d->batch;
+  p.n_q = d->n_q_heads;
+  p.n_kv = d->n_kv_heads;
+  p.n_groups = d->n_groups;
+  p.rk = d->r_k;
+  p.rv = d->r_v;
+  p.max_seq = d->max_seq;
+  p.splits = splits;
+  p.ld_u = (int)u_k_ld;
+  p.rep = rep_of(d);
+  p.scale_log2 = scale * palu::kLog2e;
+  st = recon ? dispatch_rv<true>(p, stream) : dispatch_rv<false>(p, stream);
+  if (st) return st;
+
+  palu::CombineParams c;
+  c.ws_o = ws_o;
+  c.ws_ml = ws_ml;
+  c.u_v = static_cast<const __nv_bfloat16*>(u_v);
+  c.out = out;
+  c.out_f32 = out_dtype == PALU_F32;
+  c.batch = d->batch;
+  c.n_q = d->n_q_heads;
+  c.n_kv = d->n_kv_heads;
+  c.rep = p.rep;
+  c.splits = splits;
+  c.r_lat = d->r_v;
+  c.r_out = u_v ? 128 : d->r_v;
+  palu::palu_combine_kernel<<<dim3(d->n_q_heads, d->batch), palu::kCombineThreads, u_v ? d->r_v * 4 : 0, stream>>>(c);
+  return cuda_check("combine kernel launch");
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* palu_last_error(void) { return g_err.c_str(); }
+
+const char* palu_version(void) { return "palu_b200 0.1.0 (sm_100a)"; }
+
+int32_t palu_choose_splits(const palu_decode_dims* dims) {
+  if (!dims) return 0;
+  return choose_splits(dims);
+}
+
+size_t palu_workspace_bytes(const palu_decode_dims* dims) {
+  if (!dims || dims->n_kv_heads <= 0 || dims->n_q_heads <= 0) return 0;
+  return ws_bytes(dims, choose_splits(dims));
+}
+
+int palu_decode_attn(const void* q, const void* k_lat, const void* v_lat, const void* u_k, int64_t u_k_ld,
+                     const void* u_v, const void* cs_pairs, const int32_t* cur_pos, void* out, int32_t out_dtype,
+                     void* workspace, size_t workspace_bytes, const palu_decode_dims* dims, float scale,
+                     palu_stream_t stream) {
+  g_err.clear();
+  return run_decode(true, q, k_lat, v_lat, u_k, u_k_ld, u_v, cs_pairs, cur_pos, out, out_dtype, workspace,
+                    workspace_bytes, dims, scale, stream);
+}
+
+int palu_plain_gqa_decode(const void* q, const void* k, const void* v, const int32_t* cur_pos, void* out,
+                          int32_t out_dtype, void* workspace, size_t workspace_bytes, const palu_decode_dims* dims,
+                          float scale, palu_stream_t stream) {
+  g_err.clear();
+  return run_decode(false, q, k, v, nullptr, 128, nullptr, nullptr, cur_pos, out, out_dtype, workspace,
+                    workspace_bytes, dims, scale, stream);
+}
+
+int palu_append_latents(const void* new_k, const void* new_v, const int32_t* cur_pos, void* k_cache, void* v_cache,
+                        const palu_decode_dims* d, palu_stream_t stream) {
+  g_err.clear();
+  if (!d) return fail(PALU_ERR_INVALID, "dims is NULL");
+  if (!new_k || !new_v || !cur_pos || !k_cache || !v_cache)
+    return fail(PALU_ERR_INVALID, "append: every pointer must be set");
+  if (d->batch <= 0 || d->n_groups <= 0 || d->max_seq <= 0)
+    return fail(PALU_ERR_INVALID, "append: batch, n_groups and max_seq must be positive");
+  if (d->r_k % 8 != 0 || d->r_v % 8 != 0 || d->r_k <= 0 || d->r_v <= 0)
+    return fail(PALU_ERR_INVALID, "append: r_k and r_v must be positive multiples of 8 (got %d, %d)", d->r_k, d->r_v);
+  palu::AppendParams p;
+  p.new_k = static_cast<const __nv_bfloat16*>(new_k);
+  p.new_v = static_cast<const __nv_bfloat16*>(new_v);
+  p.cur_pos = cur_pos;
+  p.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  p.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  p.batch = d->batch;
+  p.n_groups = d->n_groups;
+  p.r_k = d->r_k;
+  p.r_v = d->r_v;
+  p.max_seq = d->max_seq;
+  const long total = (long)d->batch * d->n_groups * (d->r_k / 8 + d->r_v / 8);
+  const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  palu::palu_append_kernel<<<blocks, 256, 0, stream>>>(p);
+  return cuda_check("append kernel launch");
+}
+
+int palu_pack_cs_table(const void* cs_tab, int64_t ld, int32_t in_dtype, void* cs_pairs, int32_t rows,
+                       palu_stream_t stream) {
+  g_err.clear();
+  if (!cs_tab || !cs_pairs || rows <= 0) return fail(PALU_ERR_INVALID, "cs_tab: table, output and rows must be set");
+  if (ld < 256) return fail(PALU_ERR_INVALID, "cs_tab rows must hold [cos | sin] (>= 256 columns), got %lld",
+                            (long long)ld);
+  if (in_dtype != PALU_BF16 && in_dtype != PALU_F32) return fail(PALU_ERR_INVALID, "cs_tab dtype must be bf16 or f32");
+  const long total = (long)rows * 64;
+  const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  palu::palu_pack_cs_kernel<<<blocks, 256, 0, stream>>>(cs_tab, ld, in_dtype == PALU_F32,
+                                                         static_cast<uint32_t*>(cs_pairs), rows);
+  return cuda_check("cs_tab pack kernel launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,102 @@
+"""ctypes binding of libpalu_b200.so (the C ABI in include/palu_b200.h).
+
+The shared library is built in-tree (``palu_b200.build.build()``) and loaded from this package's
+directory. There is no fallback: if the library or a CUDA device is missing, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import torch
+
+LIB_NAME = "libpalu_b200.so"
+LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
+
+PALU_OK, PALU_ERR_INVALID, PALU_ERR_WORKSPACE, PALU_ERR_CUDA = 0, 1, 2, 3
+PALU_BF16, PALU_F32 = 0, 1
+
+# Every symbol include/palu_b200.h declares (checked by the CPU test suite).
+EXPORTED = ("palu_decode_attn", "palu_workspace_bytes", "palu_choose_splits", "palu_append_latents",
+            "palu_plain_gqa_decode", "palu_pack_cs_table", "palu_last_error", "palu_version")
+
+
+class DecodeDims(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int32), ("n_q_heads", ctypes.c_int32), ("n_kv_heads", ctypes.c_int32),
+                ("n_groups", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("r_k", ctypes.c_int32),
+                ("r_v", ctypes.c_int32), ("max_seq", ctypes.c_int32), ("splits", ctypes.c_int32)]
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the library (once). Raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(f"{LIB_NAME} is not built: run palu_b200.build.build() (looked in {LIB_PATH.parent})")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    vp, i32, i64, sz, f32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t, ctypes.c_float
+    dims_p = ctypes.POINTER(DecodeDims)
+    lib.palu_decode_attn.argtypes = [vp, vp, vp, vp, i64, vp, vp, vp, vp, i32, vp, sz, dims_p, f32, vp]
+    lib.palu_decode_attn.restype = ctypes.c_int
+    lib.palu_plain_gqa_decode.argtypes = [vp, vp, vp, vp, vp, i32, vp, sz, dims_p, f32, vp]
+    lib.palu_plain_gqa_decode.restype = ctypes.c_int
+    lib.palu_workspace_bytes.argtypes = [dims_p]
+    lib.palu_workspace_bytes.restype = sz
+    lib.palu_choose_splits.argtypes = [dims_p]
+    lib.palu_choose_splits.restype = i32
+    lib.palu_append_latents.argtypes = [vp, vp, vp, vp, vp, dims_p, vp]
+    lib.palu_append_latents.restype = ctypes.c_int
+    lib.palu_pack_cs_table.argtypes = [vp, i64, i32, vp, i32, vp]
+    lib.palu_pack_cs_table.restype = ctypes.c_int
+    lib.palu_last_error.argtypes = []
+    lib.palu_last_error.restype = ctypes.c_char_p
+    lib.palu_version.argtypes = []
+    lib.palu_version.restype = ctypes.c_char_p
+    _lib = lib
+    return lib
+
+
+def check(status: int) -> None:
+    """Map a nonzero status to RuntimeError carrying palu_last_error()."""
+    if status != PALU_OK:
+        msg = load().palu_last_error().decode(errors="replace")
+        raise RuntimeError(f"palu_b200 error {status}: {msg}")
+
+
+def require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("palu_b200 runs on CUDA tensors only (no CPU path); got a tensor on "
+                               f"{t.device}")
+
+
+def ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def dims(batch, n_q, n_kv, n_groups, r_k, r_v, max_seq, splits=0) -> DecodeDims:
+    return DecodeDims(int(batch), int(n_q), int(n_kv), int(n_groups), 128, int(r_k), int(r_v), int(max_seq),
+                      int(splits))
+
+
+def workspace_bytes(d: DecodeDims) -> int:
+    return int(load().palu_workspace_bytes(ctypes.byref(d)))
+
+
+def choose_splits(d: DecodeDims) -> int:
+    return int(load().palu_choose_splits(ctypes.byref(d)))
+
+
+def env_splits() -> int:
+    """Split override for experiments (PALU_SPLITS); 0 = the library's choice."""
+    v = os.environ.get("PALU_SPLITS", "").strip()
+    return int(v) if v.isdigit() else 0

@@ -1,0 +1,295 @@
+"""Host side of the fused decode op: the RoPE table builders and the ``palu_sdpa_decode`` wrapper.
+
+Mirrors the reference's ``palu_tt/fused.py`` surface (table builders fused.py:36-79) and the
+``ttnn.transformer.palu_sdpa_decode`` keyword surface (called at palu_tt/attention.py:633-639 and
+tests/test_palu_sdpa_device.py:84-88, 255-258). The op itself runs in libpalu_b200 (CUDA, sm_100a):
+
+* K is rebuilt on the tensor cores from the latent (``w_rot``'s first 128 columns are ``u_k``; the
+  ``u_k T`` half is not read because the pair swap is free in registers), rotated in registers from the
+  packed [cos | sin] table, and scored against the rotated query;
+* V is either the latent itself (absorbed into ``wo``, M-LRD) or rebuilt per head through ``u_v``
+  (G-LRD), and the split-K partials are merged by a second kernel.
+
+Tensix-only knobs (``rot_step``/``trans_mat`` Phase 2 tables, ``rot_mode``, ``table_mcast``,
+``heads_per_core``, ``program_config``, ``compute_kernel_config``, ``memory_config``) are accepted and
+validated the way the reference validates them, and do not change the B200 computation: the B200
+kernels always read the table by absolute position and always share a group latent across the group.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Optional
+
+import torch
+
+from palu_b200 import _lib
+
+MAX_CHUNK = 512
+HEAD_DIM = 128
+ROT_MODES = ("legacy", "pack", "dst")
+
+
+# ----------------------------------------------------------------------------------------------
+# Table builders (host, once per model) -- fused.py:36-79
+# ----------------------------------------------------------------------------------------------
+
+def rope_transformation_matrix(head_dim: int) -> torch.Tensor:
+    """[hd, hd] T such that x @ T maps each adjacent pair (x0, x1) to (-x1, x0) (fused.py:36-41)."""
+    idx = torch.arange(0, head_dim, 2)
+    T = torch.zeros(head_dim, head_dim)
+    T[idx, idx + 1] = 1.0
+    T[idx + 1, idx] = -1.0
+    return T
+
+
+def trans_mat_tile() -> torch.Tensor:
+    """The [1, 1, 32, 32] pair-rotation tile (fused.py:44-46)."""
+    return rope_transformation_matrix(32).reshape(1, 1, 32, 32)
+
+
+def w_rot_from_u_k(u_k: torch.Tensor) -> torch.Tensor:
+    """u_k [n_kv, r_k, hd] -> w_rot [n_kv, r_k, 2 hd] = [u_k | u_k @ T] (fused.py:49-51)."""
+    return torch.cat([u_k, u_k @ rope_transformation_matrix(u_k.shape[-1]).to(u_k.dtype)], dim=-1)
+
+
+def chunk_size(seq_len: int) -> int:
+    """Largest power of two dividing seq_len, at most 512 (fused.py:54-59)."""
+    assert seq_len > 0, f"chunk_size requires seq_len > 0, got {seq_len}"
+    return min(MAX_CHUNK, seq_len & -seq_len)
+
+
+def _llama3_freqs(f: torch.Tensor, rs: dict) -> torch.Tensor:
+    factor, lo, hi = float(rs["factor"]), float(rs["low_freq_factor"]), float(rs["high_freq_factor"])
+    orig = float(rs["original_max_position_embeddings"])
+    wl = 2.0 * math.pi / f
+    t = (orig / wl - lo) / (hi - lo)
+    mid = (1.0 - t) * (f / factor) + t * f
+    return torch.where(wl < orig / hi, f, torch.where(wl > orig / lo, f / factor, mid)).float()
+
+
+def _scaling_dict(rope_scaling):
+    if rope_scaling is None or isinstance(rope_scaling, dict):
+        return rope_scaling
+    keys = ("rope_type", "factor", "low_freq_factor", "high_freq_factor", "original_max_position_embeddings")
+    return {k: getattr(rope_scaling, k) for k in keys if hasattr(rope_scaling, k)}
+
+
+def rope_frequencies(head_dim: int, theta: float, rope_scaling=None) -> torch.Tensor:
+    """fp32 inverse frequencies theta ** (-2i/d), with Llama-3.1 scaling when rope_scaling asks for it."""
+    f = 1.0 / (theta ** (torch.arange(0, head_dim, 2)[: head_dim // 2].float() / head_dim))
+    rs = _scaling_dict(rope_scaling)
+    if rs:
+        kind = rs.get("rope_type", rs.get("type", "llama3"))
+        if kind != "llama3":
+            raise ValueError(f"rope_scaling type {kind!r} is not supported (llama3 only)")
+        f = _llama3_freqs(f, rs)
+    return f
+
+
+def cos_sin_tables(head_dim: int, seq_len: int, theta: float, rope_scaling=None):
+    """Meta-interleaved cos / sin, fp32, each [seq_len + 513, head_dim] (fused.py:62-68)."""
+    n = seq_len + MAX_CHUNK + 1
+    ang = torch.outer(torch.arange(n).float(), rope_frequencies(head_dim, theta, rope_scaling)).float()
+    return torch.cos(ang).repeat_interleave(2, -1).contiguous(), torch.sin(ang).repeat_interleave(2, -1).contiguous()
+
+
+def cs_table(cos: torch.Tensor, sin: torch.Tensor, seq_len: int) -> torch.Tensor:
+    """[seq_len, 2 hd] = [cos | sin] for positions 0..seq_len-1 (fused.py:71-73)."""
+    return torch.cat([cos[:seq_len], sin[:seq_len]], dim=-1)
+
+
+def rot_step_table(cos: torch.Tensor, sin: torch.Tensor, chunk: int) -> torch.Tensor:
+    """[32, 2 hd] fp32 [cos(c f) | sin(c f)] rows (fused.py:76-79). Accepted by the op for surface
+    compatibility; the B200 kernels read absolute positions and do not need it."""
+    return torch.cat([cos[chunk], sin[chunk]]).expand(32, -1).contiguous().float()
+
+
+# ----------------------------------------------------------------------------------------------
+# Device-side table packing (cached per cs_tab tensor)
+# ----------------------------------------------------------------------------------------------
+
+_PACK_CACHE: dict = {}
+
+
+def pack_cs_table(cs_tab: torch.Tensor) -> torch.Tensor:
+    """[.., S, 256] [cos | sin] (bf16 or fp32, CUDA) -> [S, 64] int32 rows of bf16 (cos, sin) pairs,
+    computed by the library's pack kernel and cached while the table tensor is unchanged."""
+    _lib.require_cuda(cs_tab)
+    t = cs_tab.reshape(-1, cs_tab.shape[-1])
+    if t.stride(-1) != 1:
+        t = t.contiguous()
+    key = (t.data_ptr(), tuple(t.shape), t.dtype, cs_tab._version, t.device.index)
+    hit = _PACK_CACHE.get(key)
+    if hit is not None:
+        return hit
+    if t.dtype not in (torch.bfloat16, torch.float32):
+        t = t.float()
+    out = torch.empty(t.shape[0], 64, dtype=torch.int32, device=t.device)
+    dt = _lib.PALU_F32 if t.dtype == torch.float32 else _lib.PALU_BF16
+    _lib.check(_lib.load().palu_pack_cs_table(t.data_ptr(), t.stride(0), dt, out.data_ptr(), t.shape[0],
+                                              _lib.stream_handle(t.device)))
+    if len(_PACK_CACHE) > 16:
+        _PACK_CACHE.clear()
+    _PACK_CACHE[key] = out
+    return out
+
+
+# ----------------------------------------------------------------------------------------------
+# The op
+# ----------------------------------------------------------------------------------------------
+
+def _bf16(t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+    if t is None:
+        return None
+    t = t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16)
+    return t.contiguous()
+
+
+def _grid_cores(program_config) -> Optional[int]:
+    grid = getattr(program_config, "compute_with_storage_grid_size", None)
+    if grid is None:
+        return None
+    try:
+        gx, gy = (grid.x, grid.y) if hasattr(grid, "x") else tuple(grid)
+    except TypeError:
+        return None
+    return int(gx) * int(gy)
+
+
+def decode(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, *, u_k_ld=HEAD_DIM, u_v=None, scale=None,
+           out=None, out_dtype=torch.bfloat16, splits=0, workspace=None) -> torch.Tensor:
+    """Low-level entry (no reference-surface validation): the arrays are already in the library's layout.
+
+    q [B, nh, 128] bf16; k_latent [B, n_groups, S, r_k]; v_latent [B, n_groups, S, r_v]; u_k rows of
+    ``u_k_ld`` elements ([n_kv, r_k, u_k_ld]); cs_pairs [>= S, 64] int32 from ``pack_cs_table``;
+    cur_pos [B] int32; u_v [n_kv, r_v, 128] or None. Returns [B, nh, r_v or 128]."""
+    _lib.require_cuda(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, u_v)
+    B, nh = q.shape[0], q.shape[1]
+    n_groups, S, r_k = k_latent.shape[1], k_latent.shape[2], k_latent.shape[3]
+    r_v = v_latent.shape[3]
+    n_kv = u_k.shape[0]
+    d = _lib.dims(B, nh, n_kv, n_groups, r_k, r_v, S, splits or _lib.env_splits())
+    width = HEAD_DIM if u_v is not None else r_v
+    if out is None:
+        out = torch.empty(B, nh, width, dtype=out_dtype, device=q.device)
+    need = _lib.workspace_bytes(d)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    odt = _lib.PALU_F32 if out.dtype == torch.float32 else _lib.PALU_BF16
+    sc = HEAD_DIM ** -0.5 if scale is None else float(scale)
+    _lib.check(_lib.load().palu_decode_attn(
+        q.data_ptr(), k_latent.data_ptr(), v_latent.data_ptr(), u_k.data_ptr(), int(u_k_ld), _lib.ptr(u_v),
+        cs_pairs.data_ptr(), cur_pos.data_ptr(), out.data_ptr(), odt, workspace.data_ptr(), workspace.numel(),
+        ctypes.byref(d), sc, _lib.stream_handle(q.device)))
+    return out
+
+
+def palu_sdpa_decode(q, k_latent, w_rot, cs_tab, v_latent, head_dim_v, cur_pos_tensor, *, rot_step=None,
+                     trans_mat=None, u_v=None, scale=None, heads_per_core=None, rot_mode="dst", table_mcast=True,
+                     program_config=None, compute_kernel_config=None, memory_config=None,
+                     out_dtype=torch.bfloat16, splits=0) -> torch.Tensor:
+    """B200 implementation of ``ttnn.transformer.palu_sdpa_decode`` (same positional / keyword surface).
+
+    q [1, B, nh, 128] (rotated), k_latent [B, n_groups, S, r_k], w_rot [1, n_kv, r_k, 256],
+    cs_tab [1, 1, >= S, 256], v_latent [B, n_groups, S, r_v], cur_pos_tensor [B] ints,
+    u_v [1, n_kv, r_v, 128] (in-kernel V). Returns [1, B, nh, head_dim_v]. Raises RuntimeError with
+    the reference's message substrings on envelope violations."""
+    if rot_mode not in ROT_MODES:
+        raise RuntimeError(f"rot_mode must be one of {ROT_MODES}, got {rot_mode!r}")
+    if (rot_step is None) != (trans_mat is None):
+        raise RuntimeError("rot_step and trans_mat are optional together: pass both (Phase 2) or neither (Phase 1)")
+    chunk = getattr(program_config, "k_chunk_size", 0) or 0
+    if rot_step is None and chunk > 128:
+        raise RuntimeError(f"Phase 1 (no rot_step) needs k_chunk_size <= 128, got {chunk}")
+    if q.dim() != 4 or q.shape[0] != 1 or q.shape[-1] != HEAD_DIM:
+        raise RuntimeError(f"q must be [1, B, nh, 128], got {tuple(q.shape)}")
+    B, nh = q.shape[1], q.shape[2]
+    if k_latent.dim() != 4 or v_latent.dim() != 4:
+        raise RuntimeError("k_latent and v_latent must be [B, n_groups, S, r]")
+    n_groups, S, r_k = k_latent.shape[1], k_latent.shape[2], k_latent.shape[3]
+    r_v = v_latent.shape[3]
+    if k_latent.shape[0] != B or v_latent.shape[:3] != k_latent.shape[:3]:
+        raise RuntimeError("k_latent / v_latent batch, group or sequence dims do not match q")
+    w = w_rot.reshape(-1, *w_rot.shape[-2:]) if w_rot.dim() >= 3 else w_rot
+    if w.dim() != 3 or w.shape[-1] != 2 * HEAD_DIM:
+        raise RuntimeError(f"w_rot must be [1, n_kv, r_k, 256] = [u_k | u_k T], got {tuple(w_rot.shape)}")
+    n_kv = w.shape[0]
+    if r_k % 16 or not 16 <= r_k <= 512 or w.shape[1] != r_k:
+        raise RuntimeError(f"r_k: latent width {r_k} must be a multiple of 16 in [16, 512] and match w_rot's "
+                           f"{w.shape[1]} rows")
+    if cs_tab.shape[-1] != 2 * HEAD_DIM or cs_tab.shape[-2] < S:
+        raise RuntimeError(f"cs_tab must be [1, 1, >= {S}, 256] ([cos | sin] per position), got {tuple(cs_tab.shape)}")
+    if n_kv % n_groups:
+        raise RuntimeError(f"heads_per_group: {n_groups} latent heads do not divide {n_kv} KV heads (w_rot)")
+    if nh % n_kv:
+        raise RuntimeError(f"KV head count {n_kv} must divide the {nh} query heads")
+    hpg = n_kv // n_groups
+    if hpg > 1 and u_v is None:
+        raise RuntimeError(f"grouped latents ({hpg} KV heads per latent) need u_v (in-kernel V)")
+    if u_v is not None:
+        if head_dim_v != HEAD_DIM:
+            raise RuntimeError(f"head_dim_v must be {HEAD_DIM} when u_v is given, got {head_dim_v}")
+        uv = u_v.reshape(-1, *u_v.shape[-2:])
+        if tuple(uv.shape) != (n_kv, r_v, HEAD_DIM):
+            raise RuntimeError(f"u_v must be [1, {n_kv}, {r_v}, 128], got {tuple(u_v.shape)}")
+    elif head_dim_v != r_v:
+        raise RuntimeError(f"head_dim_v {head_dim_v} must equal the V latent width {r_v} (absorbed V)")
+    if heads_per_core is not None:
+        h = int(heads_per_core)
+        if h > n_kv:
+            raise RuntimeError(f"heads_per_core {h} exceeds the KV head count {n_kv}")
+        if h > 1 and hpg == 1:
+            raise RuntimeError("heads_per_core > 1 shares a latent read and needs grouped latents")
+        if h < 1 or hpg % h:
+            raise RuntimeError(f"heads_per_core {h} must divide heads_per_group {hpg}")
+        cores = _grid_cores(program_config)
+        if h > 1 and cores is not None and B * (n_kv // h) > cores:
+            raise RuntimeError(f"heads_per_core {h} needs {B * (n_kv // h)} cores, only {cores} available")
+    if k_latent.dtype != torch.bfloat16 or v_latent.dtype != torch.bfloat16:
+        raise RuntimeError("latent caches must be bf16 (block-float latent formats are not supported)")
+    _lib.require_cuda(q, k_latent, w_rot, cs_tab, v_latent, cur_pos_tensor, u_v)
+    pos = cur_pos_tensor.reshape(-1)
+    if pos.numel() != B:
+        raise RuntimeError(f"cur_pos_tensor must hold {B} positions, got {pos.numel()}")
+    pos = pos.to(torch.int32).contiguous()
+    wb = _bf16(w)
+    out = decode(_bf16(q[0]), k_latent.contiguous(), v_latent.contiguous(), wb, pack_cs_table(cs_tab), pos,
+                 u_k_ld=wb.shape[-1], u_v=_bf16(u_v.reshape(n_kv, r_v, HEAD_DIM)) if u_v is not None else None,
+                 scale=scale, out_dtype=out_dtype, splits=splits)
+    return out.unsqueeze(0)
+
+
+def plain_gqa_decode(q, k, v, cur_pos, *, scale=None, out_dtype=torch.bfloat16, splits=0) -> torch.Tensor:
+    """Plain GQA flash-decode over already-rotated full K (the stock decode op the identity
+    factorisation must match, tests/test_palu_sdpa_device.py:58-65). q [1, B, nh, 128],
+    k [B, n_kv, S, 128], v [B, n_kv, S, d_v] -> [1, B, nh, d_v]."""
+    _lib.require_cuda(q, k, v, cur_pos)
+    B, nh = q.shape[1], q.shape[2]
+    n_kv, S, d_v = k.shape[1], k.shape[2], v.shape[3]
+    d = _lib.dims(B, nh, n_kv, n_kv, HEAD_DIM, d_v, S, splits or _lib.env_splits())
+    out = torch.empty(B, nh, d_v, dtype=out_dtype, device=q.device)
+    ws = torch.empty(_lib.workspace_bytes(d), dtype=torch.uint8, device=q.device)
+    odt = _lib.PALU_F32 if out_dtype == torch.float32 else _lib.PALU_BF16
+    sc = HEAD_DIM ** -0.5 if scale is None else float(scale)
+    qb, kb, vb = _bf16(q[0]), _bf16(k), _bf16(v)
+    _lib.check(_lib.load().palu_plain_gqa_decode(
+        qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), cur_pos.to(torch.int32).contiguous().data_ptr(),
+        out.data_ptr(), odt, ws.data_ptr(), ws.numel(), ctypes.byref(d), sc, _lib.stream_handle(q.device)))
+    return out.unsqueeze(0)
+
+
+def append_latents(new_k, new_v, cur_pos, k_cache, v_cache) -> None:
+    """Write one step's latents [B, n_groups, r] into the caches [B, n_groups, S, r] at cur_pos[b]
+    (the reference's paged_update_cache pair, attention.py:622-623)."""
+    _lib.require_cuda(new_k, new_v, cur_pos, k_cache, v_cache)
+    B, G, S, r_k = k_cache.shape
+    r_v = v_cache.shape[-1]
+    if tuple(new_k.shape[-3:]) != (B, G, r_k) or tuple(new_v.shape[-3:]) != (B, G, r_v):
+        raise RuntimeError(f"new latents must be [B, n_groups, r]: got {tuple(new_k.shape)}, {tuple(new_v.shape)}")
+    d = _lib.dims(B, G, G, G, r_k, r_v, S)
+    nk, nv = _bf16(new_k), _bf16(new_v)
+    _lib.check(_lib.load().palu_append_latents(nk.data_ptr(), nv.data_ptr(),
+                                               cur_pos.to(torch.int32).contiguous().data_ptr(),
+                                               k_cache.data_ptr(), v_cache.data_ptr(), ctypes.byref(d),
+                                               _lib.stream_handle(k_cache.device)))
