@@ -202,9 +202,10 @@ def run_reference(args, ws, rank):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(ws):
-    return {"workload": "mlrd_r64_b32_s8192", "model": "Llama-3.1-8B attention layer (M-LRD, absorbed V)",
-            "global_batch": B_PER_GPU * ws, "seq_len": S, "rank_k": R, "rank_v": R, "n_q_heads": N_Q,
+def workload_config(ws, batch=B_PER_GPU):
+    name = "mlrd_r64_b32_s8192" if batch == B_PER_GPU else f"mlrd_r64_b{batch}_s8192"
+    return {"workload": name, "model": "Llama-3.1-8B attention layer (M-LRD, absorbed V)",
+            "global_batch": batch * ws, "seq_len": S, "rank_k": R, "rank_v": R, "n_q_heads": N_Q,
             "n_kv_heads": N_KV, "kv_heads_per_gpu": N_KV // ws, "parallelism": f"kv-head shard x{ws}",
             "l2": "no flush: each step reads 537 MB of latents (> 126 MB L2)"}
 
@@ -216,12 +217,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--clock-soak", type=float, default=2.0, help="seconds of untimed steps sampled for clocks")
+    ap.add_argument("--batch", type=int, default=B_PER_GPU, help="batch rows per GPU (profiling cases)")
+    ap.add_argument("--kernel", default="auto", choices=["auto", "tc", "mma"],
+                    help="decode kernel family: tcgen05 (tc), legacy mma.sync (mma) or the library's choice")
     args = ap.parse_args()
     ws, rank, local = dist_env()
     if args.impl == "reference":
         return run_reference(args, ws, rank)
 
     from palu_b200 import _lib, fused
+    _lib.set_kernel({"auto": _lib.PALU_KERNEL_AUTO, "tc": _lib.PALU_KERNEL_TC, "mma": _lib.PALU_KERNEL_MMA}[args.kernel])
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     if ws > 1:
@@ -230,13 +236,13 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     if N_KV % ws:
         raise SystemExit(f"{N_KV} KV heads do not shard over {ws} GPUs")
-    B = B_PER_GPU * ws
+    B = args.batch * ws
     n_kv = N_KV // ws
     n_q = N_Q // ws
     L = make_layer(dev, B, n_q, n_kv, seed=1234 + rank)
     out = torch.empty(B, n_q, R, dtype=torch.bfloat16, device=dev)
     d = _lib.dims(B, n_q, n_kv, n_kv, R, R, S)
-    ws_buf = torch.empty(_lib.workspace_bytes(d), dtype=torch.uint8, device=dev)
+    ws_buf = _lib.new_workspace(d, dev)
 
     def step():
         fused.decode(L["q"], L["k"], L["v"], L["u"], L["cs"], L["pos"], out=out, workspace=ws_buf)
@@ -255,6 +261,14 @@ def main():
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
     barrier()
     with ClockSampler(local) as clk:
+        # The timed region can be a few ms, shorter than nvidia-smi's 200 ms sampling period, so the
+        # sampler also covers a soak of the same step (same load, untimed) right before it.
+        soak_end = time.perf_counter() + args.clock_soak
+        while time.perf_counter() < soak_end:
+            for _ in range(50):
+                step()
+            torch.cuda.synchronize()
+        barrier()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record(stream)
@@ -315,6 +329,8 @@ def main():
     achieved = alg_bytes / (per_launch_ms * 1e-3) / 1e9
     peak, peak_kind = peaks()
     tr = traffic_record()
+    kernel_name = ("palu_decode_tc_kernel" if _lib.kernel_for(d) == _lib.PALU_KERNEL_TC
+                   else "palu_decode_mma_kernel")
 
     if rank == 0:
         cpu = None
@@ -325,14 +341,14 @@ def main():
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, on device)",
-            "config": workload_config(ws),
+            "config": workload_config(ws, args.batch),
             "us_per_layer": ms * 1e3, "latent_GBps": achieved,
             "e2e": {"value": B / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": (tr or {}).get("bytes_per_launch"),
-                         "kernel": "palu_decode_mma_kernel + palu_combine_kernel (one op)",
+                         "kernel": kernel_name + " + palu_combine_kernel (one decode op)",
                          "algorithmic_bytes": alg_bytes},
             "cpu_baseline": cpu,
             "gpu_launches": 2 * args.steps,

@@ -43,6 +43,10 @@ enum palu_status {
 
 enum palu_dtype { PALU_BF16 = 0, PALU_F32 = 1 };
 
+/* Decode kernel families: the tcgen05/TMEM/TMA kernel (the product path, used wherever its envelope
+ * covers the shapes) and the warp-level mma.sync kernel (the legacy tensor-core baseline). */
+enum palu_kernel { PALU_KERNEL_AUTO = 0, PALU_KERNEL_MMA = 1, PALU_KERNEL_TC = 2 };
+
 /* Shapes of one decode-attention call (the local shard on this GPU). */
 typedef struct palu_decode_dims {
   int32_t batch;      /* B */
@@ -70,7 +74,9 @@ typedef struct palu_decode_dims {
  *            position s as a bf16 pair (cos in the low half)
  *   cur_pos  [B] int32: last visible position of each row (inclusive); < 0 skips the row (zeros out)
  *   out      [B][n_q_heads][r_v or 128], out_dtype PALU_BF16 or PALU_F32
- *   workspace / workspace_bytes: >= palu_workspace_bytes(dims) bytes of device memory
+ *   workspace / workspace_bytes: >= palu_workspace_bytes(dims) bytes of device memory; its first 4
+ *            bytes are a status word that must be zero when the workspace is first used (zero the
+ *            buffer once after allocating it); see palu_read_status
  *   scale    softmax scale (the reference passes head_dim ** -0.5)
  * Query head h attends KV head h / (n_q_heads / n_kv_heads), which reads latent head
  * kv / (n_kv_heads / n_groups). Positions above cur_pos[b] are masked; cur_pos[b] >= max_seq is
@@ -110,6 +116,23 @@ int palu_plain_gqa_decode(const void* q, const void* k, const void* v, const int
  */
 int palu_pack_cs_table(const void* cs_tab, int64_t ld, int32_t in_dtype, void* cs_pairs, int32_t rows,
                        palu_stream_t stream);
+
+/*
+ * Select the decode kernel family for subsequent calls in this process (PALU_KERNEL_AUTO by default:
+ * the tcgen05 kernel where its envelope covers the shapes, else the mma.sync kernel). No reference
+ * counterpart (the Tensix op has one program); used to benchmark the legacy path against the product.
+ */
+int palu_set_kernel(int32_t which);
+
+/* The kernel family a palu_decode_attn call with these dims would run (PALU_KERNEL_MMA or _TC). */
+int32_t palu_kernel_for(const palu_decode_dims* dims);
+
+/*
+ * Read (and clear) the status word a decode call left in `workspace`: 0 = ok, 1 = a bounded device
+ * wait expired (the call's output is then invalid). Synchronises `stream`. No reference counterpart:
+ * the Tensix op has no bounded waits (its known hangs were capped by the host, README.md:301-329).
+ */
+int palu_read_status(void* workspace, int32_t* status, palu_stream_t stream);
 
 /* Description of the last failure in this thread ("" if none). */
 const char* palu_last_error(void);

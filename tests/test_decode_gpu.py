@@ -1,10 +1,15 @@
 """Parity of the CUDA decode path (through the C ABI via palu_b200.fused) with the oracle.
 
-Bar (written here, per the north star): on the bf16 output, max-abs relative error <= 2e-2 and
-mean-abs relative error <= 1e-3, globally and per (batch row, query head) row. The bf16 output is
-compared with the oracle's fp32 output rounded to bf16 (the dtype the op returns): rounding the fp32
-oracle to bf16 alone costs ~1.4e-3 mean-abs relative error, so no bf16-output kernel can meet 1e-3
-against the unrounded value. The fp32-output mode is compared with the unrounded oracle directly.
+Bar (written here, per the north star): max-abs relative error <= 2e-2 and mean-abs relative error
+<= 1e-3.
+
+* bf16 output (what the op returns): compared globally with the oracle's fp32 output rounded to bf16.
+  Rounding the fp32 oracle to bf16 alone costs ~1.4e-3 mean-abs relative error, so no bf16-output kernel
+  can meet 1e-3 against the unrounded value.
+* fp32 output mode: compared with the unrounded oracle, globally AND per (batch row, query head) row, so
+  that long-context rows (output std ~0.02) are not hidden behind short ones. The per-row bar is not
+  applied to the bf16 output: when both sides are rounded to bf16, a sub-ulp difference becomes a
+  whole-ulp flip (2^-8 relative), which on a 16-element row moves the row mean by ~1e-3 by itself.
 """
 import pytest
 import torch
@@ -24,11 +29,21 @@ def _bf(t):
     return t.to(torch.bfloat16).float()
 
 
-def assert_close(out, ref, what=""):
+@pytest.fixture(params=["tc", "mma"])
+def kernel(request, cuda):
+    """Run a test once through the tcgen05 kernel and once through the legacy mma.sync kernel."""
+    from palu_b200 import _lib
+    _lib.set_kernel(_lib.PALU_KERNEL_TC if request.param == "tc" else _lib.PALU_KERNEL_MMA)
+    yield request.param
+    _lib.set_kernel(_lib.PALU_KERNEL_AUTO)
+
+
+def assert_close(out, ref, what="", per_row=True):
     mx, mn = rel_errors(out, ref)
-    rmx, rmn = rowwise_rel_errors(out, ref)
     assert mx <= MAX_REL and mn <= MEAN_REL, f"{what}: global max {mx:.3e} mean {mn:.3e}"
-    assert rmx <= MAX_REL and rmn <= MEAN_REL, f"{what}: worst row max {rmx:.3e} mean {rmn:.3e}"
+    if per_row:
+        rmx, rmn = rowwise_rel_errors(out, ref)
+        assert rmx <= MAX_REL and rmn <= MEAN_REL, f"{what}: worst row max {rmx:.3e} mean {rmn:.3e}"
 
 
 def _run_fused(dev, q, k_lat, u_k, v_lat, pos, cos, sin, scale, u_v=None, out_dtype=torch.bfloat16, splits=0):
@@ -43,6 +58,7 @@ def _run_fused(dev, q, k_lat, u_k, v_lat, pos, cos, sin, scale, u_v=None, out_dt
         u_v=None if u_v is None else u_v[None].to(dev, torch.bfloat16), scale=scale, out_dtype=out_dtype,
         splits=splits)
     torch.cuda.synchronize()
+    assert fused.workspace_status() == 0, "a bounded device wait expired"
     return out.float().cpu()
 
 
@@ -68,7 +84,7 @@ GOLDEN_CASES = ["decode_mlrd_r64", "decode_mlrd_rk32_rv128", "decode_identity_r1
 
 @pytest.mark.parametrize("name", GOLDEN_CASES)
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32], ids=["bf16", "f32"])
-def test_golden_fixtures(cuda, name, out_dtype):
+def test_golden_fixtures(cuda, kernel, name, out_dtype):
     """The reference's own reference_decode outputs (tests/golden/make_golden.py)."""
     d = load_golden(name)
     gs = int(d["group_size"])
@@ -80,22 +96,22 @@ def test_golden_fixtures(cuda, name, out_dtype):
     if out_dtype == torch.bfloat16:
         ref = _bf(ref)
     assert out.shape == ref.shape
-    assert_close(out, ref, name)
+    assert_close(out, ref, name, per_row=out_dtype == torch.float32)
 
 
 @pytest.mark.parametrize("r_k,r_v", [(16, 16), (32, 128), (64, 64), (96, 64), (128, 128), (48, 80)])
 @pytest.mark.parametrize("B,S", [(1, 1000), (5, 333), (8, 2048)])
-def test_mlrd_matches_oracle(cuda, r_k, r_v, B, S):
+def test_mlrd_matches_oracle(cuda, kernel, r_k, r_v, B, S):
     g = torch.Generator().manual_seed(1000 + r_k + r_v + B + S)
     q, k_lat, u_k, v_lat, _, pos, cos, sin = _inputs(g, B, 8, 32, S, r_k, r_v)
     ref = oracle.reference_decode(q, k_lat, u_k, v_lat, pos, cos, sin, 128 ** -0.5)
     out = _run_fused(cuda, q, k_lat, u_k, v_lat, pos, cos, sin, 128 ** -0.5)
-    assert_close(out, _bf(ref), f"r_k={r_k} r_v={r_v} B={B} S={S}")
+    assert_close(out, _bf(ref), f"r_k={r_k} r_v={r_v} B={B} S={S}", per_row=False)
     out32 = _run_fused(cuda, q, k_lat, u_k, v_lat, pos, cos, sin, 128 ** -0.5, out_dtype=torch.float32)
     assert_close(out32, ref, "fp32 out")
 
 
-def test_full_context_rows_are_checked_per_row(cuda):
+def test_full_context_rows_are_checked_per_row(cuda, kernel):
     """Every row at full context (S-1): the rows the flattened PCC cannot see (G_kernel.md finding)."""
     g = torch.Generator().manual_seed(7)
     B, S = 4, 4096
@@ -107,7 +123,7 @@ def test_full_context_rows_are_checked_per_row(cuda):
 
 
 @pytest.mark.parametrize("splits", [1, 2, 7, 64])
-def test_split_count_does_not_change_the_result(cuda, splits):
+def test_split_count_does_not_change_the_result(cuda, kernel, splits):
     g = torch.Generator().manual_seed(11)
     q, k_lat, u_k, v_lat, _, pos, cos, sin = _inputs(g, 3, 8, 32, 3000, 64, 64)
     ref = oracle.reference_decode(q, k_lat, u_k, v_lat, pos, cos, sin, 128 ** -0.5)
@@ -115,18 +131,18 @@ def test_split_count_does_not_change_the_result(cuda, splits):
     assert_close(out, ref, f"splits={splits}")
 
 
-def test_negative_cur_pos_skips_the_row(cuda):
+def test_negative_cur_pos_skips_the_row(cuda, kernel):
     g = torch.Generator().manual_seed(12)
     q, k_lat, u_k, v_lat, _, pos, cos, sin = _inputs(g, 3, 8, 32, 256, 32, 32)
     pos[1] = -1
-    out = _run_fused(cuda, q, k_lat, u_k, v_lat, pos, cos, sin, 128 ** -0.5)
+    out = _run_fused(cuda, q, k_lat, u_k, v_lat, pos, cos, sin, 128 ** -0.5, out_dtype=torch.float32)
     assert torch.count_nonzero(out[0, 1]) == 0
     keep = torch.tensor([0, 2])
     ref = oracle.reference_decode(q[:, keep], k_lat[keep], u_k, v_lat[keep], pos[keep], cos, sin, 128 ** -0.5)
-    assert_close(out[:, keep], _bf(ref), "rows around a skipped row")
+    assert_close(out[:, keep], ref, "rows around a skipped row")
 
 
-def test_garbage_beyond_cur_pos_is_never_read_into_the_output(cuda):
+def test_garbage_beyond_cur_pos_is_never_read_into_the_output(cuda, kernel):
     """Cache rows past cur_pos hold NaN: masked positions must contribute exactly nothing."""
     g = torch.Generator().manual_seed(13)
     q, k_lat, u_k, v_lat, _, pos, cos, sin = _inputs(g, 4, 8, 32, 512, 64, 64)
@@ -134,12 +150,12 @@ def test_garbage_beyond_cur_pos_is_never_read_into_the_output(cuda):
     for b in range(4):
         k_lat[b, :, int(pos[b]) + 1:] = float("nan")
         v_lat[b, :, int(pos[b]) + 1:] = float("nan")
-    out = _run_fused(cuda, q, k_lat, u_k, v_lat, pos, cos, sin, 128 ** -0.5)
+    out = _run_fused(cuda, q, k_lat, u_k, v_lat, pos, cos, sin, 128 ** -0.5, out_dtype=torch.float32)
     assert torch.isfinite(out).all()
-    assert_close(out, _bf(ref), "NaN tail")
+    assert_close(out, ref, "NaN tail")
 
 
-def test_glrd_small_group_latents_match_oracle(cuda):
+def test_glrd_small_group_latents_match_oracle(cuda, kernel):
     """Grouped latents (gs 4) with in-kernel V through u_v, latents up to 128 wide."""
     g = torch.Generator().manual_seed(14)
     nkv, gs = 8, 4
@@ -152,20 +168,30 @@ def test_glrd_small_group_latents_match_oracle(cuda):
 
 
 def test_identity_factorisation_equals_plain_gqa_decode(cuda):
-    """U = I at rank 128 must equal plain GQA flash-decode over the rotated K."""
+    """U = I at rank 128 must equal plain GQA flash-decode over the rotated K.
+
+    A stock cache holds the rotated K in bf16, so the plain path attends over K_rot rounded to bf16 while
+    the identity path rotates the exact latent in fp32. Each kernel is held to the per-row bar against
+    the oracle on its own inputs; the two paths are compared on the global bar, where the only
+    difference left is that bf16 rounding of the stock cache (~2e-3 per long row, in the identity path's
+    favour)."""
     from palu_b200 import fused
     g = torch.Generator().manual_seed(15)
     B, nkv, nh, S = 4, 8, 32, 1500
     q, k_lat, _, v_lat, _, pos, cos, sin = _inputs(g, B, nkv, nh, S, 128, 128)
     eye = torch.eye(128).expand(nkv, 128, 128).contiguous()
-    palu_out = _run_fused(cuda, q, k_lat, eye, v_lat, pos, cos, sin, 128 ** -0.5)
+    palu_out = _run_fused(cuda, q, k_lat, eye, v_lat, pos, cos, sin, 128 ** -0.5, out_dtype=torch.float32)
     T = oracle.rope_transformation_matrix(128)
     K = _bf(k_lat * cos + (k_lat @ T) * sin)          # rotated full K, as a stock cache holds it
     plain = fused.plain_gqa_decode(q.to(cuda, torch.bfloat16), K.to(cuda, torch.bfloat16),
-                                   v_lat.to(cuda, torch.bfloat16), pos.to(cuda)).float().cpu()
+                                   v_lat.to(cuda, torch.bfloat16), pos.to(cuda), out_dtype=torch.float32).cpu()
     ref = oracle.reference_decode(q, k_lat, eye, v_lat, pos, cos, sin, 128 ** -0.5)
-    assert_close(palu_out, _bf(ref), "identity palu vs oracle")
-    assert_close(plain, palu_out, "plain GQA vs identity palu")
+    ones, zeros = torch.ones(S, 128), torch.zeros(S, 128)
+    ref_plain = oracle.reference_decode(q, K, eye, v_lat, pos, ones, zeros, 128 ** -0.5)
+    assert_close(palu_out, ref, "identity palu vs oracle")
+    assert_close(plain, ref_plain, "plain GQA vs oracle on the bf16 K cache")
+    mx, mn = rel_errors(plain, palu_out)
+    assert mx <= MAX_REL and mn <= MEAN_REL, f"plain vs identity palu: max {mx:.3e} mean {mn:.3e}"
 
 
 def test_append_latents_is_bit_exact(cuda):
@@ -197,3 +223,31 @@ def test_pack_cs_table_is_exact(cuda, dtype):
     c = tab[:, 0:128:2].to(torch.bfloat16).view(torch.int16).to(torch.int32) & 0xFFFF
     s = tab[:, 128::2].to(torch.bfloat16).view(torch.int16).to(torch.int32) & 0xFFFF
     assert torch.equal(packed, (c | (s << 16)).to(torch.int32))
+
+
+def test_kernel_families_agree_and_report_ok_status(cuda):
+    """The tcgen05 kernel and the mma.sync kernel on the same inputs, through the low-level entry with an
+    explicit workspace whose status word must read 0 (no bounded wait expired)."""
+    from palu_b200 import _lib, fused
+    g = torch.Generator().manual_seed(17)
+    B, S = 6, 5000
+    q, k_lat, u_k, v_lat, _, pos, cos, sin = _inputs(g, B, 8, 32, S, 64, 64)
+    dev = cuda
+    cs = fused.pack_cs_table(fused.cs_table(cos, sin, S).to(dev, torch.bfloat16))
+    args = (q[0].to(dev, torch.bfloat16), k_lat.to(dev, torch.bfloat16), v_lat.to(dev, torch.bfloat16),
+            u_k.to(dev, torch.bfloat16), cs, pos.to(dev))
+    d = _lib.dims(B, 32, 8, 8, 64, 64, S)
+    outs = {}
+    try:
+        for which in (_lib.PALU_KERNEL_TC, _lib.PALU_KERNEL_MMA):
+            _lib.set_kernel(which)
+            assert _lib.kernel_for(d) == which
+            ws = _lib.new_workspace(d, dev)
+            outs[which] = fused.decode(*args, out_dtype=torch.float32, workspace=ws).cpu()
+            assert _lib.read_status(ws) == 0
+    finally:
+        _lib.set_kernel(_lib.PALU_KERNEL_AUTO)
+    ref = oracle.reference_decode(q, k_lat, u_k, v_lat, pos, cos, sin, 128 ** -0.5)[0]
+    assert_close(outs[_lib.PALU_KERNEL_TC], ref, "tc vs oracle")
+    assert_close(outs[_lib.PALU_KERNEL_MMA], ref, "mma vs oracle")
+    assert_close(outs[_lib.PALU_KERNEL_TC], outs[_lib.PALU_KERNEL_MMA], "tc vs mma")

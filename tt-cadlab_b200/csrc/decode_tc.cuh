@@ -1,0 +1,692 @@
+// Split-K flash-decode over Palu latent caches on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// One CTA owns (batch row b, KV head h, split s): a contiguous range of 128-token tiles of the positions
+// 0..cur_pos[b]. Its 16 warps form two halves; half g serves the tiles t with t % 2 == g:
+//   warp 8g+0   TMA producer: K-latent tiles of half g (half 0 also loads U_k once)
+//   warp 8g+1   the thread issuing half g's tcgen05.mma and commits (warp 1 also allocates TMEM)
+//   warp 8g+2   TMA producer: packed (cos, sin) table chunks (16 frequency pairs x 128 rows each)
+//   warp 8g+3   TMA producer: V-latent tiles (V lives longest, until PV)
+//   warps 8g+4 .. 8g+7   softmax group g: one thread per token row of the tile
+// Per tile t (group g = t % 2; thread = token row inside the tile):
+//   MMA    D_k[128 tok x 128 dim] (f32) = lat_k (smem, K-major) x U_k (smem, MN-major)
+//   group  K row -> RoPE in registers from the table -> K_rot as fp16 into its own TMEM columns: the A
+//          operand of the next MMA (fp16 keeps 11 significant bits; q is bf16, exact in fp16)
+//   MMA    D_s[128 tok x 16] (f32) = K_rot (TMEM) x Q^T (smem, fp16)
+//   group  online softmax over the query heads (exp2 domain); P^T as bf16 hi + lo -> smem
+//   MMA    D_o[128 lat x 16] (f32) = V^T (smem, MN-major: the V tile exactly as TMA wrote it) x P^T
+//   group  thread c (latent dim c) accumulates O[h][c] = O * alpha + hi + lo in registers
+// Software pipeline: in its iteration for tile t a group does RoPE(t), softmax(t-2), accumulate(t-4), so
+// each wait is for an MMA issued two tiles earlier; the MMA thread issues QK(t), reconstruct(t+2),
+// PV(t-2). Every ring, barrier and TMEM region is private to one half, each role thread blocks (sleeping
+// in mbarrier try_wait) on one barrier at a time, and no barrier can run two phases ahead of its waiter,
+// so parity waits never alias. The two groups merge their
+// (m, l, O) at the end into one split partial (combine.cuh merges the splits). Every wait is bounded (1 s of globaltimer): on expiry the CTA records a status code,
+// all roles stop, copies and MMAs in flight are drained, and TMEM is freed.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include "palu_common.cuh"
+
+namespace palu {
+namespace tc {
+
+constexpr int kThreads = 512;
+constexpr int kTile = 128;
+constexpr int kBox = 16384;             // one TMA box: 128 rows x 128 B
+constexpr int kTmemCols = 512;
+constexpr int kGrpCols = 256;           // TMEM columns reserved per softmax group
+constexpr int kColDk = 0;               // 128 columns: f32 K tile (reconstruct output)
+constexpr int kColA = 128;              // 64 columns: fp16 K_rot, the A operand of QK (packed 2 per column)
+constexpr int kColDs = 192;             // 2 x 16 columns: scores, double-buffered
+constexpr int kColDo = 224;             // 2 x 16 columns: PV result, double-buffered
+constexpr unsigned long long kWaitNs = 1000000000ull;  // bound on any single wait
+constexpr uint32_t kSuspendHintNs = 0x989680;          // mbarrier try_wait suspend-time hint
+
+enum : int { kStatusOk = 0, kStatusTimeout = 1 };
+
+struct TcParams {
+  const __nv_bfloat16* q;   // [B][n_q][128]
+  const int32_t* cur_pos;   // [B]
+  float* ws_o;              // [B][n_kv][splits][rep][rv]
+  float* ws_ml;             // [B][n_kv][splits][rep][2]
+  int* status;              // device status word, 0 = ok
+  int batch, n_q, n_kv, n_groups, rk, rv, max_seq, splits, rep;
+  float scale_log2;
+};
+
+template <int KBK, int KBV>
+struct Layout {
+  static constexpr int K_BYTES = KBK * kBox;
+  static constexpr int V_BYTES = KBV * kBox;
+  static constexpr int TCH_BYTES = 8192;              // table chunk: 128 rows x 16 pairs x 4 B (SWIZZLE_64B)
+  static constexpr int U_BYTES = KBK * 2 * 64 * 128;  // 2 N-blocks x (<= 64 KBK rows) x 128 B
+  static constexpr int Q_BYTES = 2 * 2048;            // 2 K-blocks x 16 rows x 128 B (fp16)
+  static constexpr int P_BYTES = 2 * 2048;            // one buffer: 2 K-blocks x 16 rows x 128 B (bf16)
+  static constexpr int O_BYTES = 2 * 4 * 128 * 4;     // merge area [2 groups][4 heads][128] fp32
+  static constexpr int MISC_BYTES = 2048;
+  static constexpr int FIXED = U_BYTES + Q_BYTES + 4 * P_BYTES + O_BYTES + MISC_BYTES + 1024;
+  static constexpr int BUDGET = 227 * 1024;
+  // Rings, all group-private: stage i of a ring only holds tiles of group (i % 2) (K, V) or chunks of
+  // group (i / T_SLOTS) (table). V: one stage per group. Table: 4 chunk slots per group (a whole tile)
+  // when that fits, else 2. K: 2 stages per group when that fits, else 1.
+  static constexpr int NS_V = 2;
+  static constexpr int T_SLOTS = FIXED + 2 * K_BYTES + NS_V * V_BYTES + 8 * TCH_BYTES <= BUDGET ? 4 : 2;
+  static constexpr int NS_K = FIXED + 4 * K_BYTES + NS_V * V_BYTES + 2 * T_SLOTS * TCH_BYTES <= BUDGET ? 4 : 2;
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + NS_K * K_BYTES;
+  static constexpr int OFF_TAB = OFF_V + NS_V * V_BYTES;
+  static constexpr int OFF_U = OFF_TAB + 2 * T_SLOTS * TCH_BYTES;
+  static constexpr int OFF_Q = OFF_U + U_BYTES;
+  static constexpr int OFF_P = OFF_Q + Q_BYTES;
+  static constexpr int OFF_O = OFF_P + 4 * P_BYTES;
+  static constexpr int OFF_MISC = OFF_O + O_BYTES;
+  static constexpr int TOTAL = OFF_MISC + MISC_BYTES + 1024;  // + slack to align the base to 1024
+  static_assert(TOTAL <= BUDGET, "shared memory budget");
+};
+
+// ---- PTX wrappers -----------------------------------------------------------------------------------
+
+PALU_DEVINL void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+PALU_DEVINL void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+PALU_DEVINL void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+PALU_DEVINL bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+PALU_DEVINL bool mbar_test(uint32_t bar, uint32_t parity) {  // non-blocking
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+PALU_DEVINL unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;\n" : "=l"(t));
+  return t;
+}
+
+// Bounded wait for `parity` on `bar`. Returns false on timeout or when another role already gave up.
+PALU_DEVINL bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
+  if (mbar_try(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (;;) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort_flag) return mbar_try(bar, parity);
+    if (globaltimer() - t0 > kWaitNs) {
+      *abort_flag = 1;
+      atomicExch(status, kStatusTimeout);
+      return false;
+    }
+  }
+}
+
+// Bounded wait used on the abort path, to let copies already in flight land before the CTA exits.
+PALU_DEVINL void mbar_drain(uint32_t bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_try(bar, parity))
+    if (globaltimer() - t0 > kWaitNs) return;
+}
+
+PALU_DEVINL void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+PALU_DEVINL void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];\n" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+PALU_DEVINL void tma_prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Shared-memory matrix descriptor, SWIZZLE_128B, version 1 (sm_100). Offsets in bytes.
+PALU_DEVINL uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor, kind::f16 with f32 accumulate, M = 128. fmt: 0 = f16, 1 = bf16 (A and B alike).
+__host__ __device__ constexpr uint32_t idesc_f16(int n, uint32_t fmt, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+PALU_DEVINL void mma_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+PALU_DEVINL void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+PALU_DEVINL void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
+               : "memory");
+}
+PALU_DEVINL void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+PALU_DEVINL void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+PALU_DEVINL void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
+PALU_DEVINL void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+PALU_DEVINL void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+
+PALU_DEVINL void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+PALU_DEVINL void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+PALU_DEVINL void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+PALU_DEVINL float warp_max(float v) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;\n" : "=f"(r) : "f"(v));
+  return r;
+}
+PALU_DEVINL void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+PALU_DEVINL void tmem_ld4(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
+PALU_DEVINL void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
+PALU_DEVINL uint32_t pack_half2(float x0, float x1) {
+  __half2 h = __floats2half2_rn(x0, x1);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Byte offset of 16-bit element (row, k) of a K-major SWIZZLE_128B operand stored as 64-element
+// K-blocks of `rows` rows each.
+PALU_DEVINL uint32_t sw128_offset(int row, int k, int rows) {
+  const int blk = k >> 6, kk = k & 63;
+  return (uint32_t)(blk * rows * 128 + row * 128 + ((((kk >> 3) ^ (row & 7))) << 4) + (kk & 7) * 2);
+}
+
+// ---- the kernel --------------------------------------------------------------------------------------
+
+template <int KBK, int KBV>
+__global__ void __launch_bounds__(kThreads, 1)
+    palu_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                          const __grid_constant__ CUtensorMap tm_tab, const __grid_constant__ CUtensorMap tm_u,
+                          const TcParams p) {
+  using Lay = Layout<KBK, KBV>;
+  constexpr int NS_K = Lay::NS_K, NS_V = Lay::NS_V, T_SLOTS = Lay::T_SLOTS;
+  constexpr int NS_T = 2 * T_SLOTS;  // table chunk slots, [group][slot]
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int item_lat = b * p.n_groups + kvh / (p.n_kv / p.n_groups);
+
+  int L = p.cur_pos[b] + 1;
+  L = L < 0 ? 0 : (L > p.max_seq ? p.max_seq : L);
+  const int n_tiles = (L + kTile - 1) / kTile;
+  const int per = (n_tiles + p.splits - 1) / p.splits;
+  const int tile0 = split * per;
+  const int nt = max(0, min(n_tiles, tile0 + per) - tile0);
+
+  // ---- barriers and scalars (misc area) ----
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Lay::OFF_MISC);
+  auto bar = [&](int i) { return smem_u32(bars + i); };
+  constexpr int B_KF = 0, B_KE = B_KF + NS_K, B_VF = B_KE + NS_K, B_VE = B_VF + NS_V, B_TF = B_VE + NS_V,
+                B_TE = B_TF + NS_T, B_UF = B_TE + NS_T, B_REC = B_UF + 1, B_AF = B_REC + 2, B_SF = B_AF + 2,
+                B_PF = B_SF + 4, B_OF = B_PF + 4, B_OR = B_OF + 4, B_MX = B_OR + 4, B_DRAIN = B_MX + 4,
+                B_COUNT = B_DRAIN + 2;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + B_COUNT);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+  float* s_max = reinterpret_cast<float*>(s_tmem + 4);  // [2 groups][2 bufs][4 warps][4 heads]
+  float* s_lsum = s_max + 64;                             // [2 groups][4 warps][4 heads]
+  float* s_m = s_lsum + 32;                               // [2 groups][4 heads]
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS_K; ++s) {
+      mbar_init(bar(B_KF + s), 1);
+      mbar_init(bar(B_KE + s), 1);
+    }
+    for (int s = 0; s < NS_V; ++s) {
+      mbar_init(bar(B_VF + s), 1);
+      mbar_init(bar(B_VE + s), 1);
+    }
+    for (int s = 0; s < NS_T; ++s) {
+      mbar_init(bar(B_TF + s), 1);
+      mbar_init(bar(B_TE + s), 4);
+    }
+    mbar_init(bar(B_UF), 1);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(bar(B_REC + g), 1);
+      mbar_init(bar(B_AF + g), 4);
+      for (int x = 0; x < 2; ++x) {
+        // p_full is double-buffered by tile parity: a group may finish softmax(t) before the MMA thread
+        // has tested softmax(t-2)'s arrival, which on a single barrier would alias two phases.
+        mbar_init(bar(B_PF + 2 * g + x), 4);
+        mbar_init(bar(B_SF + 2 * g + x), 1);
+        mbar_init(bar(B_OF + 2 * g + x), 1);
+        mbar_init(bar(B_OR + 2 * g + x), 4);
+        mbar_init(bar(B_MX + 2 * g + x), 4);
+      }
+    }
+    mbar_init(bar(B_DRAIN), 1);
+    mbar_init(bar(B_DRAIN + 1), 1);
+    *s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 1) {  // TMEM: 512 columns; the base address lands in shared memory
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(s_tmem)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+  }
+  if ((warp & 7) >= 4) {
+    const int t = ((warp >> 3) * 4 + (warp & 3)) * 32 + lane;  // 0..255 over the 8 softmax warps
+    // Q^T operand, fp16, K-major SWIZZLE_128B: 16 rows (this KV head's query heads, zero padded) x 128 dims.
+    {
+      const int row = t >> 4, chunk = t & 15;  // 8 dims per 16-byte chunk
+      uint4 w = make_uint4(0, 0, 0, 0);
+      if (row < p.rep) {
+        const uint4 src = *reinterpret_cast<const uint4*>(p.q + ((size_t)b * p.n_q + kvh * p.rep + row) * kHeadDim +
+                                                          chunk * 8);
+        const uint32_t in[4] = {src.x, src.y, src.z, src.w};
+        uint32_t outw[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = unpack_bf16(in[i]);
+          outw[i] = pack_half2(f.x, f.y);
+        }
+        w = make_uint4(outw[0], outw[1], outw[2], outw[3]);
+      }
+      const uint32_t off = (chunk >> 3) * 2048 + row * 128 + (((chunk & 7) ^ (row & 7)) << 4);
+      *reinterpret_cast<uint4*>(smem + Lay::OFF_Q + off) = w;
+    }
+    for (int e = t; e < 4 * Lay::P_BYTES / 16; e += 256)
+      reinterpret_cast<uint4*>(smem + Lay::OFF_P)[e] = make_uint4(0, 0, 0, 0);
+    fence_proxy_async();
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  // ============================== roles ==============================
+  const int half = warp >> 3, role = warp & 7;
+  if (role == 0 || role == 2 || role == 3) {
+    // ---- TMA producers of half g: role 0 = K latent (+ U_k once), 3 = V latent, 2 = table chunks.
+    const int g = half;
+    if (lane == 0 && nt > g) {
+      if (role == 0) {
+        tma_prefetch_map(&tm_k);
+        if (g == 0) {
+          tma_prefetch_map(&tm_u);
+          mbar_expect_tx(bar(B_UF), 2 * p.rk * 128);
+          tma_load_2d(sbase + Lay::OFF_U, &tm_u, bar(B_UF), 0, kvh * p.rk);
+          tma_load_2d(sbase + Lay::OFF_U + p.rk * 128, &tm_u, bar(B_UF), 64, kvh * p.rk);
+        }
+      } else {
+        tma_prefetch_map(role == 3 ? &tm_v : &tm_tab);
+      }
+      const int per_tile = role == 2 ? 4 : 1;
+      const int count = (g == 0 ? (nt + 1) / 2 : nt / 2) * per_tile;
+      int issued = 0;
+      for (int n = 0; n < count; ++n) {
+        const int j = n / per_tile, c = n % per_tile, t = g + 2 * j;
+        int sb, use;
+        uint32_t full, empty, dst, bytes;
+        if (role == 0) {
+          sb = t % NS_K;
+          use = t / NS_K;
+          full = bar(B_KF + sb);
+          empty = bar(B_KE + sb);
+          dst = sbase + Lay::OFF_K + sb * Lay::K_BYTES;
+          bytes = Lay::K_BYTES;
+        } else if (role == 3) {
+          sb = t % NS_V;
+          use = t / NS_V;
+          full = bar(B_VF + sb);
+          empty = bar(B_VE + sb);
+          dst = sbase + Lay::OFF_V + sb * Lay::V_BYTES;
+          bytes = Lay::V_BYTES;
+        } else {
+          sb = g * T_SLOTS + n % T_SLOTS;
+          use = n / T_SLOTS;
+          full = bar(B_TF + sb);
+          empty = bar(B_TE + sb);
+          dst = sbase + Lay::OFF_TAB + sb * Lay::TCH_BYTES;
+          bytes = Lay::TCH_BYTES;
+        }
+        if (use >= 1 && !mbar_wait(empty, (use - 1) & 1, s_abort, p.status)) break;
+        mbar_expect_tx(full, bytes);
+        const int row = (tile0 + t) * kTile;
+        if (role == 0) {
+#pragma unroll
+          for (int kb = 0; kb < KBK; ++kb) tma_load_3d(dst + kb * kBox, &tm_k, full, kb * 64, row, item_lat);
+        } else if (role == 3) {
+#pragma unroll
+          for (int vb = 0; vb < KBV; ++vb) tma_load_3d(dst + vb * kBox, &tm_v, full, vb * 64, row, item_lat);
+        } else {
+          tma_load_2d(dst, &tm_tab, full, c * 16, row);
+        }
+        issued = n + 1;
+      }
+      if (*s_abort) {  // let every copy already issued land before the CTA can exit
+        if (role == 0 && g == 0) mbar_drain(bar(B_UF), 0);
+        const int ring = role == 0 ? NS_K / 2 : (role == 3 ? NS_V / 2 : T_SLOTS);
+        for (int n = max(0, issued - ring); n < issued; ++n) {
+          const int t = g + 2 * (n / per_tile);
+          if (role == 0) mbar_drain(bar(B_KF + t % NS_K), (t / NS_K) & 1);
+          else if (role == 3) mbar_drain(bar(B_VF + t % NS_V), (t / NS_V) & 1);
+          else mbar_drain(bar(B_TF + g * T_SLOTS + n % T_SLOTS), (n / T_SLOTS) & 1);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (role == 1) {  // ---- MMA issue for half g: QK(t) -> reconstruct(t+2) -> PV(t-2) per tile
+    const int g = half;
+    if (lane == 0 && nt > g) {
+      constexpr uint32_t ID_REC = idesc_f16(128, 1, false, true);  // bf16 lat x bf16 U (MN-major)
+      constexpr uint32_t ID_QK = idesc_f16(16, 0, false, false);   // fp16 K_rot (TMEM) x fp16 Q
+      constexpr uint32_t ID_PV = idesc_f16(16, 1, true, false);    // bf16 V^T (MN-major) x bf16 P
+      const uint32_t sU = sbase + Lay::OFF_U, sQ = sbase + Lay::OFF_Q;
+      const uint32_t u_lbo = p.rk * 128;            // U: stride between the two 64-dim N-blocks
+      const uint32_t v_lbo = p.rv > 64 ? kBox : 0;  // V: second 64-dim M-block (or a duplicate of the first)
+      const uint32_t tg = tmem + g * kGrpCols;
+      auto recon = [&](int t) -> bool {
+        const int s = t % NS_K;
+        if (!mbar_wait(bar(B_KF + s), (t / NS_K) & 1, s_abort, p.status)) return false;
+        fence_after();
+        const uint32_t sK = sbase + Lay::OFF_K + s * Lay::K_BYTES;
+        for (int kk = 0; kk < p.rk / 16; ++kk)
+          mma_ss(tg + kColDk, sdesc(sK + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024),
+                 sdesc(sU + kk * 2048, u_lbo, 1024), ID_REC, kk > 0);
+        mma_commit(bar(B_KE + s));
+        mma_commit(bar(B_REC + g));
+        return true;
+      };
+      bool ok = mbar_wait(bar(B_UF), 0, s_abort, p.status) && recon(g);
+      for (int t = g; ok && t - 2 < nt; t += 2) {
+        const int j = t >> 1;
+        if (t < nt) {  // QK(t)
+          if (!mbar_wait(bar(B_AF + g), j & 1, s_abort, p.status)) break;
+          fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_ts(tg + kColDs + (j & 1) * 16, tg + kColA + kk * 8,
+                   sdesc(sQ + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), ID_QK, kk > 0);
+          mma_commit(bar(B_SF + 2 * g + (j & 1)));
+        }
+        if (t + 2 < nt && !recon(t + 2)) break;  // D_k is free: RoPE(t) read it before QK(t) was allowed
+        const int tp = t - 2;
+        if (tp >= 0) {  // PV(t - 2)
+          const int jp = tp >> 1, sv = tp % NS_V;
+          if (!mbar_wait(bar(B_PF + 2 * g + (jp & 1)), (jp >> 1) & 1, s_abort, p.status)) break;
+          if (jp >= 2 && !mbar_wait(bar(B_OR + 2 * g + (jp & 1)), ((jp >> 1) - 1) & 1, s_abort, p.status)) break;
+          if (!mbar_wait(bar(B_VF + sv), (tp / NS_V) & 1, s_abort, p.status)) break;
+          fence_after();
+          const uint32_t sV = sbase + Lay::OFF_V + sv * Lay::V_BYTES;
+          const uint32_t sP = sbase + Lay::OFF_P + (2 * g + (jp & 1)) * Lay::P_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_ss(tg + kColDo + (jp & 1) * 16, sdesc(sV + kk * 2048, v_lbo, 1024),
+                   sdesc(sP + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), ID_PV, kk > 0);
+          mma_commit(bar(B_OF + 2 * g + (jp & 1)));
+          mma_commit(bar(B_VE + sv));
+        }
+      }
+      // Drain: every MMA this thread issued has completed once this barrier flips.
+      mma_commit(bar(B_DRAIN + g));
+      mbar_drain(bar(B_DRAIN + g), 0);
+    }
+    __syncwarp();
+  } else {  // ---- softmax group g (roles 4..7)
+    const int g = half, quarter = warp & 3, row = quarter * 32 + lane;
+    const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + g * kGrpCols;
+    float m_run[4], l_run[4], o_acc[4], alpha0[4], alpha1[4];  // alphaN: softmax scale of tiles j with j%2 == N
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      m_run[h] = -INFINITY;
+      l_run[h] = 0.f;
+      o_acc[h] = 0.f;
+      alpha0[h] = alpha1[h] = 1.f;
+    }
+    const int n_mine = (nt - g + 1) / 2;  // tiles g, g+2, ... below nt
+    for (int i = 0; i < n_mine + 2; ++i) {
+      // ---- RoPE(t): K row -> rotate -> fp16 A operand over the first 64 columns of D_k -------------
+      if (i < n_mine) {
+        if (!mbar_wait(bar(B_REC + g), i & 1, s_abort, p.status)) break;
+        fence_after();
+        // 8 half-chunks of 16 D_k columns (8 frequency pairs). The next half-chunk's TMEM load is issued
+        // right after the current one landed (tcgen05.wait::ld waits for every load in flight), so it
+        // overlaps this half-chunk's table reads and arithmetic.
+        bool ok = true;
+        uint32_t kbuf[2][16];
+        tmem_ld16(trow + kColDk, kbuf[0]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          const int ch = h >> 1, n = i * 4 + ch, sb = g * T_SLOTS + n % T_SLOTS;
+          if (h + 1 < 8) tmem_ld16(trow + kColDk + 16 * (h + 1), kbuf[(h + 1) & 1]);
+          if ((h & 1) == 0 && !mbar_wait(bar(B_TF + sb), (n / T_SLOTS) & 1, s_abort, p.status)) {
+            ok = false;
+            break;
+          }
+          // SWIZZLE_64B rows of 64 B: 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3).
+          const unsigned char* tb = smem + Lay::OFF_TAB + sb * Lay::TCH_BYTES + row * 64;
+          uint32_t cs[8];
+#pragma unroll
+          for (int c2 = 0; c2 < 2; ++c2) {
+            const uint4 w = *reinterpret_cast<const uint4*>(tb + (((2 * (h & 1) + c2) ^ ((row >> 1) & 3)) << 4));
+            cs[4 * c2 + 0] = w.x;
+            cs[4 * c2 + 1] = w.y;
+            cs[4 * c2 + 2] = w.z;
+            cs[4 * c2 + 3] = w.w;
+          }
+          uint32_t out[8];
+#pragma unroll
+          for (int pp = 0; pp < 8; ++pp) {
+            const float c = __uint_as_float(cs[pp] << 16), sn = __uint_as_float(cs[pp] & 0xFFFF0000u);
+            const float k0 = __uint_as_float(kbuf[h & 1][2 * pp]), k1 = __uint_as_float(kbuf[h & 1][2 * pp + 1]);
+            out[pp] = pack_half2(k0 * c - k1 * sn, k1 * c + k0 * sn);
+          }
+          if (h & 1) {  // both halves of this table chunk consumed by every lane: its slot may refill
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_TE + sb));
+          }
+          if (h == 0 && i >= 1) {
+            // A still feeds QK(t - 2) until that MMA completes; its commit is the scores barrier.
+            const int jq = i - 1;
+            if (!mbar_wait(bar(B_SF + 2 * g + (jq & 1)), (jq >> 1) & 1, s_abort, p.status)) {
+              ok = false;
+              break;
+            }
+            fence_after();
+          }
+          tmem_st8(trow + kColA + 8 * h, out);
+          if (h + 1 < 8) tmem_wait_ld();
+        }
+        if (!ok) {
+          tmem_wait_ld();  // no TMEM load may still be landing in registers
+          break;
+        }
+        tmem_wait_st();
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_AF + g));
+      }
+      // ---- softmax(t - 2) ---------------------------------------------------------------------------
+      if (i >= 1 && i - 1 < n_mine) {
+        const int j = i - 1, t = g + 2 * j;
+        if (!mbar_wait(bar(B_SF + 2 * g + (j & 1)), (j >> 1) & 1, s_abort, p.status)) break;
+        fence_after();
+        uint32_t sc[4];
+        tmem_ld4(trow + kColDs + (j & 1) * 16, sc);
+        tmem_wait_ld();
+        const int tile_start = (tile0 + t) * kTile;
+        const bool valid = tile_start + row < L;
+        float x[4], mx[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          x[h] = (valid && h < p.rep) ? __uint_as_float(sc[h]) * p.scale_log2 : -INFINITY;
+          mx[h] = warp_max(x[h]);
+        }
+        // The 4 warps' maxima meet through a double-buffered mbarrier (bounded wait, unlike bar.sync).
+        float* smx = s_max + ((g * 2 + (j & 1)) * 4) * 4;
+        if (lane == 0) {
+#pragma unroll
+          for (int h = 0; h < 4; ++h) smx[quarter * 4 + h] = mx[h];
+          mbar_arrive(bar(B_MX + 2 * g + (j & 1)));
+        }
+        if (!mbar_wait(bar(B_MX + 2 * g + (j & 1)), (j >> 1) & 1, s_abort, p.status)) break;
+        unsigned char* sP = smem + Lay::OFF_P + (2 * g + (j & 1)) * Lay::P_BYTES;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float tmax = fmaxf(fmaxf(smx[h], smx[4 + h]), fmaxf(smx[8 + h], smx[12 + h]));
+          const float m_new = fmaxf(m_run[h], tmax);
+          const float alpha = (m_new == -INFINITY) ? 1.f : fast_exp2(m_run[h] - m_new);
+          const float pv = (m_new == -INFINITY) ? 0.f : fast_exp2(x[h] - m_new);
+          if (j & 1)
+            alpha1[h] = alpha;
+          else
+            alpha0[h] = alpha;
+          l_run[h] = l_run[h] * alpha + pv;
+          m_run[h] = m_new;
+          const __nv_bfloat16 hi = __float2bfloat16_rn(pv);
+          const __nv_bfloat16 lo = __float2bfloat16_rn(pv - __bfloat162float(hi));
+          *reinterpret_cast<__nv_bfloat16*>(sP + sw128_offset(h, row, 16)) = hi;
+          *reinterpret_cast<__nv_bfloat16*>(sP + sw128_offset(4 + h, row, 16)) = lo;
+        }
+        if (tile_start + kTile > L) {
+          // V rows past cur_pos may hold anything (NaN included): P is 0 there, but 0 * NaN is not.
+          const int sv = t % NS_V;
+          if (!mbar_wait(bar(B_VF + sv), (t / NS_V) & 1, s_abort, p.status)) break;
+          if (!valid) {
+            unsigned char* vrow = smem + Lay::OFF_V + sv * Lay::V_BYTES + row * 128;
+#pragma unroll
+            for (int vb = 0; vb < KBV; ++vb)
+#pragma unroll
+              for (int c = 0; c < 8; ++c) reinterpret_cast<uint4*>(vrow + vb * kBox)[c] = make_uint4(0, 0, 0, 0);
+          }
+        }
+        fence_proxy_async();
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_PF + 2 * g + (j & 1)));
+      }
+      // ---- accumulate(t - 4) ------------------------------------------------------------------------
+      if (i >= 2 && i - 2 < n_mine) {
+        const int j = i - 2;
+        if (!mbar_wait(bar(B_OF + 2 * g + (j & 1)), (j >> 1) & 1, s_abort, p.status)) break;
+        fence_after();
+        uint32_t ov[8];
+        tmem_ld8(trow + kColDo + (j & 1) * 16, ov);
+        tmem_wait_ld();
+#pragma unroll
+        for (int h = 0; h < 4; ++h)
+          o_acc[h] = o_acc[h] * ((j & 1) ? alpha1[h] : alpha0[h]) + __uint_as_float(ov[h]) + __uint_as_float(ov[4 + h]);
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_OR + 2 * g + (j & 1)));
+      }
+    }
+    // ---- this group's partial -> shared memory -----------------------------------------------------
+    float* s_o = reinterpret_cast<float*>(smem + Lay::OFF_O);
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      float v = l_run[h];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) s_lsum[(g * 4 + quarter) * 4 + h] = v;
+      s_o[(g * 4 + h) * 128 + row] = o_acc[h];
+    }
+    if (quarter == 0 && lane == 0) {
+#pragma unroll
+      for (int h = 0; h < 4; ++h) s_m[g * 4 + h] = m_run[h];
+    }
+  }
+  // every role reaches this point warp-converged
+  fence_before();
+  __syncthreads();
+
+  // ---- merge the two groups and write this split's partial (unnormalised O, m, l) ----------------
+  if ((warp & 7) >= 4) {
+    const float* s_o = reinterpret_cast<const float*>(smem + Lay::OFF_O);
+    const size_t item = ((size_t)(b * p.n_kv + kvh) * p.splits + split) * p.rep;
+    for (int idx = ((warp >> 3) * 4 + (warp & 3)) * 32 + lane; idx < p.rep * p.rv; idx += 256) {
+      const int h = idx / p.rv, c = idx - h * p.rv;
+      const float m0 = s_m[h], m1 = s_m[4 + h];
+      const float M = fmaxf(m0, m1);
+      float acc = 0.f, lsum = 0.f;
+      if (M != -INFINITY) {
+        const float w0 = m0 == -INFINITY ? 0.f : fast_exp2(m0 - M);
+        const float w1 = m1 == -INFINITY ? 0.f : fast_exp2(m1 - M);
+        const float l0 = s_lsum[h] + s_lsum[4 + h] + s_lsum[8 + h] + s_lsum[12 + h];
+        const float l1 = s_lsum[16 + h] + s_lsum[20 + h] + s_lsum[24 + h] + s_lsum[28 + h];
+        acc = s_o[h * 128 + c] * w0 + s_o[(4 + h) * 128 + c] * w1;
+        lsum = l0 * w0 + l1 * w1;
+      }
+      p.ws_o[(item + h) * p.rv + c] = acc;
+      if (c == 0) {
+        p.ws_ml[(item + h) * 2 + 0] = M;
+        p.ws_ml[(item + h) * 2 + 1] = lsum;
+      }
+    }
+  }
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+}  // namespace tc
+}  // namespace palu

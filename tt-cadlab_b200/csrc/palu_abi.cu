@@ -1,6 +1,7 @@
 // C ABI of libpalu_b200 (declared in include/palu_b200.h): envelope validation, split planning,
 // workspace layout and kernel dispatch. Everything here runs on the host; the kernels live in the
 // .cuh files next to it.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -11,6 +12,7 @@
 #include "append.cuh"
 #include "combine.cuh"
 #include "decode_mma.cuh"
+#include "decode_tc.cuh"
 
 namespace {
 
@@ -89,6 +91,9 @@ int choose_splits(const palu_decode_dims* d) {
   return (int)s;
 }
 
+// Workspace layout: [256 B status header: int32 status word][O partials][(m, l) partials].
+constexpr size_t kWsHeader = 256;
+
 size_t ws_floats_o(const palu_decode_dims* d, int splits) {
   return (size_t)d->batch * d->n_kv_heads * splits * rep_of(d) * d->r_v;
 }
@@ -97,7 +102,140 @@ size_t ws_floats_ml(const palu_decode_dims* d, int splits) {
 }
 size_t ws_bytes(const palu_decode_dims* d, int splits) {
   const size_t o = (ws_floats_o(d, splits) * 4 + 255) / 256 * 256;
-  return o + ws_floats_ml(d, splits) * 4 + 256;
+  return kWsHeader + o + ws_floats_ml(d, splits) * 4 + 256;
+}
+
+// ---- tcgen05 path: availability, split planning, tensor maps ---------------------------------------
+
+int g_kernel_choice = PALU_KERNEL_AUTO;
+
+bool tc_supported(const palu_decode_dims* d, bool recon) {
+  return recon && d->r_k <= 128 && d->r_v <= 128 && rep_of(d) <= 4;
+}
+
+bool use_tc(const palu_decode_dims* d, bool recon) {
+  if (g_kernel_choice == PALU_KERNEL_MMA) return false;
+  return tc_supported(d, recon);
+}
+
+// One CTA per SM: pick the split count whose CTA count fills the last wave best, with >= 4 tiles each.
+int choose_splits_tc(const palu_decode_dims* d) {
+  if (d->splits > 0) return d->splits < palu::kMaxSplits ? d->splits : palu::kMaxSplits;
+  const long items = (long)d->batch * d->n_kv_heads;
+  const int tiles = (d->max_seq + palu::tc::kTile - 1) / palu::tc::kTile;
+  const long G = device_sms();
+  int best = 1;
+  double best_eff = -1.0;
+  for (int s = 1; s <= 64 && s <= tiles; ++s) {
+    if (s > 1 && tiles / s < 4) break;
+    const long units = items * s;
+    const double eff = (double)units / (double)(((units + G - 1) / G) * G);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return best;
+}
+
+int splits_for(const palu_decode_dims* d, bool recon) {
+  return use_tc(d, recon) ? choose_splits_tc(d) : choose_splits(d);
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+int encode(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const cuuint64_t* dims,
+           const cuuint64_t* strides, const cuuint32_t* box, const char* what,
+           CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(PALU_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(m, dt, (cuuint32_t)rank, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PALU_ERR_INVALID, "tensor map for %s rejected (CUresult %d)", what, (int)r);
+  return PALU_OK;
+}
+
+template <int KBK, int KBV>
+int launch_tc(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mt, const CUtensorMap& mu,
+              const palu::tc::TcParams& p, cudaStream_t stream) {
+  using Lay = palu::tc::Layout<KBK, KBV>;
+  auto kern = palu::tc::palu_decode_tc_kernel<KBK, KBV>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::TOTAL) != cudaSuccess)
+    return cuda_check("cudaFuncSetAttribute(decode tc)");
+  kern<<<dim3(p.splits, p.n_kv, p.batch), palu::tc::kThreads, Lay::TOTAL, stream>>>(mk, mv, mt, mu, p);
+  return cuda_check("decode tc kernel launch");
+}
+
+int run_tc(const void* q, const void* k, const void* v, const void* u_k, int64_t u_k_ld, const void* cs_pairs,
+           const int32_t* cur_pos, void* workspace, float* ws_o, float* ws_ml, const palu_decode_dims* d, int splits,
+           float scale, cudaStream_t stream) {
+  CUtensorMap mk, mv, mt, mu;
+  const cuuint64_t items = (cuuint64_t)d->batch * d->n_groups;
+  {
+    const cuuint64_t dims[3] = {(cuuint64_t)d->r_k, (cuuint64_t)d->max_seq, items};
+    const cuuint64_t str[2] = {(cuuint64_t)d->r_k * 2, (cuuint64_t)d->max_seq * d->r_k * 2};
+    const cuuint32_t box[3] = {64, 128, 1};
+    if (int st = encode(&mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, k, dims, str, box, "k_lat")) return st;
+  }
+  {
+    const cuuint64_t dims[3] = {(cuuint64_t)d->r_v, (cuuint64_t)d->max_seq, items};
+    const cuuint64_t str[2] = {(cuuint64_t)d->r_v * 2, (cuuint64_t)d->max_seq * d->r_v * 2};
+    const cuuint32_t box[3] = {64, 128, 1};
+    if (int st = encode(&mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, v, dims, str, box, "v_lat")) return st;
+  }
+  {
+    const cuuint64_t dims[2] = {64, (cuuint64_t)d->max_seq};
+    const cuuint64_t str[1] = {256};
+    const cuuint32_t box[2] = {16, 128};  // 16 frequency pairs (64 B) x 128 positions
+    if (int st = encode(&mt, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, cs_pairs, dims, str, box, "cs_tab",
+                        CU_TENSOR_MAP_SWIZZLE_64B))
+      return st;
+  }
+  {
+    const cuuint64_t dims[2] = {128, (cuuint64_t)d->n_kv_heads * d->r_k};
+    const cuuint64_t str[1] = {(cuuint64_t)u_k_ld * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)d->r_k};
+    if (int st = encode(&mu, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, u_k, dims, str, box, "w_rot")) return st;
+  }
+  palu::tc::TcParams p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.cur_pos = cur_pos;
+  p.ws_o = ws_o;
+  p.ws_ml = ws_ml;
+  p.status = static_cast<int*>(workspace);
+  p.batch = d->batch;
+  p.n_q = d->n_q_heads;
+  p.n_kv = d->n_kv_heads;
+  p.n_groups = d->n_groups;
+  p.rk = d->r_k;
+  p.rv = d->r_v;
+  p.max_seq = d->max_seq;
+  p.splits = splits;
+  p.rep = rep_of(d);
+  p.scale_log2 = scale * palu::kLog2e;
+  const int kbk = d->r_k > 64 ? 2 : 1, kbv = d->r_v > 64 ? 2 : 1;
+  if (kbk == 1 && kbv == 1) return launch_tc<1, 1>(mk, mv, mt, mu, p, stream);
+  if (kbk == 1 && kbv == 2) return launch_tc<1, 2>(mk, mv, mt, mu, p, stream);
+  if (kbk == 2 && kbv == 1) return launch_tc<2, 1>(mk, mv, mt, mu, p, stream);
+  return launch_tc<2, 2>(mk, mv, mt, mu, p, stream);
 }
 
 template <int RV16, bool RECON>
@@ -138,12 +276,16 @@ int run_decode(bool recon, const void* q, const void* k, const void* v, const vo
   if (recon && (u_k_ld < 128 || u_k_ld % 8 != 0))
     return fail(PALU_ERR_INVALID, "w_rot/u_k row length %lld must be >= 128 and a multiple of 8", (long long)u_k_ld);
   if (out_dtype != PALU_BF16 && out_dtype != PALU_F32) return fail(PALU_ERR_INVALID, "out_dtype must be bf16 or f32");
-  const int splits = choose_splits(d);
+  const bool tc = use_tc(d, recon);
+  const int splits = tc ? choose_splits_tc(d) : choose_splits(d);
   if (!workspace || workspace_bytes < ws_bytes(d, splits))
     return fail(PALU_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu bytes needed", workspace_bytes,
                 ws_bytes(d, splits));
-  float* ws_o = static_cast<float*>(workspace);
-  float* ws_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + (ws_floats_o(d, splits) * 4 + 255) / 256 * 256);
+  if (tc && reinterpret_cast<uintptr_t>(cs_pairs) % 16 != 0)
+    return fail(PALU_ERR_INVALID, "cs_tab (packed) must be 16-byte aligned");
+  float* ws_o = reinterpret_cast<float*>(static_cast<char*>(workspace) + kWsHeader);
+  float* ws_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + kWsHeader +
+                                          (ws_floats_o(d, splits) * 4 + 255) / 256 * 256);
 
   palu::DecodeParams p;
   p.q = static_cast<const __nv_bfloat16*>(q);
@@ -165,7 +307,10 @@ int run_decode(bool recon, const void* q, const void* k, const void* v, const vo
   p.ld_u = (int)u_k_ld;
   p.rep = rep_of(d);
   p.scale_log2 = scale * palu::kLog2e;
-  st = recon ? dispatch_rv<true>(p, stream) : dispatch_rv<false>(p, stream);
+  if (tc)
+    st = run_tc(q, k, v, u_k, u_k_ld, cs_pairs, cur_pos, workspace, ws_o, ws_ml, d, splits, scale, stream);
+  else
+    st = recon ? dispatch_rv<true>(p, stream) : dispatch_rv<false>(p, stream);
   if (st) return st;
 
   palu::CombineParams c;
@@ -194,13 +339,38 @@ const char* palu_last_error(void) { return g_err.c_str(); }
 const char* palu_version(void) { return "palu_b200 0.1.0 (sm_100a)"; }
 
 int32_t palu_choose_splits(const palu_decode_dims* dims) {
-  if (!dims) return 0;
-  return choose_splits(dims);
+  if (!dims || dims->n_kv_heads <= 0 || dims->n_q_heads <= 0) return 0;
+  return splits_for(dims, true);
 }
 
 size_t palu_workspace_bytes(const palu_decode_dims* dims) {
   if (!dims || dims->n_kv_heads <= 0 || dims->n_q_heads <= 0) return 0;
-  return ws_bytes(dims, choose_splits(dims));
+  const int a = choose_splits(dims), b = choose_splits_tc(dims);
+  return ws_bytes(dims, a > b ? a : b);
+}
+
+int palu_set_kernel(int32_t which) {
+  g_err.clear();
+  if (which != PALU_KERNEL_AUTO && which != PALU_KERNEL_MMA && which != PALU_KERNEL_TC)
+    return fail(PALU_ERR_INVALID, "kernel choice must be PALU_KERNEL_AUTO, _MMA or _TC");
+  g_kernel_choice = which;
+  return PALU_OK;
+}
+
+int32_t palu_kernel_for(const palu_decode_dims* dims) {
+  if (!dims) return -1;
+  return use_tc(dims, true) ? PALU_KERNEL_TC : PALU_KERNEL_MMA;
+}
+
+int palu_read_status(void* workspace, int32_t* status, palu_stream_t stream) {
+  g_err.clear();
+  if (!workspace || !status) return fail(PALU_ERR_INVALID, "workspace and status must be set");
+  if (cudaMemcpyAsync(status, workspace, sizeof(int32_t), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+      cudaStreamSynchronize(stream) != cudaSuccess)
+    return cuda_check("reading the status word");
+  if (*status != 0 && cudaMemsetAsync(workspace, 0, sizeof(int32_t), stream) != cudaSuccess)
+    return cuda_check("clearing the status word");
+  return PALU_OK;
 }
 
 int palu_decode_attn(const void* q, const void* k_lat, const void* v_lat, const void* u_k, int64_t u_k_ld,

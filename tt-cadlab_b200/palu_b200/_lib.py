@@ -19,7 +19,9 @@ PALU_BF16, PALU_F32 = 0, 1
 
 # Every symbol include/palu_b200.h declares (checked by the CPU test suite).
 EXPORTED = ("palu_decode_attn", "palu_workspace_bytes", "palu_choose_splits", "palu_append_latents",
-            "palu_plain_gqa_decode", "palu_pack_cs_table", "palu_last_error", "palu_version")
+            "palu_plain_gqa_decode", "palu_pack_cs_table", "palu_set_kernel", "palu_kernel_for", "palu_read_status",
+            "palu_last_error", "palu_version")
+PALU_KERNEL_AUTO, PALU_KERNEL_MMA, PALU_KERNEL_TC = 0, 1, 2
 
 
 class DecodeDims(ctypes.Structure):
@@ -53,6 +55,12 @@ def load() -> ctypes.CDLL:
     lib.palu_append_latents.restype = ctypes.c_int
     lib.palu_pack_cs_table.argtypes = [vp, i64, i32, vp, i32, vp]
     lib.palu_pack_cs_table.restype = ctypes.c_int
+    lib.palu_set_kernel.argtypes = [i32]
+    lib.palu_set_kernel.restype = ctypes.c_int
+    lib.palu_kernel_for.argtypes = [dims_p]
+    lib.palu_kernel_for.restype = i32
+    lib.palu_read_status.argtypes = [vp, ctypes.POINTER(i32), vp]
+    lib.palu_read_status.restype = ctypes.c_int
     lib.palu_last_error.argtypes = []
     lib.palu_last_error.restype = ctypes.c_char_p
     lib.palu_version.argtypes = []
@@ -92,8 +100,29 @@ def workspace_bytes(d: DecodeDims) -> int:
     return int(load().palu_workspace_bytes(ctypes.byref(d)))
 
 
+def new_workspace(d: DecodeDims, device) -> torch.Tensor:
+    """A zeroed workspace for calls with these dims (the status word at its start must start at 0)."""
+    return torch.zeros(workspace_bytes(d), dtype=torch.uint8, device=device)
+
+
 def choose_splits(d: DecodeDims) -> int:
     return int(load().palu_choose_splits(ctypes.byref(d)))
+
+
+def set_kernel(which: int) -> None:
+    """Choose the decode kernel family (PALU_KERNEL_AUTO / _MMA / _TC) for this process."""
+    check(load().palu_set_kernel(int(which)))
+
+
+def kernel_for(d: DecodeDims) -> int:
+    return int(load().palu_kernel_for(ctypes.byref(d)))
+
+
+def read_status(workspace: torch.Tensor) -> int:
+    """The status word a decode call left in ``workspace`` (0 = ok); reading clears it."""
+    st = ctypes.c_int32(0)
+    check(load().palu_read_status(workspace.data_ptr(), ctypes.byref(st), stream_handle(workspace.device)))
+    return int(st.value)
 
 
 def env_splits() -> int:

@@ -157,6 +157,31 @@ def _grid_cores(program_config) -> Optional[int]:
     return int(gx) * int(gy)
 
 
+_WS_CACHE: dict = {}
+
+
+def _workspace_for(d, device) -> torch.Tensor:
+    """A zeroed workspace, cached per (device, size) so that repeated calls reuse it; calls that overlap on
+    different streams must pass their own ``workspace``."""
+    need = _lib.workspace_bytes(d)
+    key = (device.index if device.index is not None else torch.cuda.current_device(), need)
+    ws = _WS_CACHE.get(key)
+    if ws is None:
+        if len(_WS_CACHE) > 8:
+            _WS_CACHE.clear()
+        ws = _WS_CACHE[key] = _lib.new_workspace(d, device)
+    return ws
+
+
+def workspace_status() -> int:
+    """Read and clear the status words of the cached workspaces: 0 when no bounded device wait expired
+    in any call since the last read (a nonzero value marks that call's output as invalid)."""
+    st = 0
+    for ws in list(_WS_CACHE.values()):
+        st = max(st, _lib.read_status(ws))
+    return st
+
+
 def decode(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, *, u_k_ld=HEAD_DIM, u_v=None, scale=None,
            out=None, out_dtype=torch.bfloat16, splits=0, workspace=None) -> torch.Tensor:
     """Low-level entry (no reference-surface validation): the arrays are already in the library's layout.
@@ -173,9 +198,8 @@ def decode(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, *, u_k_ld=HEAD_DIM, u_
     width = HEAD_DIM if u_v is not None else r_v
     if out is None:
         out = torch.empty(B, nh, width, dtype=out_dtype, device=q.device)
-    need = _lib.workspace_bytes(d)
-    if workspace is None or workspace.numel() < need:
-        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    if workspace is None or workspace.numel() < _lib.workspace_bytes(d):
+        workspace = _workspace_for(d, q.device)
     odt = _lib.PALU_F32 if out.dtype == torch.float32 else _lib.PALU_BF16
     sc = HEAD_DIM ** -0.5 if scale is None else float(scale)
     _lib.check(_lib.load().palu_decode_attn(
@@ -269,7 +293,7 @@ def plain_gqa_decode(q, k, v, cur_pos, *, scale=None, out_dtype=torch.bfloat16, 
     n_kv, S, d_v = k.shape[1], k.shape[2], v.shape[3]
     d = _lib.dims(B, nh, n_kv, n_kv, HEAD_DIM, d_v, S, splits or _lib.env_splits())
     out = torch.empty(B, nh, d_v, dtype=out_dtype, device=q.device)
-    ws = torch.empty(_lib.workspace_bytes(d), dtype=torch.uint8, device=q.device)
+    ws = _workspace_for(d, q.device)
     odt = _lib.PALU_F32 if out_dtype == torch.float32 else _lib.PALU_BF16
     sc = HEAD_DIM ** -0.5 if scale is None else float(scale)
     qb, kb, vb = _bf16(q[0]), _bf16(k), _bf16(v)
