@@ -506,44 +506,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (i < n_mine) {
         if (!mbar_wait(bar(B_REC + g), i & 1, s_abort, p.status)) break;
         fence_after();
-        // 8 half-chunks of 16 D_k columns (8 frequency pairs). The next half-chunk's TMEM load is issued
-        // right after the current one landed (tcgen05.wait::ld waits for every load in flight), so it
-        // overlaps this half-chunk's table reads and arithmetic.
+        // 4 chunks of 32 D_k columns (16 frequency pairs, one table chunk). Each TMEM load is waited for
+        // before any of its registers is touched: an inline-asm tcgen05.ld must not stay in flight across
+        // code the compiler may reschedule.
         bool ok = true;
-        uint32_t kbuf[2][16];
-        tmem_ld16(trow + kColDk, kbuf[0]);
-        tmem_wait_ld();
-#pragma unroll
-        for (int h = 0; h < 8; ++h) {
-          const int ch = h >> 1, n = i * 4 + ch, sb = g * T_SLOTS + n % T_SLOTS;
-          if (h + 1 < 8) tmem_ld16(trow + kColDk + 16 * (h + 1), kbuf[(h + 1) & 1]);
-          if ((h & 1) == 0 && !mbar_wait(bar(B_TF + sb), (n / T_SLOTS) & 1, s_abort, p.status)) {
+#pragma unroll 1
+        for (int ch = 0; ch < 4; ++ch) {
+          const int n = i * 4 + ch, sb = g * T_SLOTS + n % T_SLOTS;
+          if (!mbar_wait(bar(B_TF + sb), (n / T_SLOTS) & 1, s_abort, p.status)) {
             ok = false;
             break;
           }
           // SWIZZLE_64B rows of 64 B: 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3).
           const unsigned char* tb = smem + Lay::OFF_TAB + sb * Lay::TCH_BYTES + row * 64;
-          uint32_t cs[8];
+          uint32_t cs[16];
 #pragma unroll
-          for (int c2 = 0; c2 < 2; ++c2) {
-            const uint4 w = *reinterpret_cast<const uint4*>(tb + (((2 * (h & 1) + c2) ^ ((row >> 1) & 3)) << 4));
-            cs[4 * c2 + 0] = w.x;
-            cs[4 * c2 + 1] = w.y;
-            cs[4 * c2 + 2] = w.z;
-            cs[4 * c2 + 3] = w.w;
+          for (int c4 = 0; c4 < 4; ++c4) {
+            const uint4 w = *reinterpret_cast<const uint4*>(tb + ((c4 ^ ((row >> 1) & 3)) << 4));
+            cs[4 * c4 + 0] = w.x;
+            cs[4 * c4 + 1] = w.y;
+            cs[4 * c4 + 2] = w.z;
+            cs[4 * c4 + 3] = w.w;
           }
-          uint32_t out[8];
+          uint32_t kr[32];
+          tmem_ld32(trow + kColDk + 32 * ch, kr);
+          tmem_wait_ld();
+          uint32_t out[16];
 #pragma unroll
-          for (int pp = 0; pp < 8; ++pp) {
+          for (int pp = 0; pp < 16; ++pp) {
             const float c = __uint_as_float(cs[pp] << 16), sn = __uint_as_float(cs[pp] & 0xFFFF0000u);
-            const float k0 = __uint_as_float(kbuf[h & 1][2 * pp]), k1 = __uint_as_float(kbuf[h & 1][2 * pp + 1]);
+            const float k0 = __uint_as_float(kr[2 * pp]), k1 = __uint_as_float(kr[2 * pp + 1]);
             out[pp] = pack_half2(k0 * c - k1 * sn, k1 * c + k0 * sn);
           }
-          if (h & 1) {  // both halves of this table chunk consumed by every lane: its slot may refill
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(B_TE + sb));
-          }
-          if (h == 0 && i >= 1) {
+          __syncwarp();  // every lane has consumed its table values: the slot may refill
+          if (lane == 0) mbar_arrive(bar(B_TE + sb));
+          if (ch == 0 && i >= 1) {
             // A still feeds QK(t - 2) until that MMA completes; its commit is the scores barrier.
             const int jq = i - 1;
             if (!mbar_wait(bar(B_SF + 2 * g + (jq & 1)), (jq >> 1) & 1, s_abort, p.status)) {
@@ -552,13 +549,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             fence_after();
           }
-          tmem_st8(trow + kColA + 8 * h, out);
-          if (h + 1 < 8) tmem_wait_ld();
+          tmem_st16(trow + kColA + 16 * ch, out);
         }
-        if (!ok) {
-          tmem_wait_ld();  // no TMEM load may still be landing in registers
-          break;
-        }
+        if (!ok) break;
         tmem_wait_st();
         fence_before();
         __syncwarp();
