@@ -87,6 +87,21 @@ int palu_decode_attn(const void* q, const void* k_lat, const void* v_lat, const 
                      void* workspace, size_t workspace_bytes, const palu_decode_dims* dims, float scale,
                      palu_stream_t stream);
 
+/*
+ * palu_decode_attn without a caller workspace: allocates nothing. No reference counterpart (the Tensix
+ * op sizes its own circular buffers); for callers that cannot hand over device memory.
+ * Arguments and results as palu_decode_attn. The split-K partials and status word live in a static
+ * 8 MiB device array, one per device: shapes whose palu_workspace_bytes() exceeds 8 MiB are rejected
+ * with PALU_ERR_WORKSPACE. Calls that overlap in time on one device (other streams, other host
+ * threads) race on that array; calls in one stream are ordered and safe. The first call on each
+ * device sets the array up with synchronous CUDA calls, so make it before any stream capture.
+ * A bounded device wait that expires is recorded in the array's status word, which this entry point
+ * does not report; use palu_decode_attn + palu_read_status where that report is needed.
+ */
+int palu_decode_attn_static(const void* q, const void* k_lat, const void* v_lat, const void* u_k, int64_t u_k_ld,
+                            const void* u_v, const void* cs_pairs, const int32_t* cur_pos, void* out,
+                            int32_t out_dtype, const palu_decode_dims* dims, float scale, palu_stream_t stream);
+
 /* Device bytes palu_decode_attn / palu_plain_gqa_decode need for their split-K partials. */
 size_t palu_workspace_bytes(const palu_decode_dims* dims);
 

@@ -6,6 +6,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "../../include/palu_b200.h"
@@ -330,6 +331,42 @@ int run_decode(bool recon, const void* q, const void* k, const void* v, const vo
   return cuda_check("combine kernel launch");
 }
 
+// ---- static-scratch variant (palu_decode_attn_static) ----------------------------------------------
+
+// The split-K partials and status word of palu_decode_attn_static live in this module-global array, one
+// copy per device, so that entry point allocates nothing. 8 MiB holds every call whose
+// palu_workspace_bytes() fits it, e.g. B = 32, 8 KV heads, 4 query heads each, r_v = 64 at up to
+// 28 splits. All calls on one device share it: calls that overlap in time (other streams, other
+// host threads) race on it.
+constexpr size_t kStaticScratchBytes = size_t(8) << 20;
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+void* g_static_ptr[kMaxDevices] = {nullptr};
+
+// Per-device setup, once: resolve the array's address on the current device and zero its status word.
+// Runs synchronous CUDA calls, so the first call on a device must come before any stream capture.
+int static_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(PALU_ERR_CUDA, "palu_decode_attn_static: no current device");
+  if (dev < 0 || dev >= kMaxDevices) return fail(PALU_ERR_CUDA, "palu_decode_attn_static: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(PALU_ERR_CUDA, "palu_decode_attn_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    e = cudaMemset(p, 0, sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess)
+      return fail(PALU_ERR_CUDA, "palu_decode_attn_static: clearing the status word: %s", cudaGetErrorString(e));
+    g_static_ptr[dev] = p;
+  }
+  *out = g_static_ptr[dev];
+  return PALU_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -380,6 +417,23 @@ int palu_decode_attn(const void* q, const void* k_lat, const void* v_lat, const 
   g_err.clear();
   return run_decode(true, q, k_lat, v_lat, u_k, u_k_ld, u_v, cs_pairs, cur_pos, out, out_dtype, workspace,
                     workspace_bytes, dims, scale, stream);
+}
+
+int palu_decode_attn_static(const void* q, const void* k_lat, const void* v_lat, const void* u_k, int64_t u_k_ld,
+                            const void* u_v, const void* cs_pairs, const int32_t* cur_pos, void* out,
+                            int32_t out_dtype, const palu_decode_dims* dims, float scale, palu_stream_t stream) {
+  g_err.clear();
+  int st = validate(dims, true, u_v != nullptr);
+  if (st) return st;
+  const size_t need = ws_bytes(dims, splits_for(dims, true));
+  if (need > kStaticScratchBytes)
+    return fail(PALU_ERR_WORKSPACE, "palu_decode_attn_static: these shapes need %zu bytes of scratch, more than the "
+                "%zu-byte static scratch; use palu_decode_attn with a caller workspace", need, kStaticScratchBytes);
+  void* scratch = nullptr;
+  st = static_scratch(&scratch);
+  if (st) return st;
+  return run_decode(true, q, k_lat, v_lat, u_k, u_k_ld, u_v, cs_pairs, cur_pos, out, out_dtype, scratch,
+                    kStaticScratchBytes, dims, scale, stream);
 }
 
 int palu_plain_gqa_decode(const void* q, const void* k, const void* v, const int32_t* cur_pos, void* out,

@@ -18,7 +18,7 @@ PALU_OK, PALU_ERR_INVALID, PALU_ERR_WORKSPACE, PALU_ERR_CUDA = 0, 1, 2, 3
 PALU_BF16, PALU_F32 = 0, 1
 
 # Every symbol include/palu_b200.h declares (checked by the CPU test suite).
-EXPORTED = ("palu_decode_attn", "palu_workspace_bytes", "palu_choose_splits", "palu_append_latents",
+EXPORTED = ("palu_decode_attn", "palu_decode_attn_static", "palu_workspace_bytes", "palu_choose_splits", "palu_append_latents",
             "palu_plain_gqa_decode", "palu_pack_cs_table", "palu_set_kernel", "palu_kernel_for", "palu_read_status",
             "palu_last_error", "palu_version")
 PALU_KERNEL_AUTO, PALU_KERNEL_MMA, PALU_KERNEL_TC = 0, 1, 2
@@ -45,6 +45,8 @@ def load() -> ctypes.CDLL:
     dims_p = ctypes.POINTER(DecodeDims)
     lib.palu_decode_attn.argtypes = [vp, vp, vp, vp, i64, vp, vp, vp, vp, i32, vp, sz, dims_p, f32, vp]
     lib.palu_decode_attn.restype = ctypes.c_int
+    lib.palu_decode_attn_static.argtypes = [vp, vp, vp, vp, i64, vp, vp, vp, vp, i32, dims_p, f32, vp]
+    lib.palu_decode_attn_static.restype = ctypes.c_int
     lib.palu_plain_gqa_decode.argtypes = [vp, vp, vp, vp, vp, i32, vp, sz, dims_p, f32, vp]
     lib.palu_plain_gqa_decode.restype = ctypes.c_int
     lib.palu_workspace_bytes.argtypes = [dims_p]
