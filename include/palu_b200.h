@@ -70,8 +70,7 @@ typedef struct palu_decode_dims {
  *            (interleaved-pair) order. u_k_ld = 128 for u_k itself, 256 for w_rot = [u_k | u_k T].
  *   u_v      NULL: absorbed V (M-LRD) -- the output is the attention-weighted V latent, r_v wide;
  *            else [n_kv_heads][r_v][128] bf16 -- V rebuilt per head (G-LRD), the output is 128 wide.
- *   cs_pairs [>= max_seq][64] packed rows from palu_pack_cs_table: (cos, sin) of frequency j at
- *            position s as a bf16 pair (cos in the low half)
+ *   cs_pairs [>= max_seq][64] 32-bit words: packed rows from palu_pack_cs_table (16-byte aligned)
  *   cur_pos  [B] int32: last visible position of each row (inclusive); < 0 skips the row (zeros out)
  *   out      [B][n_q_heads][r_v or 128], out_dtype PALU_BF16 or PALU_F32
  *   workspace / workspace_bytes: >= palu_workspace_bytes(dims) bytes of device memory; its first 4
@@ -127,7 +126,8 @@ int palu_plain_gqa_decode(const void* q, const void* k, const void* v, const int
 
 /*
  * Pack the reference's [rows][ld] [cos | sin] table (bf16 or fp32, pair-duplicated frequency
- * columns: cos_j at column 2j, sin_j at 128 + 2j) into [rows][64] bf16 (cos, sin) pairs.
+ * columns: cos_j at column 2j, sin_j at 128 + 2j) into rows of 128 bf16 (= 64 32-bit words): 4 blocks
+ * of 16 frequencies, each block the 16 cosines (frequency order) followed by the same 16 sines.
  */
 int palu_pack_cs_table(const void* cs_tab, int64_t ld, int32_t in_dtype, void* cs_pairs, int32_t rows,
                        palu_stream_t stream);

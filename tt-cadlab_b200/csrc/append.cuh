@@ -2,8 +2,10 @@
 //  * palu_append_kernel: write one decode step's latents into the caches at cur_pos[b]
 //    (the reference's paged_update_cache calls, attention.py:612-625);
 //  * palu_pack_cs_kernel: turn the reference's [S, 256] [cos | sin] table (pair-duplicated,
-//    Meta-interleaved, fused.py:62-73) into the packed [S, 64] (cos, sin) bf16x2 rows the decode
-//    kernels read (half the bytes, one 4-byte load per frequency pair).
+//    Meta-interleaved, fused.py:62-73) into the packed 256-byte rows the decode kernels read (half the
+//    bytes): per row, 4 blocks of 16 frequencies, each block 16 bf16 cosines then their 16 sines. One
+//    block is one 64-byte TMA row segment, and consecutive frequencies sit side by side so that the
+//    rotation runs on two frequencies per packed fp32x2 instruction.
 #pragma once
 #include "palu_common.cuh"
 
@@ -39,23 +41,26 @@ __global__ void palu_append_kernel(const AppendParams p) {
 }
 
 // cs_tab row s: cos at columns 2j (== 2j+1), sin at 128 + 2j. in_f32 selects an fp32 table
-// (rounded to bf16 here) instead of bf16.
+// (rounded to bf16 here) instead of bf16. Output word w of row s (w = 16 blk + x):
+// x < 8: (cos f0, cos f0+1), x >= 8: (sin f1, sin f1+1), f0 = 16 blk + 2x, f1 = f0 - 16 (low half first).
 __global__ void palu_pack_cs_kernel(const void* cs_tab, long ld, int in_f32, uint32_t* out, int rows) {
   const long total = (long)rows * 64;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
     const long s = i >> 6;
-    const int j = (int)(i & 63);
-    float c, sn;
+    const int w = (int)(i & 63), x = w & 15;
+    const int f = (w & ~15) + 2 * (x & 7);       // first of the word's two frequencies
+    const int col = (x < 8 ? 0 : kHeadDim) + 2 * f;  // cos_f at 2f, sin_f at 128 + 2f
+    float a, bv;
     if (in_f32) {
       const float* r = reinterpret_cast<const float*>(cs_tab) + s * ld;
-      c = r[2 * j];
-      sn = r[kHeadDim + 2 * j];
+      a = r[col];
+      bv = r[col + 2];
     } else {
       const __nv_bfloat16* r = reinterpret_cast<const __nv_bfloat16*>(cs_tab) + s * ld;
-      c = __bfloat162float(r[2 * j]);
-      sn = __bfloat162float(r[kHeadDim + 2 * j]);
+      a = __bfloat162float(r[col]);
+      bv = __bfloat162float(r[col + 2]);
     }
-    out[i] = pack_bf16(c, sn);
+    out[i] = pack_bf16(a, bv);
   }
 }
 

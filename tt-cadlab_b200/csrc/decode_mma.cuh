@@ -27,7 +27,7 @@ struct DecodeParams {
   const __nv_bfloat16* k;   // RECON: [B][n_groups][max_seq][rk]; plain: [B][n_kv][max_seq][128] (rotated)
   const __nv_bfloat16* v;   // [B][n_groups][max_seq][rv]
   const __nv_bfloat16* u_k; // [n_kv][rk] rows of ld_u elements (first 128 used); RECON only
-  const uint32_t* cs;       // [max_seq][64] packed bf16x2 (cos lo, sin hi); RECON only
+  const uint32_t* cs;       // [max_seq][64] words: packed table rows (append.cuh); RECON only
   const int32_t* cur_pos;   // [B]
   float* ws_o;              // [B][n_kv][splits][rep][rv]
   float* ws_ml;             // [B][n_kv][splits][rep][2]  (m in log2 units, l)
@@ -171,12 +171,13 @@ __global__ void __launch_bounds__(kMmaThreads, 2) palu_decode_mma_kernel(const D
       }
       // RoPE: K_rot[2j] = K[2j] cos - K[2j+1] sin ; K_rot[2j+1] = K[2j+1] cos + K[2j] sin.
       const uint32_t* sT = reinterpret_cast<const uint32_t*>(st + lay.k_bytes() + MmaSmem<RV16, RECON>::v_bytes);
-      const uint32_t* t0 = sT + (warp * 16 + g) * kCsLd + t;
-      const uint32_t* t1 = t0 + 8 * kCsLd;
+      const __nv_bfloat16* t0 = reinterpret_cast<const __nv_bfloat16*>(sT + (warp * 16 + g) * kCsLd);
+      const __nv_bfloat16* t1 = t0 + 16 * kCsLd;
 #pragma unroll
       for (int n = 0; n < 16; ++n) {
-        const float2 c0 = unpack_bf16(t0[4 * n]);
-        const float2 c1 = unpack_bf16(t1[4 * n]);
+        const int f = 4 * n + t;  // frequency pair of this thread's two accumulator columns
+        const float2 c0 = make_float2(__bfloat162float(t0[packed_cos_index(f)]), __bfloat162float(t0[packed_sin_index(f)]));
+        const float2 c1 = make_float2(__bfloat162float(t1[packed_cos_index(f)]), __bfloat162float(t1[packed_sin_index(f)]));
         const float k0 = acc[n][0], k1 = acc[n][1], k2 = acc[n][2], k3 = acc[n][3];
         acc[n][0] = k0 * c0.x - k1 * c0.y;
         acc[n][1] = k1 * c0.x + k0 * c0.y;

@@ -2,22 +2,26 @@
 //
 // One CTA owns (batch row b, KV head h, split s): a contiguous range of 128-token tiles of the positions
 // 0..cur_pos[b]. Its 16 warps form two halves; half g serves the tiles t with t % 2 == g:
-//   warp 8g+0   TMA producer: K-latent tiles of half g (half 0 also loads U_k once)
+//   warp 8g+0   TMA producer: K-latent tiles of half g
 //   warp 8g+1   the thread issuing half g's tcgen05.mma and commits (warp 1 also allocates TMEM)
-//   warp 8g+2   TMA producer: packed (cos, sin) table chunks (16 frequency pairs x 128 rows each)
+//   warp 8g+2   TMA producer: packed table chunks (16 frequencies x 128 rows: 16 cos then 16 sin per row)
 //   warp 8g+3   TMA producer: V-latent tiles (V lives longest, until PV)
 //   warps 8g+4 .. 8g+7   softmax group g: one thread per token row of the tile
+// At start the 8 softmax warps stage Q^T (fp16) and U_k (bf16) in shared memory with their head dims
+// reordered as [even dims | odd dims], so that D_k holds each rotation pair (2f, 2f+1) in columns f and
+// 64 + f and the rotation of two adjacent frequencies is one packed fp32x2 operation.
 // Per tile t (group g = t % 2; thread = token row inside the tile):
 //   MMA    D_k[128 tok x 128 dim] (f32) = lat_k (smem, K-major) x U_k (smem, MN-major)
 //   group  K row -> RoPE in registers from the table -> K_rot as fp16 into its own TMEM columns: the A
 //          operand of the next MMA (fp16 keeps 11 significant bits; q is bf16, exact in fp16)
-//   MMA    D_s[128 tok x 16] (f32) = K_rot (TMEM) x Q^T (smem, fp16)
+//   MMA    D_s[128 tok x 16] (f32) = K_rot (TMEM, fp16) x Q^T (smem, fp16)
 //   group  online softmax over the query heads (exp2 domain); P^T as bf16 hi + lo -> smem
 //   MMA    D_o[128 lat x 16] (f32) = V^T (smem, MN-major: the V tile exactly as TMA wrote it) x P^T
 //   group  thread c (latent dim c) accumulates O[h][c] = O * alpha + hi + lo in registers
 // Software pipeline: in its iteration for tile t a group does RoPE(t), softmax(t-2), accumulate(t-4), so
 // each wait is for an MMA issued two tiles earlier; the MMA thread issues QK(t), reconstruct(t+2),
-// PV(t-2). Every ring, barrier and TMEM region is private to one half, each role thread blocks (sleeping
+// PV(t-2). A single thread issues at most one tcgen05.mma per ~64 cycles whatever its shape (measured
+// on B200), so the per-tile MMA count (r_k/16 + 8 + 8) matters as much as their arithmetic. Every ring, barrier and TMEM region is private to one half, each role thread blocks (sleeping
 // in mbarrier try_wait) on one barrier at a time, and no barrier can run two phases ahead of its waiter,
 // so parity waits never alias. The two groups merge their
 // (m, l, O) at the end into one split partial (combine.cuh merges the splits). Every wait is bounded (1 s of globaltimer): on expiry the CTA records a status code,
@@ -36,7 +40,7 @@ constexpr int kTile = 128;
 constexpr int kBox = 16384;             // one TMA box: 128 rows x 128 B
 constexpr int kTmemCols = 512;
 constexpr int kGrpCols = 256;           // TMEM columns reserved per softmax group
-constexpr int kColDk = 0;               // 128 columns: f32 K tile (reconstruct output)
+constexpr int kColDk = 0;               // 128 columns: f32 K tile, dims [even | odd] (reconstruct output)
 constexpr int kColA = 128;              // 64 columns: fp16 K_rot, the A operand of QK (packed 2 per column)
 constexpr int kColDs = 192;             // 2 x 16 columns: scores, double-buffered
 constexpr int kColDo = 224;             // 2 x 16 columns: PV result, double-buffered
@@ -47,11 +51,12 @@ enum : int { kStatusOk = 0, kStatusTimeout = 1 };
 
 struct TcParams {
   const __nv_bfloat16* q;   // [B][n_q][128]
+  const __nv_bfloat16* u_k; // [n_kv][r_k] rows of ld_u elements (U_k in the first 128)
   const int32_t* cur_pos;   // [B]
   float* ws_o;              // [B][n_kv][splits][rep][rv]
   float* ws_ml;             // [B][n_kv][splits][rep][2]
   int* status;              // device status word, 0 = ok
-  int batch, n_q, n_kv, n_groups, rk, rv, max_seq, splits, rep;
+  int batch, n_q, n_kv, n_groups, rk, rv, max_seq, splits, rep, ld_u;
   float scale_log2;
 };
 
@@ -258,8 +263,7 @@ PALU_DEVINL uint32_t sw128_offset(int row, int k, int rows) {
 template <int KBK, int KBV>
 __global__ void __launch_bounds__(kThreads, 1)
     palu_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                          const __grid_constant__ CUtensorMap tm_tab, const __grid_constant__ CUtensorMap tm_u,
-                          const TcParams p) {
+                          const __grid_constant__ CUtensorMap tm_tab, const TcParams p) {
   using Lay = Layout<KBK, KBV>;
   constexpr int NS_K = Lay::NS_K, NS_V = Lay::NS_V, T_SLOTS = Lay::T_SLOTS;
   constexpr int NS_T = 2 * T_SLOTS;  // table chunk slots, [group][slot]
@@ -305,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(B_TF + s), 1);
       mbar_init(bar(B_TE + s), 4);
     }
-    mbar_init(bar(B_UF), 1);
+    mbar_init(bar(B_UF), 8);  // the 8 softmax warps stage U_k
     for (int g = 0; g < 2; ++g) {
       mbar_init(bar(B_REC + g), 1);
       mbar_init(bar(B_AF + g), 4);
@@ -332,24 +336,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if ((warp & 7) >= 4) {
     const int t = ((warp >> 3) * 4 + (warp & 3)) * 32 + lane;  // 0..255 over the 8 softmax warps
-    // Q^T operand, fp16, K-major SWIZZLE_128B: 16 rows (this KV head's query heads, zero padded) x 128 dims.
+    // Q^T operand, fp16, K-major SWIZZLE_128B: 16 rows (this KV head's query heads, zero padded) x 128
+    // dims in [even | odd] order: K-block 0 = even dims, K-block 1 = odd dims (64 fp16 per 128-B row).
+    // Thread: (row, 16-byte chunk of 8 reordered dims); bf16 q is exact in fp16.
     {
-      const int row = t >> 4, chunk = t & 15;  // 8 dims per 16-byte chunk
-      uint4 w = make_uint4(0, 0, 0, 0);
+      const int row = t >> 4, chunk = t & 15;
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
       if (row < p.rep) {
-        const uint4 src = *reinterpret_cast<const uint4*>(p.q + ((size_t)b * p.n_q + kvh * p.rep + row) * kHeadDim +
-                                                          chunk * 8);
-        const uint32_t in[4] = {src.x, src.y, src.z, src.w};
-        uint32_t outw[4];
+        const uint4* qr = reinterpret_cast<const uint4*>(p.q + ((size_t)b * p.n_q + kvh * p.rep + row) * kHeadDim +
+                                                         16 * (chunk & 7));
+        const uint4 x0 = qr[0], x1 = qr[1];  // source dims 16 (chunk & 7) .. + 15
+        const uint32_t sel = chunk < 8 ? 0x5410u : 0x7632u;  // even (low) or odd (high) halves
+        const uint32_t bw[4] = {__byte_perm(x0.x, x0.y, sel), __byte_perm(x0.z, x0.w, sel),
+                                __byte_perm(x1.x, x1.y, sel), __byte_perm(x1.z, x1.w, sel)};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const float2 f = unpack_bf16(in[i]);
-          outw[i] = pack_half2(f.x, f.y);
+          const float2 f = unpack_bf16(bw[i]);
+          w[i] = pack_half2(f.x, f.y);
         }
-        w = make_uint4(outw[0], outw[1], outw[2], outw[3]);
       }
       const uint32_t off = (chunk >> 3) * 2048 + row * 128 + (((chunk & 7) ^ (row & 7)) << 4);
-      *reinterpret_cast<uint4*>(smem + Lay::OFF_Q + off) = w;
+      *reinterpret_cast<uint4*>(smem + Lay::OFF_Q + off) = make_uint4(w[0], w[1], w[2], w[3]);
     }
     for (int e = t; e < 4 * Lay::P_BYTES / 16; e += 256)
       reinterpret_cast<uint4*>(smem + Lay::OFF_P)[e] = make_uint4(0, 0, 0, 0);
@@ -368,12 +375,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && nt > g) {
       if (role == 0) {
         tma_prefetch_map(&tm_k);
-        if (g == 0) {
-          tma_prefetch_map(&tm_u);
-          mbar_expect_tx(bar(B_UF), 2 * p.rk * 128);
-          tma_load_2d(sbase + Lay::OFF_U, &tm_u, bar(B_UF), 0, kvh * p.rk);
-          tma_load_2d(sbase + Lay::OFF_U + p.rk * 128, &tm_u, bar(B_UF), 64, kvh * p.rk);
-        }
       } else {
         tma_prefetch_map(role == 3 ? &tm_v : &tm_tab);
       }
@@ -421,7 +422,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         issued = n + 1;
       }
       if (*s_abort) {  // let every copy already issued land before the CTA can exit
-        if (role == 0 && g == 0) mbar_drain(bar(B_UF), 0);
         const int ring = role == 0 ? NS_K / 2 : (role == 3 ? NS_V / 2 : T_SLOTS);
         for (int n = max(0, issued - ring); n < issued; ++n) {
           const int t = g + 2 * (n / per_tile);
@@ -461,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(bar(B_AF + g), j & 1, s_abort, p.status)) break;
           fence_after();
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
+          for (int kk = 0; kk < 8; ++kk)  // K = 16 fp16 (32 bytes, 8 TMEM columns) per MMA
             mma_ts(tg + kColDs + (j & 1) * 16, tg + kColA + kk * 8,
                    sdesc(sQ + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), ID_QK, kk > 0);
           mma_commit(bar(B_SF + 2 * g + (j & 1)));
@@ -492,6 +492,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {  // ---- softmax group g (roles 4..7)
     const int g = half, quarter = warp & 3, row = quarter * 32 + lane;
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + g * kGrpCols;
+    {
+      // U_k -> shared memory as the MN-major SWIZZLE_128B B operand of the reconstruction, its 128 dims
+      // reordered [even | odd]: N-block 0 holds dims 0, 2, .., 126 and N-block 1 dims 1, 3, .., 127.
+      // Item: (latent row r, 16 source dims) -> one 16-byte chunk of each N-block.
+      const int t = (half * 4 + quarter) * 32 + lane;
+      for (int e = t; e < p.rk * 8; e += 256) {
+        const int r = e >> 3, a = e & 7;
+        const uint4* src = reinterpret_cast<const uint4*>(p.u_k + ((size_t)kvh * p.rk + r) * p.ld_u + 16 * a);
+        const uint4 x0 = src[0], x1 = src[1];
+        const uint4 ev = make_uint4(__byte_perm(x0.x, x0.y, 0x5410), __byte_perm(x0.z, x0.w, 0x5410),
+                                    __byte_perm(x1.x, x1.y, 0x5410), __byte_perm(x1.z, x1.w, 0x5410));
+        const uint4 od = make_uint4(__byte_perm(x0.x, x0.y, 0x7632), __byte_perm(x0.z, x0.w, 0x7632),
+                                    __byte_perm(x1.x, x1.y, 0x7632), __byte_perm(x1.z, x1.w, 0x7632));
+        const uint32_t off = r * 128 + ((a ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(smem + Lay::OFF_U + off) = ev;
+        *reinterpret_cast<uint4*>(smem + Lay::OFF_U + p.rk * 128 + off) = od;
+      }
+      fence_proxy_async();  // generic-proxy writes -> visible to the tensor core's reads
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_UF));
+    }
     float m_run[4], l_run[4], o_acc[4], alpha0[4], alpha1[4];  // alphaN: softmax scale of tiles j with j%2 == N
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
@@ -502,13 +523,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const int n_mine = (nt - g + 1) / 2;  // tiles g, g+2, ... below nt
     for (int i = 0; i < n_mine + 2; ++i) {
-      // ---- RoPE(t): K row -> rotate -> fp16 A operand over the first 64 columns of D_k -------------
+      // ---- RoPE(t): column f of D_k holds dim 2f, column 64 + f dim 2f + 1; K_rot -> fp16 A columns ----
       if (i < n_mine) {
         if (!mbar_wait(bar(B_REC + g), i & 1, s_abort, p.status)) break;
         fence_after();
-        // 4 chunks of 32 D_k columns (16 frequency pairs, one table chunk). Each TMEM load is waited for
-        // before any of its registers is touched: an inline-asm tcgen05.ld must not stay in flight across
-        // code the compiler may reschedule.
+        // 4 chunks of 16 frequencies (one table chunk each). Each TMEM load is waited for before any of
+        // its registers is touched: an inline-asm tcgen05.ld must not stay in flight across code the
+        // compiler may reschedule.
         bool ok = true;
 #pragma unroll 1
         for (int ch = 0; ch < 4; ++ch) {
@@ -517,7 +538,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          // SWIZZLE_64B rows of 64 B: 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3).
+          // SWIZZLE_64B rows of 64 B: 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3). Words 0..7:
+          // cos of frequency pairs (f, f+1), words 8..15: their sines (bf16, low half first).
           const unsigned char* tb = smem + Lay::OFF_TAB + sb * Lay::TCH_BYTES + row * 64;
           uint32_t cs[16];
 #pragma unroll
@@ -528,18 +550,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             cs[4 * c4 + 2] = w.z;
             cs[4 * c4 + 3] = w.w;
           }
-          uint32_t kr[32];
-          tmem_ld32(trow + kColDk + 32 * ch, kr);
-          tmem_wait_ld();
-          uint32_t out[16];
-#pragma unroll
-          for (int pp = 0; pp < 16; ++pp) {
-            const float c = __uint_as_float(cs[pp] << 16), sn = __uint_as_float(cs[pp] & 0xFFFF0000u);
-            const float k0 = __uint_as_float(kr[2 * pp]), k1 = __uint_as_float(kr[2 * pp + 1]);
-            out[pp] = pack_half2(k0 * c - k1 * sn, k1 * c + k0 * sn);
-          }
-          __syncwarp();  // every lane has consumed its table values: the slot may refill
+          __syncwarp();  // every lane has read its table values: the slot may refill
           if (lane == 0) mbar_arrive(bar(B_TE + sb));
+          uint32_t ke[16], ko[16], ae[8], ao[8];
+          tmem_ld16(trow + kColDk + 16 * ch, ke);
+          tmem_ld16(trow + kColDk + 64 + 16 * ch, ko);
+          tmem_wait_ld();
+#pragma unroll
+          for (int x = 0; x < 8; ++x) {
+            const float2 c = make_float2(__uint_as_float(cs[x] << 16), __uint_as_float(cs[x] & 0xFFFF0000u));
+            const float2 sn = make_float2(__uint_as_float(cs[8 + x] << 16), __uint_as_float(cs[8 + x] & 0xFFFF0000u));
+            const float2 e = make_float2(__uint_as_float(ke[2 * x]), __uint_as_float(ke[2 * x + 1]));
+            const float2 o = make_float2(__uint_as_float(ko[2 * x]), __uint_as_float(ko[2 * x + 1]));
+            // rot(2f) = k(2f) cos - k(2f+1) sin ; rot(2f+1) = k(2f+1) cos + k(2f) sin
+            const float2 re = __ffma2_rn(o, make_float2(-sn.x, -sn.y), __fmul2_rn(e, c));
+            const float2 ro = __ffma2_rn(e, sn, __fmul2_rn(o, c));
+            ae[x] = pack_half2(re.x, re.y);
+            ao[x] = pack_half2(ro.x, ro.y);
+          }
           if (ch == 0 && i >= 1) {
             // A still feeds QK(t - 2) until that MMA completes; its commit is the scores barrier.
             const int jq = i - 1;
@@ -549,7 +577,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             fence_after();
           }
-          tmem_st16(trow + kColA + 16 * ch, out);
+          // A column 8 ch + x: K_rot dims (2f, 2f+2) of f = 16 ch + 2x, i.e. reordered elements 16 ch + 2x, +1;
+          // column 32 + 8 ch + x: the odd dims of the same frequencies.
+          tmem_st8(trow + kColA + 8 * ch, ae);
+          tmem_st8(trow + kColA + 32 + 8 * ch, ao);
         }
         if (!ok) break;
         tmem_wait_st();

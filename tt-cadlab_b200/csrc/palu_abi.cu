@@ -119,21 +119,23 @@ bool use_tc(const palu_decode_dims* d, bool recon) {
   return tc_supported(d, recon);
 }
 
-// One CTA per SM: pick the split count whose CTA count fills the last wave best, with >= 4 tiles each.
+// One CTA per SM. A CTA costs its tiles plus a fixed setup/drain share worth about 3.3 tiles (TMEM and
+// barrier setup, U load, pipeline fill and drain, the partial's epilogue; measured on B200 at r = 64:
+// ~1.36 us per 128-token tile, ~4.4 us fixed). Pick the split count that minimises
+// waves x (tiles per split + 3.3), fewer splits on ties (the merge also reads every split).
 int choose_splits_tc(const palu_decode_dims* d) {
   if (d->splits > 0) return d->splits < palu::kMaxSplits ? d->splits : palu::kMaxSplits;
   const long items = (long)d->batch * d->n_kv_heads;
-  const int tiles = (d->max_seq + palu::tc::kTile - 1) / palu::tc::kTile;
+  const long tiles = (d->max_seq + palu::tc::kTile - 1) / palu::tc::kTile;
   const long G = device_sms();
   int best = 1;
-  double best_eff = -1.0;
-  for (int s = 1; s <= 64 && s <= tiles; ++s) {
-    if (s > 1 && tiles / s < 4) break;
-    const long units = items * s;
-    const double eff = (double)units / (double)(((units + G - 1) / G) * G);
-    if (eff > best_eff + 1e-9) {
-      best_eff = eff;
-      best = s;
+  long best_cost = -1;
+  for (long s = 1; s <= 64 && s <= tiles; ++s) {
+    const long waves = (items * s + G - 1) / G;
+    const long cost = waves * (10 * ((tiles + s - 1) / s) + 33);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = (int)s;
     }
   }
   return best;
@@ -175,20 +177,20 @@ int encode(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, c
 }
 
 template <int KBK, int KBV>
-int launch_tc(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mt, const CUtensorMap& mu,
-              const palu::tc::TcParams& p, cudaStream_t stream) {
+int launch_tc(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mt, const palu::tc::TcParams& p,
+              cudaStream_t stream) {
   using Lay = palu::tc::Layout<KBK, KBV>;
   auto kern = palu::tc::palu_decode_tc_kernel<KBK, KBV>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::TOTAL) != cudaSuccess)
     return cuda_check("cudaFuncSetAttribute(decode tc)");
-  kern<<<dim3(p.splits, p.n_kv, p.batch), palu::tc::kThreads, Lay::TOTAL, stream>>>(mk, mv, mt, mu, p);
+  kern<<<dim3(p.splits, p.n_kv, p.batch), palu::tc::kThreads, Lay::TOTAL, stream>>>(mk, mv, mt, p);
   return cuda_check("decode tc kernel launch");
 }
 
 int run_tc(const void* q, const void* k, const void* v, const void* u_k, int64_t u_k_ld, const void* cs_pairs,
            const int32_t* cur_pos, void* workspace, float* ws_o, float* ws_ml, const palu_decode_dims* d, int splits,
            float scale, cudaStream_t stream) {
-  CUtensorMap mk, mv, mt, mu;
+  CUtensorMap mk, mv, mt;
   const cuuint64_t items = (cuuint64_t)d->batch * d->n_groups;
   {
     const cuuint64_t dims[3] = {(cuuint64_t)d->r_k, (cuuint64_t)d->max_seq, items};
@@ -205,19 +207,15 @@ int run_tc(const void* q, const void* k, const void* v, const void* u_k, int64_t
   {
     const cuuint64_t dims[2] = {64, (cuuint64_t)d->max_seq};
     const cuuint64_t str[1] = {256};
-    const cuuint32_t box[2] = {16, 128};  // 16 frequency pairs (64 B) x 128 positions
+    const cuuint32_t box[2] = {16, 128};  // one 16-frequency block (16 cos + 16 sin, 64 B) x 128 positions
     if (int st = encode(&mt, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, cs_pairs, dims, str, box, "cs_tab",
                         CU_TENSOR_MAP_SWIZZLE_64B))
       return st;
   }
-  {
-    const cuuint64_t dims[2] = {128, (cuuint64_t)d->n_kv_heads * d->r_k};
-    const cuuint64_t str[1] = {(cuuint64_t)u_k_ld * 2};
-    const cuuint32_t box[2] = {64, (cuuint32_t)d->r_k};
-    if (int st = encode(&mu, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, u_k, dims, str, box, "w_rot")) return st;
-  }
   palu::tc::TcParams p;
   p.q = static_cast<const __nv_bfloat16*>(q);
+  p.u_k = static_cast<const __nv_bfloat16*>(u_k);
+  p.ld_u = (int)u_k_ld;
   p.cur_pos = cur_pos;
   p.ws_o = ws_o;
   p.ws_ml = ws_ml;
@@ -233,10 +231,10 @@ int run_tc(const void* q, const void* k, const void* v, const void* u_k, int64_t
   p.rep = rep_of(d);
   p.scale_log2 = scale * palu::kLog2e;
   const int kbk = d->r_k > 64 ? 2 : 1, kbv = d->r_v > 64 ? 2 : 1;
-  if (kbk == 1 && kbv == 1) return launch_tc<1, 1>(mk, mv, mt, mu, p, stream);
-  if (kbk == 1 && kbv == 2) return launch_tc<1, 2>(mk, mv, mt, mu, p, stream);
-  if (kbk == 2 && kbv == 1) return launch_tc<2, 1>(mk, mv, mt, mu, p, stream);
-  return launch_tc<2, 2>(mk, mv, mt, mu, p, stream);
+  if (kbk == 1 && kbv == 1) return launch_tc<1, 1>(mk, mv, mt, p, stream);
+  if (kbk == 1 && kbv == 2) return launch_tc<1, 2>(mk, mv, mt, p, stream);
+  if (kbk == 2 && kbv == 1) return launch_tc<2, 1>(mk, mv, mt, p, stream);
+  return launch_tc<2, 2>(mk, mv, mt, p, stream);
 }
 
 template <int RV16, bool RECON>
@@ -284,6 +282,8 @@ int run_decode(bool recon, const void* q, const void* k, const void* v, const vo
                 ws_bytes(d, splits));
   if (tc && reinterpret_cast<uintptr_t>(cs_pairs) % 16 != 0)
     return fail(PALU_ERR_INVALID, "cs_tab (packed) must be 16-byte aligned");
+  if (tc && reinterpret_cast<uintptr_t>(u_k) % 16 != 0)
+    return fail(PALU_ERR_INVALID, "w_rot/u_k must be 16-byte aligned");
   float* ws_o = reinterpret_cast<float*>(static_cast<char*>(workspace) + kWsHeader);
   float* ws_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + kWsHeader +
                                           (ws_floats_o(d, splits) * 4 + 255) / 256 * 256);

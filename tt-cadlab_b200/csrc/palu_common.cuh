@@ -50,6 +50,11 @@ PALU_DEVINL void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Packed RoPE table rows (palu_pack_cs_kernel): 128 bf16 per position, 4 blocks of 16 frequencies,
+// each block 16 cosines then the same 16 frequencies' sines. Element index of cos / sin of frequency f:
+PALU_DEVINL int packed_cos_index(int f) { return 32 * (f >> 4) + (f & 15); }
+PALU_DEVINL int packed_sin_index(int f) { return 32 * (f >> 4) + 16 + (f & 15); }
+
 // Two fp32 -> packed bf16x2 (round to nearest even); x0 in the low half.
 PALU_DEVINL uint32_t pack_bf16(float x0, float x1) {
   __nv_bfloat162 v = __floats2bfloat162_rn(x0, x1);
