@@ -1,31 +1,29 @@
 // Split-K flash-decode over Palu latent caches on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
 //
 // One CTA owns (batch row b, KV head h, split s): a contiguous range of 128-token tiles of the positions
-// 0..cur_pos[b]. Its 16 warps form two halves; half g serves the tiles t with t % 2 == g:
-//   warp 8g+0   TMA producer: K-latent tiles of half g
-//   warp 8g+1   the thread issuing half g's tcgen05.mma and commits (warp 1 also allocates TMEM)
-//   warp 8g+2   TMA producer: packed table chunks (16 frequencies x 128 rows: 16 cos then 16 sin per row)
-//   warp 8g+3   TMA producer: V-latent tiles (V lives longest, until PV)
-//   warps 8g+4 .. 8g+7   softmax group g: one thread per token row of the tile
-// At start the 8 softmax warps stage Q^T (fp16) and U_k (bf16) in shared memory with their head dims
-// reordered as [even dims | odd dims], so that D_k holds each rotation pair (2f, 2f+1) in columns f and
-// 64 + f and the rotation of two adjacent frequencies is one packed fp32x2 operation.
-// Per tile t (group g = t % 2; thread = token row inside the tile):
-//   MMA    D_k[128 tok x 128 dim] (f32) = lat_k (smem, K-major) x U_k (smem, MN-major)
-//   group  K row -> RoPE in registers from the table -> K_rot as fp16 into its own TMEM columns: the A
-//          operand of the next MMA (fp16 keeps 11 significant bits; q is bf16, exact in fp16)
-//   MMA    D_s[128 tok x 16] (f32) = K_rot (TMEM, fp16) x Q^T (smem, fp16)
-//   group  online softmax over the query heads (exp2 domain); P^T as bf16 hi + lo -> smem
-//   MMA    D_o[128 lat x 16] (f32) = V^T (smem, MN-major: the V tile exactly as TMA wrote it) x P^T
-//   group  thread c (latent dim c) accumulates O[h][c] = O * alpha + hi + lo in registers
-// Software pipeline: in its iteration for tile t a group does RoPE(t), softmax(t-2), accumulate(t-4), so
-// each wait is for an MMA issued two tiles earlier; the MMA thread issues QK(t), reconstruct(t+2),
-// PV(t-2). A single thread issues at most one tcgen05.mma per ~64 cycles whatever its shape (measured
-// on B200), so the per-tile MMA count (r_k/16 + 8 + 8) matters as much as their arithmetic. Every ring, barrier and TMEM region is private to one half, each role thread blocks (sleeping
-// in mbarrier try_wait) on one barrier at a time, and no barrier can run two phases ahead of its waiter,
-// so parity waits never alias. The two groups merge their
-// (m, l, O) at the end into one split partial (combine.cuh merges the splits). Every wait is bounded (1 s of globaltimer): on expiry the CTA records a status code,
-// all roles stop, copies and MMAs in flight are drained, and TMEM is freed.
+// 0..cur_pos[b]. Two groups work on alternate tiles (group g on tiles t with t % 2 == g), so two tiles are in
+// flight per CTA. Each group has its own warps, rings, barriers and TMEM columns (24 warps in all, see
+// role_of): a K+table TMA producer, a V producer, a QK issuer, a reconstruct+PV issuer (a single thread
+// issues at most one tcgen05.mma per ~64 cycles whatever its shape, measured on B200, so the MMAs are
+// split over two threads), 4 RoPE warps and 4 softmax warps (a warp of either kind owns the 32 TMEM lanes
+// of its SMSP quarter: 32 token rows of the tile, or 32 latent dims of the PV output).
+// At start the softmax warps stage Q^T (fp16) and the RoPE warps U_k (bf16) in shared memory with their
+// head dims reordered as [even dims | odd dims], so that D_k holds each rotation pair (2f, 2f+1) in columns
+// f and 64 + f and the rotation of two adjacent frequencies is one packed fp32x2 operation.
+// Per group-local tile j (tile t = g + 2 j):
+//   MMA      D_k[128 tok x 128 dim] (f32) = lat_k (smem, K-major) x U_k (smem, MN-major)
+//   RoPE     K row -> rotate in registers from the table -> K_rot as fp16 into its own TMEM columns: the A
+//            operand of QK (fp16 keeps 11 significant bits; q is bf16, exact in fp16)
+//   MMA      D_s[128 tok x 16] (f32) = K_rot (TMEM) x Q^T (smem, fp16)
+//   softmax  online softmax over the query heads (exp2 domain); P^T as bf16 hi + lo -> smem
+//   MMA      D_o[128 lat x 16] (f32) = V^T (smem, MN-major: the V tile exactly as TMA wrote it) x P^T
+//   softmax  thread c (latent dim c) accumulates O[h][c] = O * alpha + hi + lo in registers
+// The reconstruction of tile j + 1 is issued as soon as RoPE(j) has read D_k; RoPE(j + 1) then overlaps
+// softmax(j) and PV(j - 1). D_s, D_o and P are double-buffered by j % 2, and every consumer releases what
+// it read with its own barrier, so no barrier runs two phases ahead of a waiter. The two groups merge
+// their (m, l, O) at the end into one split partial (combine.cuh merges the splits). Every wait is bounded
+// (1 s of globaltimer): on expiry the CTA records a status code, all roles stop, copies and MMAs in flight
+// are drained, and TMEM is freed.
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -35,7 +33,7 @@
 namespace palu {
 namespace tc {
 
-constexpr int kThreads = 512;
+constexpr int kThreads = 768;
 constexpr int kTile = 128;
 constexpr int kBox = 16384;             // one TMA box: 128 rows x 128 B
 constexpr int kTmemCols = 512;
@@ -260,6 +258,30 @@ PALU_DEVINL uint32_t sw128_offset(int row, int k, int rows) {
 
 // ---- the kernel --------------------------------------------------------------------------------------
 
+PALU_DEVINL void tmem_st4(uint32_t taddr, const uint32_t (&r)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};\n" ::"r"(taddr), "r"(r[0]), "r"(r[1]),
+               "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+
+// Warp roles (24 warps). Warps 0..7 are single-lane role warps, two per SMSP (warp w runs on SMSP w % 4):
+//   group 0: 0 = K+table producer, 1 = QK issuer, 2 = reconstruct+PV issuer, 3 = V producer
+//   group 1: 4 = QK issuer, 5 = K+table producer, 6 = V producer, 7 = reconstruct+PV issuer
+// Warps 8..15: RoPE warps (group (w - 8) / 4), warps 16..23: softmax warps (group (w - 16) / 4); warp w of
+// either kind owns TMEM lanes 32 (w % 4) .. + 31, i.e. token rows (tile) or latent dims (PV output).
+enum : int { kRoleKT = 0, kRoleQK = 1, kRoleRP = 2, kRoleV = 3 };
+PALU_DEVINL int role_of(int warp) {
+  switch (warp) {
+    case 0:
+    case 5: return kRoleKT;
+    case 1:
+    case 4: return kRoleQK;
+    case 2:
+    case 7: return kRoleRP;
+    default: return kRoleV;
+  }
+}
+
 template <int KBK, int KBV>
 __global__ void __launch_bounds__(kThreads, 1)
     palu_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -286,10 +308,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---- barriers and scalars (misc area) ----
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Lay::OFF_MISC);
   auto bar = [&](int i) { return smem_u32(bars + i); };
+  // [g][x] pairs are double-buffered by the group-local tile index parity x.
   constexpr int B_KF = 0, B_KE = B_KF + NS_K, B_VF = B_KE + NS_K, B_VE = B_VF + NS_V, B_TF = B_VE + NS_V,
                 B_TE = B_TF + NS_T, B_UF = B_TE + NS_T, B_REC = B_UF + 1, B_AF = B_REC + 2, B_SF = B_AF + 2,
-                B_PF = B_SF + 4, B_OF = B_PF + 4, B_OR = B_OF + 4, B_MX = B_OR + 4, B_DRAIN = B_MX + 4,
-                B_COUNT = B_DRAIN + 2;
+                B_SR = B_SF + 4, B_PF = B_SR + 4, B_OF = B_PF + 4, B_OR = B_OF + 4, B_MX = B_OR + 4,
+                B_DRAIN = B_MX + 4, B_COUNT = B_DRAIN + 4;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + B_COUNT);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
   float* s_max = reinterpret_cast<float*>(s_tmem + 4);  // [2 groups][2 bufs][4 warps][4 heads]
@@ -307,24 +330,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < NS_T; ++s) {
       mbar_init(bar(B_TF + s), 1);
-      mbar_init(bar(B_TE + s), 4);
+      mbar_init(bar(B_TE + s), 4);  // the group's 4 RoPE warps
     }
-    mbar_init(bar(B_UF), 8);  // the 8 softmax warps stage U_k
+    mbar_init(bar(B_UF), 8);  // the 8 RoPE warps stage U_k
     for (int g = 0; g < 2; ++g) {
       mbar_init(bar(B_REC + g), 1);
       mbar_init(bar(B_AF + g), 4);
       for (int x = 0; x < 2; ++x) {
-        // p_full is double-buffered by tile parity: a group may finish softmax(t) before the MMA thread
-        // has tested softmax(t-2)'s arrival, which on a single barrier would alias two phases.
-        mbar_init(bar(B_PF + 2 * g + x), 4);
         mbar_init(bar(B_SF + 2 * g + x), 1);
+        mbar_init(bar(B_SR + 2 * g + x), 4);
+        mbar_init(bar(B_PF + 2 * g + x), 4);
         mbar_init(bar(B_OF + 2 * g + x), 1);
         mbar_init(bar(B_OR + 2 * g + x), 4);
         mbar_init(bar(B_MX + 2 * g + x), 4);
       }
     }
-    mbar_init(bar(B_DRAIN), 1);
-    mbar_init(bar(B_DRAIN + 1), 1);
+    for (int x = 0; x < 4; ++x) mbar_init(bar(B_DRAIN + x), 1);
     *s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
@@ -334,8 +355,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
   }
-  if ((warp & 7) >= 4) {
-    const int t = ((warp >> 3) * 4 + (warp & 3)) * 32 + lane;  // 0..255 over the 8 softmax warps
+  if (warp >= 16) {
+    const int t = (warp - 16) * 32 + lane;  // 0..255 over the 8 softmax warps
     // Q^T operand, fp16, K-major SWIZZLE_128B: 16 rows (this KV head's query heads, zero padded) x 128
     // dims in [even | odd] order: K-block 0 = even dims, K-block 1 = odd dims (64 fp16 per 128-B row).
     // Thread: (row, 16-byte chunk of 8 reordered dims); bf16 q is exact in fp16.
@@ -367,137 +388,132 @@ __global__ void __launch_bounds__(kThreads, 1)
   fence_after();
   const uint32_t tmem = *s_tmem;
 
-  // ============================== roles ==============================
-  const int half = warp >> 3, role = warp & 7;
-  if (role == 0 || role == 2 || role == 3) {
-    // ---- TMA producers of half g: role 0 = K latent (+ U_k once), 3 = V latent, 2 = table chunks.
-    const int g = half;
-    if (lane == 0 && nt > g) {
-      if (role == 0) {
-        tma_prefetch_map(&tm_k);
+  if (warp < 8) {
+    // ============================== single-lane role warps ==============================
+    const int g = warp < 4 ? 0 : 1, role = role_of(warp);
+    const int n_g = (nt - g + 1) / 2;  // this group's tiles: t = g + 2 j, j < n_g
+    if (lane == 0 && n_g > 0) {
+      if (role == kRoleKT || role == kRoleV) {
+        // ---- TMA producers: K tile then its 4 table chunks (KT), or the V tile (V), per group tile.
+        const bool kt = role == kRoleKT;
+        tma_prefetch_map(kt ? &tm_k : &tm_v);
+        if (kt) tma_prefetch_map(&tm_tab);
+        int issued_kv = 0, issued_t = 0;
+        for (int j = 0; j < n_g; ++j) {
+          const int t = g + 2 * j, row = (tile0 + t) * kTile;
+          const int sb = kt ? t % NS_K : t % NS_V, use = kt ? t / NS_K : t / NS_V;
+          const uint32_t full = bar((kt ? B_KF : B_VF) + sb), empty = bar((kt ? B_KE : B_VE) + sb);
+          if (use >= 1 && !mbar_wait(empty, (use - 1) & 1, s_abort, p.status)) break;
+          if (kt) {
+            mbar_expect_tx(full, Lay::K_BYTES);
+            const uint32_t dst = sbase + Lay::OFF_K + sb * Lay::K_BYTES;
+#pragma unroll
+            for (int kb = 0; kb < KBK; ++kb) tma_load_3d(dst + kb * kBox, &tm_k, full, kb * 64, row, item_lat);
+          } else {
+            mbar_expect_tx(full, Lay::V_BYTES);
+            const uint32_t dst = sbase + Lay::OFF_V + sb * Lay::V_BYTES;
+#pragma unroll
+            for (int vb = 0; vb < KBV; ++vb) tma_load_3d(dst + vb * kBox, &tm_v, full, vb * 64, row, item_lat);
+          }
+          issued_kv = j + 1;
+          if (kt) {
+            bool ok = true;
+            for (int c = 0; c < 4; ++c) {
+              const int n = 4 * j + c, ts = g * T_SLOTS + n % T_SLOTS, tuse = n / T_SLOTS;
+              if (tuse >= 1 && !mbar_wait(bar(B_TE + ts), (tuse - 1) & 1, s_abort, p.status)) {
+                ok = false;
+                break;
+              }
+              mbar_expect_tx(bar(B_TF + ts), Lay::TCH_BYTES);
+              tma_load_2d(sbase + Lay::OFF_TAB + ts * Lay::TCH_BYTES, &tm_tab, bar(B_TF + ts), c * 16, row);
+              issued_t = n + 1;
+            }
+            if (!ok) break;
+          }
+        }
+        if (*s_abort) {  // let every copy already issued land before the CTA can exit
+          const int ring = kt ? NS_K / 2 : NS_V / 2;
+          for (int j = max(0, issued_kv - ring); j < issued_kv; ++j) {
+            const int t = g + 2 * j;
+            if (kt) mbar_drain(bar(B_KF + t % NS_K), (t / NS_K) & 1);
+            else mbar_drain(bar(B_VF + t % NS_V), (t / NS_V) & 1);
+          }
+          for (int n = max(0, issued_t - T_SLOTS); n < issued_t; ++n)
+            mbar_drain(bar(B_TF + g * T_SLOTS + n % T_SLOTS), (n / T_SLOTS) & 1);
+        }
       } else {
-        tma_prefetch_map(role == 3 ? &tm_v : &tm_tab);
-      }
-      const int per_tile = role == 2 ? 4 : 1;
-      const int count = (g == 0 ? (nt + 1) / 2 : nt / 2) * per_tile;
-      int issued = 0;
-      for (int n = 0; n < count; ++n) {
-        const int j = n / per_tile, c = n % per_tile, t = g + 2 * j;
-        int sb, use;
-        uint32_t full, empty, dst, bytes;
-        if (role == 0) {
-          sb = t % NS_K;
-          use = t / NS_K;
-          full = bar(B_KF + sb);
-          empty = bar(B_KE + sb);
-          dst = sbase + Lay::OFF_K + sb * Lay::K_BYTES;
-          bytes = Lay::K_BYTES;
-        } else if (role == 3) {
-          sb = t % NS_V;
-          use = t / NS_V;
-          full = bar(B_VF + sb);
-          empty = bar(B_VE + sb);
-          dst = sbase + Lay::OFF_V + sb * Lay::V_BYTES;
-          bytes = Lay::V_BYTES;
-        } else {
-          sb = g * T_SLOTS + n % T_SLOTS;
-          use = n / T_SLOTS;
-          full = bar(B_TF + sb);
-          empty = bar(B_TE + sb);
-          dst = sbase + Lay::OFF_TAB + sb * Lay::TCH_BYTES;
-          bytes = Lay::TCH_BYTES;
-        }
-        if (use >= 1 && !mbar_wait(empty, (use - 1) & 1, s_abort, p.status)) break;
-        mbar_expect_tx(full, bytes);
-        const int row = (tile0 + t) * kTile;
-        if (role == 0) {
+        const uint32_t tg = tmem + g * kGrpCols;
+        const int drain = B_DRAIN + 2 * g + (role == kRoleQK ? 0 : 1);
+        if (role == kRoleQK) {
+          // ---- QK(j): D_s[j & 1] = K_rot (TMEM, fp16) x Q^T, once RoPE(j) wrote A and softmax(j - 2) read D_s.
+          constexpr uint32_t ID_QK = idesc_f16(16, 0, false, false);
+          const uint32_t sQ = sbase + Lay::OFF_Q;
+          for (int j = 0; j < n_g; ++j) {
+            if (!mbar_wait(bar(B_AF + g), j & 1, s_abort, p.status)) break;
+            if (j >= 2 && !mbar_wait(bar(B_SR + 2 * g + (j & 1)), ((j >> 1) - 1) & 1, s_abort, p.status)) break;
+            fence_after();
 #pragma unroll
-          for (int kb = 0; kb < KBK; ++kb) tma_load_3d(dst + kb * kBox, &tm_k, full, kb * 64, row, item_lat);
-        } else if (role == 3) {
-#pragma unroll
-          for (int vb = 0; vb < KBV; ++vb) tma_load_3d(dst + vb * kBox, &tm_v, full, vb * 64, row, item_lat);
+            for (int kk = 0; kk < 8; ++kk)  // K = 16 fp16 (32 bytes, 8 TMEM columns) per MMA
+              mma_ts(tg + kColDs + (j & 1) * 16, tg + kColA + kk * 8,
+                     sdesc(sQ + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), ID_QK, kk > 0);
+            mma_commit(bar(B_SF + 2 * g + (j & 1)));
+          }
         } else {
-          tma_load_2d(dst, &tm_tab, full, c * 16, row);
+          // ---- reconstruct(j + 1) once RoPE(j) has read D_k; PV(j - 1) once softmax(j - 1) wrote P.
+          constexpr uint32_t ID_REC = idesc_f16(128, 1, false, true);  // bf16 lat x bf16 U (MN-major)
+          constexpr uint32_t ID_PV = idesc_f16(16, 1, true, false);    // bf16 V^T (MN-major) x bf16 P
+          const uint32_t sU = sbase + Lay::OFF_U;
+          const uint32_t u_lbo = p.rk * 128;            // U: stride between the two 64-dim N-blocks
+          const uint32_t v_lbo = p.rv > 64 ? kBox : 0;  // V: second 64-dim M-block (or a duplicate of the first)
+          auto recon = [&](int j) -> bool {
+            const int t = g + 2 * j, s = t % NS_K;
+            if (!mbar_wait(bar(B_KF + s), (t / NS_K) & 1, s_abort, p.status)) return false;
+            fence_after();
+            const uint32_t sK = sbase + Lay::OFF_K + s * Lay::K_BYTES;
+            for (int kk = 0; kk < p.rk / 16; ++kk)
+              mma_ss(tg + kColDk, sdesc(sK + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024),
+                     sdesc(sU + kk * 2048, u_lbo, 1024), ID_REC, kk > 0);
+            mma_commit(bar(B_KE + s));
+            mma_commit(bar(B_REC + g));
+            return true;
+          };
+          bool ok = mbar_wait(bar(B_UF), 0, s_abort, p.status) && recon(0);
+          for (int j = 0; ok && j <= n_g; ++j) {
+            if (j + 1 < n_g) {
+              if (!mbar_wait(bar(B_AF + g), j & 1, s_abort, p.status) || !recon(j + 1)) break;
+            }
+            if (j >= 1) {  // PV(j - 1)
+              const int jp = j - 1, tp = g + 2 * jp, sv = tp % NS_V;
+              if (!mbar_wait(bar(B_PF + 2 * g + (jp & 1)), (jp >> 1) & 1, s_abort, p.status)) break;
+              if (jp >= 2 && !mbar_wait(bar(B_OR + 2 * g + (jp & 1)), ((jp >> 1) - 1) & 1, s_abort, p.status)) break;
+              if (!mbar_wait(bar(B_VF + sv), (tp / NS_V) & 1, s_abort, p.status)) break;
+              fence_after();
+              const uint32_t sV = sbase + Lay::OFF_V + sv * Lay::V_BYTES;
+              const uint32_t sP = sbase + Lay::OFF_P + (2 * g + (jp & 1)) * Lay::P_BYTES;
+#pragma unroll
+              for (int kk = 0; kk < 8; ++kk)
+                mma_ss(tg + kColDo + (jp & 1) * 16, sdesc(sV + kk * 2048, v_lbo, 1024),
+                       sdesc(sP + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), ID_PV, kk > 0);
+              mma_commit(bar(B_OF + 2 * g + (jp & 1)));
+              mma_commit(bar(B_VE + sv));
+            }
+          }
         }
-        issued = n + 1;
-      }
-      if (*s_abort) {  // let every copy already issued land before the CTA can exit
-        const int ring = role == 0 ? NS_K / 2 : (role == 3 ? NS_V / 2 : T_SLOTS);
-        for (int n = max(0, issued - ring); n < issued; ++n) {
-          const int t = g + 2 * (n / per_tile);
-          if (role == 0) mbar_drain(bar(B_KF + t % NS_K), (t / NS_K) & 1);
-          else if (role == 3) mbar_drain(bar(B_VF + t % NS_V), (t / NS_V) & 1);
-          else mbar_drain(bar(B_TF + g * T_SLOTS + n % T_SLOTS), (n / T_SLOTS) & 1);
-        }
+        // Drain: every MMA this thread issued has completed once this barrier flips.
+        mma_commit(bar(drain));
+        mbar_drain(bar(drain), 0);
       }
     }
     __syncwarp();
-  } else if (role == 1) {  // ---- MMA issue for half g: QK(t) -> reconstruct(t+2) -> PV(t-2) per tile
-    const int g = half;
-    if (lane == 0 && nt > g) {
-      constexpr uint32_t ID_REC = idesc_f16(128, 1, false, true);  // bf16 lat x bf16 U (MN-major)
-      constexpr uint32_t ID_QK = idesc_f16(16, 0, false, false);   // fp16 K_rot (TMEM) x fp16 Q
-      constexpr uint32_t ID_PV = idesc_f16(16, 1, true, false);    // bf16 V^T (MN-major) x bf16 P
-      const uint32_t sU = sbase + Lay::OFF_U, sQ = sbase + Lay::OFF_Q;
-      const uint32_t u_lbo = p.rk * 128;            // U: stride between the two 64-dim N-blocks
-      const uint32_t v_lbo = p.rv > 64 ? kBox : 0;  // V: second 64-dim M-block (or a duplicate of the first)
-      const uint32_t tg = tmem + g * kGrpCols;
-      auto recon = [&](int t) -> bool {
-        const int s = t % NS_K;
-        if (!mbar_wait(bar(B_KF + s), (t / NS_K) & 1, s_abort, p.status)) return false;
-        fence_after();
-        const uint32_t sK = sbase + Lay::OFF_K + s * Lay::K_BYTES;
-        for (int kk = 0; kk < p.rk / 16; ++kk)
-          mma_ss(tg + kColDk, sdesc(sK + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024),
-                 sdesc(sU + kk * 2048, u_lbo, 1024), ID_REC, kk > 0);
-        mma_commit(bar(B_KE + s));
-        mma_commit(bar(B_REC + g));
-        return true;
-      };
-      bool ok = mbar_wait(bar(B_UF), 0, s_abort, p.status) && recon(g);
-      for (int t = g; ok && t - 2 < nt; t += 2) {
-        const int j = t >> 1;
-        if (t < nt) {  // QK(t)
-          if (!mbar_wait(bar(B_AF + g), j & 1, s_abort, p.status)) break;
-          fence_after();
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)  // K = 16 fp16 (32 bytes, 8 TMEM columns) per MMA
-            mma_ts(tg + kColDs + (j & 1) * 16, tg + kColA + kk * 8,
-                   sdesc(sQ + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), ID_QK, kk > 0);
-          mma_commit(bar(B_SF + 2 * g + (j & 1)));
-        }
-        if (t + 2 < nt && !recon(t + 2)) break;  // D_k is free: RoPE(t) read it before QK(t) was allowed
-        const int tp = t - 2;
-        if (tp >= 0) {  // PV(t - 2)
-          const int jp = tp >> 1, sv = tp % NS_V;
-          if (!mbar_wait(bar(B_PF + 2 * g + (jp & 1)), (jp >> 1) & 1, s_abort, p.status)) break;
-          if (jp >= 2 && !mbar_wait(bar(B_OR + 2 * g + (jp & 1)), ((jp >> 1) - 1) & 1, s_abort, p.status)) break;
-          if (!mbar_wait(bar(B_VF + sv), (tp / NS_V) & 1, s_abort, p.status)) break;
-          fence_after();
-          const uint32_t sV = sbase + Lay::OFF_V + sv * Lay::V_BYTES;
-          const uint32_t sP = sbase + Lay::OFF_P + (2 * g + (jp & 1)) * Lay::P_BYTES;
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            mma_ss(tg + kColDo + (jp & 1) * 16, sdesc(sV + kk * 2048, v_lbo, 1024),
-                   sdesc(sP + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), ID_PV, kk > 0);
-          mma_commit(bar(B_OF + 2 * g + (jp & 1)));
-          mma_commit(bar(B_VE + sv));
-        }
-      }
-      // Drain: every MMA this thread issued has completed once this barrier flips.
-      mma_commit(bar(B_DRAIN + g));
-      mbar_drain(bar(B_DRAIN + g), 0);
-    }
-    __syncwarp();
-  } else {  // ---- softmax group g (roles 4..7)
-    const int g = half, quarter = warp & 3, row = quarter * 32 + lane;
+  } else if (warp < 16) {
+    // ============================== RoPE warps ==============================
+    const int g = (warp - 8) >> 2, quarter = warp & 3, row = quarter * 32 + lane;
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + g * kGrpCols;
     {
       // U_k -> shared memory as the MN-major SWIZZLE_128B B operand of the reconstruction, its 128 dims
       // reordered [even | odd]: N-block 0 holds dims 0, 2, .., 126 and N-block 1 dims 1, 3, .., 127.
       // Item: (latent row r, 16 source dims) -> one 16-byte chunk of each N-block.
-      const int t = (half * 4 + quarter) * 32 + lane;
-      for (int e = t; e < p.rk * 8; e += 256) {
+      for (int e = (warp - 8) * 32 + lane; e < p.rk * 8; e += 256) {
         const int r = e >> 3, a = e & 7;
         const uint4* src = reinterpret_cast<const uint4*>(p.u_k + ((size_t)kvh * p.rk + r) * p.ld_u + 16 * a);
         const uint4 x0 = src[0], x1 = src[1];
@@ -513,53 +529,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(B_UF));
     }
-    float m_run[4], l_run[4], o_acc[4], alpha0[4], alpha1[4];  // alphaN: softmax scale of tiles j with j%2 == N
-#pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      m_run[h] = -INFINITY;
-      l_run[h] = 0.f;
-      o_acc[h] = 0.f;
-      alpha0[h] = alpha1[h] = 1.f;
-    }
-    const int n_mine = (nt - g + 1) / 2;  // tiles g, g+2, ... below nt
-    for (int i = 0; i < n_mine + 2; ++i) {
-      // ---- RoPE(t): column f of D_k holds dim 2f, column 64 + f dim 2f + 1; K_rot -> fp16 A columns ----
-      if (i < n_mine) {
-        if (!mbar_wait(bar(B_REC + g), i & 1, s_abort, p.status)) break;
-        fence_after();
-        // 4 chunks of 16 frequencies (one table chunk each). Each TMEM load is waited for before any of
-        // its registers is touched: an inline-asm tcgen05.ld must not stay in flight across code the
-        // compiler may reschedule.
-        bool ok = true;
+    const int n_g = (nt - g + 1) / 2;
+    for (int i = 0; i < n_g; ++i) {
+      // ---- RoPE(i): column f of D_k holds dim 2f, column 64 + f dim 2f + 1; K_rot -> fp16 A columns ----
+      if (!mbar_wait(bar(B_REC + g), i & 1, s_abort, p.status)) break;
+      fence_after();
+      bool ok = true;
 #pragma unroll 1
-        for (int ch = 0; ch < 4; ++ch) {
-          const int n = i * 4 + ch, sb = g * T_SLOTS + n % T_SLOTS;
-          if (!mbar_wait(bar(B_TF + sb), (n / T_SLOTS) & 1, s_abort, p.status)) {
-            ok = false;
-            break;
-          }
-          // SWIZZLE_64B rows of 64 B: 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3). Words 0..7:
-          // cos of frequency pairs (f, f+1), words 8..15: their sines (bf16, low half first).
-          const unsigned char* tb = smem + Lay::OFF_TAB + sb * Lay::TCH_BYTES + row * 64;
-          uint32_t cs[16];
+      for (int ch = 0; ch < 4; ++ch) {
+        const int n = i * 4 + ch, sb = g * T_SLOTS + n % T_SLOTS;
+        if (!mbar_wait(bar(B_TF + sb), (n / T_SLOTS) & 1, s_abort, p.status)) {
+          ok = false;
+          break;
+        }
+        // SWIZZLE_64B rows of 64 B: 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3). Words 0..7:
+        // cos of frequency pairs (f, f+1), words 8..15: their sines (bf16, low half first).
+        const unsigned char* tb = smem + Lay::OFF_TAB + sb * Lay::TCH_BYTES + row * 64;
+        uint32_t cs[16];
 #pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            const uint4 w = *reinterpret_cast<const uint4*>(tb + ((c4 ^ ((row >> 1) & 3)) << 4));
-            cs[4 * c4 + 0] = w.x;
-            cs[4 * c4 + 1] = w.y;
-            cs[4 * c4 + 2] = w.z;
-            cs[4 * c4 + 3] = w.w;
-          }
-          __syncwarp();  // every lane has read its table values: the slot may refill
-          if (lane == 0) mbar_arrive(bar(B_TE + sb));
-          uint32_t ke[16], ko[16], ae[8], ao[8];
-          tmem_ld16(trow + kColDk + 16 * ch, ke);
-          tmem_ld16(trow + kColDk + 64 + 16 * ch, ko);
+        for (int c4 = 0; c4 < 4; ++c4) {
+          const uint4 w = *reinterpret_cast<const uint4*>(tb + ((c4 ^ ((row >> 1) & 3)) << 4));
+          cs[4 * c4 + 0] = w.x;
+          cs[4 * c4 + 1] = w.y;
+          cs[4 * c4 + 2] = w.z;
+          cs[4 * c4 + 3] = w.w;
+        }
+        __syncwarp();  // every lane has read its table values: the slot may refill
+        if (lane == 0) mbar_arrive(bar(B_TE + sb));
+#pragma unroll
+        for (int hc = 0; hc < 2; ++hc) {  // 8 frequencies per half chunk
+          uint32_t ke[8], ko[8], ae[4], ao[4];
+          tmem_ld8(trow + kColDk + 16 * ch + 8 * hc, ke);
+          tmem_ld8(trow + kColDk + 64 + 16 * ch + 8 * hc, ko);
           tmem_wait_ld();
 #pragma unroll
-          for (int x = 0; x < 8; ++x) {
-            const float2 c = make_float2(__uint_as_float(cs[x] << 16), __uint_as_float(cs[x] & 0xFFFF0000u));
-            const float2 sn = make_float2(__uint_as_float(cs[8 + x] << 16), __uint_as_float(cs[8 + x] & 0xFFFF0000u));
+          for (int x = 0; x < 4; ++x) {
+            const uint32_t cw = cs[4 * hc + x], sw = cs[8 + 4 * hc + x];
+            const float2 c = make_float2(__uint_as_float(cw << 16), __uint_as_float(cw & 0xFFFF0000u));
+            const float2 sn = make_float2(__uint_as_float(sw << 16), __uint_as_float(sw & 0xFFFF0000u));
             const float2 e = make_float2(__uint_as_float(ke[2 * x]), __uint_as_float(ke[2 * x + 1]));
             const float2 o = make_float2(__uint_as_float(ko[2 * x]), __uint_as_float(ko[2 * x + 1]));
             // rot(2f) = k(2f) cos - k(2f+1) sin ; rot(2f+1) = k(2f+1) cos + k(2f) sin
@@ -568,8 +575,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             ae[x] = pack_half2(re.x, re.y);
             ao[x] = pack_half2(ro.x, ro.y);
           }
-          if (ch == 0 && i >= 1) {
-            // A still feeds QK(t - 2) until that MMA completes; its commit is the scores barrier.
+          if (ch == 0 && hc == 0 && i >= 1) {
+            // A still feeds QK(i - 1) until that MMA completes; its commit is the scores barrier.
             const int jq = i - 1;
             if (!mbar_wait(bar(B_SF + 2 * g + (jq & 1)), (jq >> 1) & 1, s_abort, p.status)) {
               ok = false;
@@ -577,25 +584,44 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             fence_after();
           }
-          // A column 8 ch + x: K_rot dims (2f, 2f+2) of f = 16 ch + 2x, i.e. reordered elements 16 ch + 2x, +1;
-          // column 32 + 8 ch + x: the odd dims of the same frequencies.
-          tmem_st8(trow + kColA + 8 * ch, ae);
-          tmem_st8(trow + kColA + 32 + 8 * ch, ao);
+          // A column 8 ch + 4 hc + x: K_rot dims (2f, 2f + 2) of f = 16 ch + 8 hc + 2x (reordered elements
+          // f, f + 1); column 32 + the same: the odd dims of those frequencies.
+          tmem_st4(trow + kColA + 8 * ch + 4 * hc, ae);
+          tmem_st4(trow + kColA + 32 + 8 * ch + 4 * hc, ao);
         }
         if (!ok) break;
-        tmem_wait_st();
-        fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_AF + g));
       }
-      // ---- softmax(t - 2) ---------------------------------------------------------------------------
-      if (i >= 1 && i - 1 < n_mine) {
-        const int j = i - 1, t = g + 2 * j;
+      if (!ok) break;
+      tmem_wait_st();
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_AF + g));
+    }
+  } else {
+    // ============================== softmax warps ==============================
+    const int g = (warp - 16) >> 2, quarter = warp & 3, row = quarter * 32 + lane;
+    const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + g * kGrpCols;
+    float m_run[4], l_run[4], o_acc[4], alpha0[4], alpha1[4];  // alphaN: softmax scale of tiles j with j%2 == N
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      m_run[h] = -INFINITY;
+      l_run[h] = 0.f;
+      o_acc[h] = 0.f;
+      alpha0[h] = alpha1[h] = 1.f;
+    }
+    const int n_g = (nt - g + 1) / 2;
+    for (int j = 0; j <= n_g; ++j) {
+      // ---- softmax(j) ---------------------------------------------------------------------------------
+      if (j < n_g) {
+        const int t = g + 2 * j;
         if (!mbar_wait(bar(B_SF + 2 * g + (j & 1)), (j >> 1) & 1, s_abort, p.status)) break;
         fence_after();
         uint32_t sc[4];
         tmem_ld4(trow + kColDs + (j & 1) * 16, sc);
         tmem_wait_ld();
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_SR + 2 * g + (j & 1)));  // D_s[j & 1] may be overwritten
         const int tile_start = (tile0 + t) * kTile;
         const bool valid = tile_start + row < L;
         float x[4], mx[4];
@@ -647,20 +673,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B_PF + 2 * g + (j & 1)));
       }
-      // ---- accumulate(t - 4) ------------------------------------------------------------------------
-      if (i >= 2 && i - 2 < n_mine) {
-        const int j = i - 2;
-        if (!mbar_wait(bar(B_OF + 2 * g + (j & 1)), (j >> 1) & 1, s_abort, p.status)) break;
+      // ---- accumulate(j - 1) ------------------------------------------------------------------------
+      if (j >= 1) {
+        const int ja = j - 1;
+        if (!mbar_wait(bar(B_OF + 2 * g + (ja & 1)), (ja >> 1) & 1, s_abort, p.status)) break;
         fence_after();
         uint32_t ov[8];
-        tmem_ld8(trow + kColDo + (j & 1) * 16, ov);
+        tmem_ld8(trow + kColDo + (ja & 1) * 16, ov);
         tmem_wait_ld();
 #pragma unroll
         for (int h = 0; h < 4; ++h)
-          o_acc[h] = o_acc[h] * ((j & 1) ? alpha1[h] : alpha0[h]) + __uint_as_float(ov[h]) + __uint_as_float(ov[4 + h]);
+          o_acc[h] = o_acc[h] * ((ja & 1) ? alpha1[h] : alpha0[h]) + __uint_as_float(ov[h]) + __uint_as_float(ov[4 + h]);
         fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_OR + 2 * g + (j & 1)));
+        if (lane == 0) mbar_arrive(bar(B_OR + 2 * g + (ja & 1)));
       }
     }
     // ---- this group's partial -> shared memory -----------------------------------------------------
@@ -683,10 +709,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
 
   // ---- merge the two groups and write this split's partial (unnormalised O, m, l) ----------------
-  if ((warp & 7) >= 4) {
+  if (warp >= 16) {
     const float* s_o = reinterpret_cast<const float*>(smem + Lay::OFF_O);
     const size_t item = ((size_t)(b * p.n_kv + kvh) * p.splits + split) * p.rep;
-    for (int idx = ((warp >> 3) * 4 + (warp & 3)) * 32 + lane; idx < p.rep * p.rv; idx += 256) {
+    for (int idx = (warp - 16) * 32 + lane; idx < p.rep * p.rv; idx += 256) {
       const int h = idx / p.rv, c = idx - h * p.rv;
       const float m0 = s_m[h], m1 = s_m[4 + h];
       const float M = fmaxf(m0, m1);
