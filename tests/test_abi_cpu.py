@@ -46,6 +46,8 @@ def _call_invalid(dims, **kw):
     (dict(head_dim=64), "head_dim"),
     (dict(r_k=40), "r_k"),
     (dict(r_v=24), "r_v"),
+    (dict(r_k=144), "r_k"),   # above 128 widths step by 32
+    (dict(r_v=288), "r_v"),   # widest supported latent is 256
     (dict(n_groups=3), "heads_per_group"),
     (dict(n_q_heads=30), "KV head count"),
     (dict(n_groups=2), "u_v"),

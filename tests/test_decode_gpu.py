@@ -87,9 +87,6 @@ GOLDEN_CASES = ["decode_mlrd_r64", "decode_mlrd_rk32_rv128", "decode_identity_r1
 def test_golden_fixtures(cuda, kernel, name, out_dtype):
     """The reference's own reference_decode outputs (tests/golden/make_golden.py)."""
     d = load_golden(name)
-    gs = int(d["group_size"])
-    if gs > 1 and (d["k_lat"].shape[-1] > 128 or d["v_lat"].shape[-1] > 128):
-        pytest.skip("G-LRD latents wider than 128 need the group kernel")
     out = _run_fused(cuda, d["q"], d["k_lat"], d["u_k"], d["v_lat"], d["cur_pos"], d["cos"], d["sin"],
                      float(d["scale"]), u_v=d.get("u_v"), out_dtype=out_dtype)
     ref = d["out"]
@@ -109,6 +106,22 @@ def test_mlrd_matches_oracle(cuda, kernel, r_k, r_v, B, S):
     assert_close(out, _bf(ref), f"r_k={r_k} r_v={r_v} B={B} S={S}", per_row=False)
     out32 = _run_fused(cuda, q, k_lat, u_k, v_lat, pos, cos, sin, 128 ** -0.5, out_dtype=torch.float32)
     assert_close(out32, ref, "fp32 out")
+
+
+@pytest.mark.parametrize("r_k,r_v,n_groups", [(256, 256, 2), (160, 224, 8), (64, 256, 8)])
+def test_wide_latents_match_oracle(cuda, r_k, r_v, n_groups):
+    """Latents wider than 128 (BASELINE's G-LRD config: 2 groups of 4 KV heads, rank 256, V rebuilt per
+    head), at a reduced batch and context. They run on the mma.sync kernel with one pipeline stage."""
+    g = torch.Generator().manual_seed(r_k + r_v + n_groups)
+    B, S = 3, 1500
+    q, k_lat, u_k, v_lat, u_v, pos, cos, sin = _inputs(g, B, 8, 32, S, r_k, r_v, n_groups=n_groups,
+                                                      uv=n_groups != 8)
+    gs = 8 // n_groups
+    ref = oracle.reference_decode(q, oracle.expand_groups(k_lat, gs), u_k, oracle.expand_groups(v_lat, gs), pos,
+                                  cos, sin, 128 ** -0.5, u_v=u_v)
+    out = _run_fused(cuda, q, k_lat, u_k, v_lat, pos, cos, sin, 128 ** -0.5, u_v=u_v, out_dtype=torch.float32)
+    assert out.shape == ref.shape
+    assert_close(out, ref, f"r_k={r_k} r_v={r_v} groups={n_groups}")
 
 
 def test_full_context_rows_are_checked_per_row(cuda, kernel):

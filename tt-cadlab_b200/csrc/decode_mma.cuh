@@ -144,10 +144,19 @@ __global__ void __launch_bounds__(kMmaThreads, 2) palu_decode_mma_kernel(const D
   const int lcol = (lane >> 4) * 8;                     // ldmatrix column offset (A / trans-B order)
 
   for (int it = 0; it < my_tiles; ++it) {
-    cp_async_wait<NS - 2>();
-    __syncthreads();
-    if (it + NS - 1 < my_tiles) load_tile(tile0 + it + NS - 1, (it + NS - 1) % NS);
-    cp_async_commit();
+    if constexpr (NS == 1) {
+      // One stage (wide latents): every warp is done with the previous tile before it is overwritten.
+      __syncthreads();
+      load_tile(tile0 + it, 0);
+      cp_async_commit();
+      cp_async_wait<0>();
+      __syncthreads();
+    } else {
+      cp_async_wait<NS - 2>();
+      __syncthreads();
+      if (it + NS - 1 < my_tiles) load_tile(tile0 + it + NS - 1, (it + NS - 1) % NS);
+      cp_async_commit();
+    }
 
     unsigned char* st = sStages + (it % NS) * lay.stage_bytes();
     const uint32_t sK = smem_u32(st), sV = smem_u32(st + lay.k_bytes());

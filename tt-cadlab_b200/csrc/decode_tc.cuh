@@ -197,6 +197,27 @@ PALU_DEVINL void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;
 PALU_DEVINL void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 PALU_DEVINL void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 PALU_DEVINL void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+// tcgen05.ld returns before its registers are written, and the compiler treats an inline-asm load's
+// outputs as ready at once: a register-only use could be scheduled above a plain wait::ld. These waits
+// take the loaded registers as read-write operands, so every use depends on the wait.
+PALU_DEVINL void tmem_wait_ld_regs(uint32_t (&r)[4]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3])::"memory");
+}
+PALU_DEVINL void tmem_wait_ld_regs(uint32_t (&r)[8]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7])::"memory");
+}
+PALU_DEVINL void tmem_wait_ld_regs(uint32_t (&a)[8], uint32_t (&b)[8]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+               : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]),
+                 "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7])::"memory");
+}
+// tcgen05.st may read its source registers after it issues: keep them unmodified until the wait, which
+// takes them as read-write operands so the compiler cannot reuse them earlier.
+PALU_DEVINL void tmem_wait_st_regs(uint32_t (&a)[4], uint32_t (&b)[4]) {
+  asm volatile("tcgen05.wait::st.sync.aligned;\n"
+               : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3])::"memory");
+}
 
 PALU_DEVINL void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -561,7 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t ke[8], ko[8], ae[4], ao[4];
           tmem_ld8(trow + kColDk + 16 * ch + 8 * hc, ke);
           tmem_ld8(trow + kColDk + 64 + 16 * ch + 8 * hc, ko);
-          tmem_wait_ld();
+          tmem_wait_ld_regs(ke, ko);
 #pragma unroll
           for (int x = 0; x < 4; ++x) {
             const uint32_t cw = cs[4 * hc + x], sw = cs[8 + 4 * hc + x];
@@ -588,6 +609,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // f, f + 1); column 32 + the same: the odd dims of those frequencies.
           tmem_st4(trow + kColA + 8 * ch + 4 * hc, ae);
           tmem_st4(trow + kColA + 32 + 8 * ch + 4 * hc, ao);
+          tmem_wait_st_regs(ae, ao);
         }
         if (!ok) break;
       }
@@ -618,7 +640,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_after();
         uint32_t sc[4];
         tmem_ld4(trow + kColDs + (j & 1) * 16, sc);
-        tmem_wait_ld();
+        tmem_wait_ld_regs(sc);
         fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B_SR + 2 * g + (j & 1)));  // D_s[j & 1] may be overwritten
@@ -680,7 +702,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_after();
         uint32_t ov[8];
         tmem_ld8(trow + kColDo + (ja & 1) * 16, ov);
-        tmem_wait_ld();
+        tmem_wait_ld_regs(ov);
 #pragma unroll
         for (int h = 0; h < 4; ++h)
           o_acc[h] = o_acc[h] * ((ja & 1) ? alpha1[h] : alpha0[h]) + __uint_as_float(ov[h]) + __uint_as_float(ov[4 + h]);

@@ -63,11 +63,16 @@ int validate(const palu_decode_dims* d, bool latent, bool has_uv) {
   if (d->n_kv_heads % d->n_groups != 0)
     return fail(PALU_ERR_INVALID, "heads_per_group: %d latent heads do not divide %d KV heads", d->n_groups,
                 d->n_kv_heads);
-  if (d->r_v % 16 != 0 || d->r_v < 16 || d->r_v > 128)
-    return fail(PALU_ERR_INVALID, "r_v must be a multiple of 16 in [16, 128], got %d", d->r_v);
+  // Latent widths: multiples of 16 up to 128, multiples of 32 up to 256 (wider ones run on the mma.sync
+  // kernel with a single pipeline stage).
+  auto rank_ok = [](int r) { return r >= 16 && ((r <= 128 && r % 16 == 0) || (r <= 256 && r % 32 == 0)); };
+  if (!rank_ok(d->r_v))
+    return fail(PALU_ERR_INVALID, "r_v must be a multiple of 16 in [16, 128] or of 32 in (128, 256], got %d",
+                d->r_v);
   if (latent) {
-    if (d->r_k % 16 != 0 || d->r_k < 16 || d->r_k > 128)
-      return fail(PALU_ERR_INVALID, "r_k must be a multiple of 16 in [16, 128], got %d", d->r_k);
+    if (!rank_ok(d->r_k))
+      return fail(PALU_ERR_INVALID, "r_k must be a multiple of 16 in [16, 128] or of 32 in (128, 256], got %d",
+                  d->r_k);
     if (d->n_groups != d->n_kv_heads && !has_uv)
       return fail(PALU_ERR_INVALID, "grouped latents (%d groups for %d KV heads) need u_v", d->n_groups,
                   d->n_kv_heads);
@@ -237,16 +242,23 @@ int run_tc(const void* q, const void* k, const void* v, const void* u_k, int64_t
   return launch_tc<2, 2>(mk, mv, mt, p, stream);
 }
 
-template <int RV16, bool RECON>
-int launch_mma(const palu::DecodeParams& p, cudaStream_t stream) {
-  constexpr int NS = 2;
-  const palu::MmaSmem<RV16, RECON> lay(p.rk);
-  const int bytes = lay.total(NS);
+template <int RV16, bool RECON, int NS>
+int launch_mma_ns(const palu::DecodeParams& p, int bytes, cudaStream_t stream) {
   auto kern = palu::palu_decode_mma_kernel<RV16, RECON, NS>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
     return cuda_check("cudaFuncSetAttribute(decode)");
   kern<<<dim3(p.splits, p.n_kv, p.batch), palu::kMmaThreads, bytes, stream>>>(p);
   return cuda_check("decode kernel launch");
+}
+
+// Two pipeline stages where they fit in shared memory, else one (latents wider than 128).
+template <int RV16, bool RECON>
+int launch_mma(const palu::DecodeParams& p, cudaStream_t stream) {
+  constexpr int kSmemMax = 227 * 1024;
+  const palu::MmaSmem<RV16, RECON> lay(p.rk);
+  if (lay.total(2) <= kSmemMax) return launch_mma_ns<RV16, RECON, 2>(p, lay.total(2), stream);
+  if (lay.total(1) <= kSmemMax) return launch_mma_ns<RV16, RECON, 1>(p, lay.total(1), stream);
+  return fail(PALU_ERR_INVALID, "r_k %d / r_v %d need %d bytes of shared memory", p.rk, p.rv, lay.total(1));
 }
 
 template <bool RECON>
@@ -260,6 +272,10 @@ int dispatch_rv(const palu::DecodeParams& p, cudaStream_t s) {
     case 6: return launch_mma<6, RECON>(p, s);
     case 7: return launch_mma<7, RECON>(p, s);
     case 8: return launch_mma<8, RECON>(p, s);
+    case 10: return launch_mma<10, RECON>(p, s);
+    case 12: return launch_mma<12, RECON>(p, s);
+    case 14: return launch_mma<14, RECON>(p, s);
+    case 16: return launch_mma<16, RECON>(p, s);
   }
   return fail(PALU_ERR_INVALID, "r_v %d unsupported", p.rv);
 }
