@@ -1,0 +1,171 @@
+"""Palu attention layer on B200: the decode path of palu_tt/attention.py's ``PaluAttention``.
+
+Per decode step (attention.py:585-733):
+
+1. q = x @ wq (Meta head order), rotated at each row's position (``rotary_embedding_llama``);
+2. the step's latents h_k = x @ VT_k, h_v = x @ VT_v, one per latent group, appended to the caches at
+   cur_pos (two ``paged_update_cache`` calls, attention.py:612-625 -> ``fused.append_latents``);
+3. the fused op (``ttnn.transformer.palu_sdpa_decode``, attention.py:633-639 -> ``fused.palu_sdpa_decode``):
+   K rebuilt from the latent cache, RoPE, online softmax; V absorbed into ``wo_fused`` (M-LRD) or
+   rebuilt per head from the group latent (G-LRD);
+4. heads concatenated into their head_dim slots, ``@ wo_fused^T``, and with KV heads sharded over ranks,
+   one all-reduce of [B, dim] (attention.py:718-733).
+
+``forward_prefill`` fills the caches for a prompt and returns the prompt's attention output with torch
+SDPA on the rebuilt K / V (the reference runs its prefill on full K / V too, attention.py:382-516).
+
+Weights follow the reference's layout (palu_tt/convert.py): q / K in Meta (interleaved-pair) head order
+so they meet the interleaved RoPE tables, ``u_k`` = U_kᵀ in Meta order, ``wo_fused`` absorbing U_v.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from palu_b200 import fused
+from palu_b200.convert import LowRank, reverse_permute
+from palu_b200.shard import KVShard, all_reduce_layer_output, layer_output_partial
+
+LLAMA3_SCALING = {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+                  "original_max_position_embeddings": 8192}
+
+
+class PaluAttention:
+    """One attention layer with per-head (M-LRD) or per-group (G-LRD) latent K/V caches.
+
+    wq, wo: [dim, n_heads * head_dim] in HF order (as in the checkpoint); ``lowrank``: the layer's
+    factors (``convert.LowRank``: k_VT [n_kv, r_k, dim], k_U [n_kv, head_dim, r_k], v_VT, v_U, with
+    G-LRD groups repeated per head as ``load_palu_dir`` returns them). ``shard`` selects this rank's
+    KV heads (``shard.KVShard``); the layer output is then all-reduced over the default process group.
+    """
+
+    def __init__(self, wq: torch.Tensor, wo: torch.Tensor, lowrank: LowRank, n_heads: int, n_kv_heads: int, *,
+                 max_batch: int, max_seq: int, head_dim: int = 128, rope_theta: float = 500000.0,
+                 rope_scaling: Optional[dict] = LLAMA3_SCALING, shard: Optional[KVShard] = None,
+                 device: str = "cuda", cache_dtype: torch.dtype = torch.bfloat16):
+        if head_dim != fused.HEAD_DIM:
+            raise RuntimeError(f"head_dim must be {fused.HEAD_DIM}, got {head_dim}")
+        gs = lowrank.group_size
+        n_groups = n_kv_heads // gs
+        self.shard = shard or KVShard(0, 1, n_kv_heads, n_heads, n_groups)
+        sh = self.shard
+        self.n_heads, self.n_kv_heads, self.head_dim, self.group_size = n_heads, n_kv_heads, head_dim, gs
+        self.nh, self.nkv, self.ng = len(sh.q), len(sh.kv), len(sh.groups)  # local counts
+        self.max_batch, self.max_seq, self.device = max_batch, max_seq, torch.device(device)
+        self.r_k, self.r_v = lowrank.r_k, lowrank.r_v
+        self.grouped = gs > 1
+        dim = wq.shape[1]
+        self.dim = dim
+        dev, bf = self.device, torch.bfloat16
+
+        qs, ks = sh.q, sh.kv
+        wq_meta = reverse_permute(wq.float(), n_heads, n_heads * head_dim, dim)
+        # Projections are kept (and applied) in fp32: the checkpoint values are exact in it, and the only
+        # rounding left on the path is the bf16 of q and of the cached latents, as on the device.
+        f32 = torch.float32
+        self.wq = wq_meta[qs.start * head_dim:qs.stop * head_dim].to(dev, f32)           # [nh*hd, dim]
+        # one latent projection per local group: the group's first head carries its VT (convert.py:266-276)
+        first = [g * gs for g in sh.groups]
+        self.wk_lat = torch.cat([lowrank.k_VT[h].float() for h in first]).to(dev, f32)  # [ng*r_k, dim]
+        self.wv_lat = torch.cat([lowrank.v_VT[h].float() for h in first]).to(dev, f32)  # [ng*r_v, dim]
+        u_k = torch.stack([reverse_permute(lowrank.k_U[h].float(), 1, head_dim, self.r_k).T for h in ks])
+        self.u_k = u_k.to(dev, bf)                                                        # [nkv, r_k, hd]
+        self.w_rot = fused.w_rot_from_u_k(u_k)[None].to(dev, bf)                          # [1, nkv, r_k, 2hd]
+        # fp32 copies of U for the prefill path (K / V rebuilt over the prompt)
+        self._u_k32 = u_k.to(dev)
+        self._u_v32 = torch.stack([lowrank.v_U[h].float().T for h in ks]).to(dev)          # [nkv, r_v, hd]
+        wo = wo.float()
+        cols = slice(qs.start * head_dim, qs.stop * head_dim)
+        if self.grouped:
+            self.u_v = self._u_v32[None].to(bf)                                            # [1, nkv, r_v, hd]
+            self.wo = wo[:, cols].to(dev, f32)
+            self.head_dim_v = head_dim
+        else:
+            # M-LRD: the attention output stays in latent space; U_v folds into wo (convert.py:278-286)
+            rep = n_heads // n_kv_heads
+            wf = torch.zeros(dim, self.nh * head_dim)
+            for i, qh in enumerate(qs):
+                blk = wo[:, qh * head_dim:(qh + 1) * head_dim] @ lowrank.v_U[qh // rep].float()
+                wf[:, i * head_dim:i * head_dim + self.r_v] = blk
+            self.u_v = None
+            self.wo = wf.to(dev, f32)
+            self.head_dim_v = self.r_v
+
+        cos, sin = fused.cos_sin_tables(head_dim, max_seq, rope_theta, rope_scaling)
+        self.cos, self.sin = cos.to(dev), sin.to(dev)                                      # fp32 [>= S, hd]
+        self.cs_tab = fused.cs_table(cos, sin, max_seq)[None, None].to(dev, bf)           # [1, 1, S, 2hd]
+        self.k_cache = torch.zeros(max_batch, self.ng, max_seq, self.r_k, dtype=cache_dtype, device=dev)
+        self.v_cache = torch.zeros(max_batch, self.ng, max_seq, self.r_v, dtype=cache_dtype, device=dev)
+        self.scale = head_dim ** -0.5
+        # The two device ops of a decode step (the CUDA library; the tests substitute CPU models here to
+        # check the layer algebra on a machine without a GPU).
+        self.append_op = fused.append_latents
+        self.attend_op = fused.palu_sdpa_decode
+
+    # ---- RoPE on q (Meta-interleaved pairs, rotary_embedding_llama) ----------------------------------
+    def _rotate(self, t: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        """t [..., n, hd] fp32 at positions pos (broadcast over the head axis): pairs (2j, 2j+1) rotate by
+        pos * f_j."""
+        c = self.cos[pos].unsqueeze(-2)
+        s = self.sin[pos].unsqueeze(-2)
+        tr = torch.stack([-t[..., 1::2], t[..., 0::2]], dim=-1).flatten(-2)  # (-x1, x0) per pair
+        return t * c + tr * s
+
+    def _out(self, attn: torch.Tensor) -> torch.Tensor:
+        """[B, nh_local, w] attention output -> [B, dim] layer output (summed over ranks)."""
+        y = layer_output_partial(attn, self.wo)
+        return all_reduce_layer_output(y) if self.shard.world > 1 else y
+
+    @torch.no_grad()
+    def forward_decode(self, x: torch.Tensor, current_pos: torch.Tensor) -> torch.Tensor:
+        """x [B, dim] or [1, 1, B, dim]; current_pos [B] ints (each row's position; < 0 skips the row).
+        Returns the layer output in x's layout, fp32."""
+        shape4 = x.dim() == 4
+        xb = (x.reshape(-1, x.shape[-1]) if shape4 else x).to(self.device, torch.float32)
+        B = xb.shape[0]
+        if B > self.max_batch:
+            raise RuntimeError(f"batch {B} exceeds the cache's {self.max_batch} rows")
+        pos = current_pos.to(self.device, torch.int32).reshape(B)
+        q = (xb @ self.wq.T).view(B, self.nh, self.head_dim)
+        q = self._rotate(q, pos.clamp(min=0).long()).to(torch.bfloat16)
+        k_new = (xb @ self.wk_lat.T).view(B, self.ng, self.r_k).to(self.k_cache.dtype)
+        v_new = (xb @ self.wv_lat.T).view(B, self.ng, self.r_v).to(self.v_cache.dtype)
+        kc, vc = self.k_cache[:B], self.v_cache[:B]
+        self.append_op(k_new, v_new, pos, kc, vc)
+        attn = self.attend_op(q[None], kc, self.w_rot, self.cs_tab, vc, self.head_dim_v, pos, u_v=self.u_v,
+                                      scale=self.scale, out_dtype=torch.float32)[0]
+        y = self._out(attn)
+        return y.view(1, 1, B, self.dim) if shape4 else y
+
+    @torch.no_grad()
+    def forward_prefill(self, x: torch.Tensor, user_id: Optional[int] = None) -> torch.Tensor:
+        """Prompt of P tokens at positions 0..P-1: x [B, P, dim] (cache rows 0..B-1), or [1, 1, P, dim] for
+        cache row ``user_id`` (the reference's per-user prefill). Writes the prompt's latents into the
+        caches and returns its causal attention output (fp32, x's layout) computed with torch SDPA on K and
+        V rebuilt from the cached (bf16) latents."""
+        shape4 = x.dim() == 4
+        xb = (x.reshape(1, x.shape[-2], x.shape[-1]) if shape4 else x).to(self.device, torch.float32)
+        B, P, _ = xb.shape
+        rows = slice(user_id, user_id + 1) if shape4 else slice(0, B)
+        if P > self.max_seq or rows.stop > self.max_batch:
+            raise RuntimeError(f"prompt of {P} tokens / cache rows {rows} exceed the cache")
+        lat_k = (xb @ self.wk_lat.T).view(B, P, self.ng, self.r_k).transpose(1, 2)
+        lat_v = (xb @ self.wv_lat.T).view(B, P, self.ng, self.r_v).transpose(1, 2)
+        self.k_cache[rows, :, :P] = lat_k.to(self.k_cache.dtype)
+        self.v_cache[rows, :, :P] = lat_v.to(self.v_cache.dtype)
+        gs_local = self.nkv // self.ng
+        rep = self.nh // self.nkv
+        lk = self.k_cache[rows, :, :P].float().repeat_interleave(gs_local, dim=1)        # [B, nkv, P, r_k]
+        lv = self.v_cache[rows, :, :P].float().repeat_interleave(gs_local, dim=1)
+        K = torch.einsum("bhpr,hrd->bhpd", lk, self._u_k32)
+        V = torch.einsum("bhpr,hrd->bhpd", lv, self._u_v32) if self.grouped else lv
+        p_idx = torch.arange(P, device=self.device)
+        K = self._rotate(K.transpose(1, 2), p_idx[None]).transpose(1, 2)                # [B, nkv, P, hd]
+        q = (xb @ self.wq.T).view(B, P, self.nh, self.head_dim)
+        q = self._rotate(q, p_idx[None]).transpose(1, 2)                               # [B, nh, P, hd]
+        attn = torch.nn.functional.scaled_dot_product_attention(
+            q, K.repeat_interleave(rep, dim=1), V.repeat_interleave(rep, dim=1), is_causal=True, scale=self.scale)
+        attn = attn.transpose(1, 2).reshape(B * P, self.nh, -1)
+        y = self._out(attn).view(B, P, self.dim)
+        return y.view(1, 1, P, self.dim) if shape4 else y
