@@ -54,8 +54,8 @@ typedef struct palu_decode_dims {
   int32_t n_kv_heads; /* KV heads */
   int32_t n_groups;   /* latent heads in the caches: n_kv_heads (M-LRD) or n_kv_heads / group size (G-LRD) */
   int32_t head_dim;   /* must be 128 */
-  int32_t r_k;        /* K latent width (multiple of 16) */
-  int32_t r_v;        /* V latent width (multiple of 16) */
+  int32_t r_k;        /* K latent width: a multiple of 16 up to 128, or of 32 up to 256 */
+  int32_t r_v;        /* V latent width: a multiple of 16 up to 128, or of 32 up to 256 */
   int32_t max_seq;    /* cache rows per (batch row, latent head) */
   int32_t splits;     /* split-K partitions per (batch row, KV head); 0 = choose for this GPU */
 } palu_decode_dims;
@@ -126,7 +126,7 @@ int palu_plain_gqa_decode(const void* q, const void* k, const void* v, const int
 
 /*
  * Pack the reference's [rows][ld] [cos | sin] table (bf16 or fp32, pair-duplicated frequency
- * columns: cos_j at column 2j, sin_j at 128 + 2j) into rows of 128 bf16 (= 64 32-bit words): 4 blocks
+ * columns: cos_j at column 2j, sin_j at 128 + 2j) into rows of 128 fp16 (= 64 32-bit words): 4 blocks
  * of 16 frequencies, each block the 16 cosines (frequency order) followed by the same 16 sines.
  */
 int palu_pack_cs_table(const void* cs_tab, int64_t ld, int32_t in_dtype, void* cs_pairs, int32_t rows,

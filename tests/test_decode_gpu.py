@@ -233,9 +233,9 @@ def test_pack_cs_table_is_exact(cuda, dtype):
     cos, sin = oracle.cos_sin_tables(128, 700, THETA, LLAMA3)
     tab = oracle.cs_table(cos, sin, 700).to(dtype)
     packed = fused.pack_cs_table(tab[None, None].to(cuda)).cpu()
-    # per row: 4 blocks of 16 frequencies, each 16 bf16 cosines then their 16 sines
-    c = tab[:, 0:128:2].to(torch.bfloat16).reshape(700, 4, 16)
-    s = tab[:, 128::2].to(torch.bfloat16).reshape(700, 4, 16)
+    # per row: 4 blocks of 16 frequencies, each 16 fp16 cosines then their 16 sines
+    c = tab[:, 0:128:2].to(torch.float16).reshape(700, 4, 16)
+    s = tab[:, 128::2].to(torch.float16).reshape(700, 4, 16)
     want = torch.cat([c, s], dim=-1).reshape(700, 128).view(torch.int32)
     assert torch.equal(packed, want)
 

@@ -18,6 +18,8 @@
 // The semantics follow the reference's fp32 model of palu_sdpa_decode (palu_tt/fused.py:82-107):
 // query head qh attends KV head qh / rep; position p is visible iff p <= cur_pos[b].
 #pragma once
+#include <cuda_fp16.h>
+
 #include "palu_common.cuh"
 
 namespace palu {
@@ -180,13 +182,13 @@ __global__ void __launch_bounds__(kMmaThreads, 2) palu_decode_mma_kernel(const D
       }
       // RoPE: K_rot[2j] = K[2j] cos - K[2j+1] sin ; K_rot[2j+1] = K[2j+1] cos + K[2j] sin.
       const uint32_t* sT = reinterpret_cast<const uint32_t*>(st + lay.k_bytes() + MmaSmem<RV16, RECON>::v_bytes);
-      const __nv_bfloat16* t0 = reinterpret_cast<const __nv_bfloat16*>(sT + (warp * 16 + g) * kCsLd);
-      const __nv_bfloat16* t1 = t0 + 16 * kCsLd;
+      const __half* t0 = reinterpret_cast<const __half*>(sT + (warp * 16 + g) * kCsLd);
+      const __half* t1 = t0 + 16 * kCsLd;
 #pragma unroll
       for (int n = 0; n < 16; ++n) {
         const int f = 4 * n + t;  // frequency pair of this thread's two accumulator columns
-        const float2 c0 = make_float2(__bfloat162float(t0[packed_cos_index(f)]), __bfloat162float(t0[packed_sin_index(f)]));
-        const float2 c1 = make_float2(__bfloat162float(t1[packed_cos_index(f)]), __bfloat162float(t1[packed_sin_index(f)]));
+        const float2 c0 = make_float2(__half2float(t0[packed_cos_index(f)]), __half2float(t0[packed_sin_index(f)]));
+        const float2 c1 = make_float2(__half2float(t1[packed_cos_index(f)]), __half2float(t1[packed_sin_index(f)]));
         const float k0 = acc[n][0], k1 = acc[n][1], k2 = acc[n][2], k3 = acc[n][3];
         acc[n][0] = k0 * c0.x - k1 * c0.y;
         acc[n][1] = k1 * c0.x + k0 * c0.y;

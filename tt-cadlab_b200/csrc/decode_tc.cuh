@@ -9,11 +9,11 @@
 // of its SMSP quarter: 32 token rows of the tile, or 32 latent dims of the PV output).
 // At start the softmax warps stage Q^T (fp16) and the RoPE warps U_k (bf16) in shared memory with their
 // head dims reordered as [even dims | odd dims], so that D_k holds each rotation pair (2f, 2f+1) in columns
-// f and 64 + f and the rotation of two adjacent frequencies is one packed fp32x2 operation.
+// f and 64 + f and the rotation of two adjacent frequencies is one packed half2 operation.
 // Per group-local tile j (tile t = g + 2 j):
 //   MMA      D_k[128 tok x 128 dim] (f32) = lat_k (smem, K-major) x U_k (smem, MN-major)
-//   RoPE     K row -> rotate in registers from the table -> K_rot as fp16 into its own TMEM columns: the A
-//            operand of QK (fp16 keeps 11 significant bits; q is bf16, exact in fp16)
+//   RoPE     K row -> fp16, rotated in half2 arithmetic with the fp16 table -> K_rot into its own TMEM
+//            columns: the A operand of QK (fp16 keeps 11 significant bits; q is bf16, exact in fp16)
 //   MMA      D_s[128 tok x 16] (f32) = K_rot (TMEM) x Q^T (smem, fp16)
 //   softmax  online softmax over the query heads (exp2 domain); P^T as bf16 hi + lo -> smem
 //   MMA      D_o[128 lat x 16] (f32) = V^T (smem, MN-major: the V tile exactly as TMA wrote it) x P^T
@@ -214,10 +214,13 @@ PALU_DEVINL void tmem_wait_ld_regs(uint32_t (&a)[8], uint32_t (&b)[8]) {
 }
 // tcgen05.st may read its source registers after it issues: keep them unmodified until the wait, which
 // takes them as read-write operands so the compiler cannot reuse them earlier.
-PALU_DEVINL void tmem_wait_st_regs(uint32_t (&a)[4], uint32_t (&b)[4]) {
+PALU_DEVINL void tmem_wait_st_regs(uint32_t (&a)[4], uint32_t (&b)[4], uint32_t (&c)[4], uint32_t (&d)[4]) {
   asm volatile("tcgen05.wait::st.sync.aligned;\n"
-               : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3])::"memory");
+               : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]),
+                 "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3]), "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])::"memory");
 }
+PALU_DEVINL __half2 u32_as_half2(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
+PALU_DEVINL uint32_t half2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
 PALU_DEVINL void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -564,7 +567,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         // SWIZZLE_64B rows of 64 B: 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3). Words 0..7:
-        // cos of frequency pairs (f, f+1), words 8..15: their sines (bf16, low half first).
+        // cos of frequency pairs (f, f+1), words 8..15: their sines (fp16, low half first).
         const unsigned char* tb = smem + Lay::OFF_TAB + sb * Lay::TCH_BYTES + row * 64;
         uint32_t cs[16];
 #pragma unroll
@@ -577,24 +580,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();  // every lane has read its table values: the slot may refill
         if (lane == 0) mbar_arrive(bar(B_TE + sb));
+        uint32_t ae[2][4], ao[2][4];  // per half chunk: the stores of half 0 overlap the math of half 1
 #pragma unroll
         for (int hc = 0; hc < 2; ++hc) {  // 8 frequencies per half chunk
-          uint32_t ke[8], ko[8], ae[4], ao[4];
+          uint32_t ke[8], ko[8];
           tmem_ld8(trow + kColDk + 16 * ch + 8 * hc, ke);
           tmem_ld8(trow + kColDk + 64 + 16 * ch + 8 * hc, ko);
           tmem_wait_ld_regs(ke, ko);
 #pragma unroll
           for (int x = 0; x < 4; ++x) {
-            const uint32_t cw = cs[4 * hc + x], sw = cs[8 + 4 * hc + x];
-            const float2 c = make_float2(__uint_as_float(cw << 16), __uint_as_float(cw & 0xFFFF0000u));
-            const float2 sn = make_float2(__uint_as_float(sw << 16), __uint_as_float(sw & 0xFFFF0000u));
-            const float2 e = make_float2(__uint_as_float(ke[2 * x]), __uint_as_float(ke[2 * x + 1]));
-            const float2 o = make_float2(__uint_as_float(ko[2 * x]), __uint_as_float(ko[2 * x + 1]));
+            // half2 math on two adjacent frequencies: K to fp16 first (the A operand is fp16 anyway), then
             // rot(2f) = k(2f) cos - k(2f+1) sin ; rot(2f+1) = k(2f+1) cos + k(2f) sin
-            const float2 re = __ffma2_rn(o, make_float2(-sn.x, -sn.y), __fmul2_rn(e, c));
-            const float2 ro = __ffma2_rn(e, sn, __fmul2_rn(o, c));
-            ae[x] = pack_half2(re.x, re.y);
-            ao[x] = pack_half2(ro.x, ro.y);
+            const __half2 c = u32_as_half2(cs[4 * hc + x]), sn = u32_as_half2(cs[8 + 4 * hc + x]);
+            const __half2 e = __floats2half2_rn(__uint_as_float(ke[2 * x]), __uint_as_float(ke[2 * x + 1]));
+            const __half2 o = __floats2half2_rn(__uint_as_float(ko[2 * x]), __uint_as_float(ko[2 * x + 1]));
+            ae[hc][x] = half2_as_u32(__hfma2(__hneg2(o), sn, __hmul2(e, c)));
+            ao[hc][x] = half2_as_u32(__hfma2(e, sn, __hmul2(o, c)));
           }
           if (ch == 0 && hc == 0 && i >= 1) {
             // A still feeds QK(i - 1) until that MMA completes; its commit is the scores barrier.
@@ -607,10 +608,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           // A column 8 ch + 4 hc + x: K_rot dims (2f, 2f + 2) of f = 16 ch + 8 hc + 2x (reordered elements
           // f, f + 1); column 32 + the same: the odd dims of those frequencies.
-          tmem_st4(trow + kColA + 8 * ch + 4 * hc, ae);
-          tmem_st4(trow + kColA + 32 + 8 * ch + 4 * hc, ao);
-          tmem_wait_st_regs(ae, ao);
+          tmem_st4(trow + kColA + 8 * ch + 4 * hc, ae[hc]);
+          tmem_st4(trow + kColA + 32 + 8 * ch + 4 * hc, ao[hc]);
         }
+        if (ok) tmem_wait_st_regs(ae[0], ao[0], ae[1], ao[1]);
         if (!ok) break;
       }
       if (!ok) break;

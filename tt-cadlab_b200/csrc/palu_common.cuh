@@ -50,7 +50,7 @@ PALU_DEVINL void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Packed RoPE table rows (palu_pack_cs_kernel): 128 bf16 per position, 4 blocks of 16 frequencies,
+// Packed RoPE table rows (palu_pack_cs_kernel): 128 fp16 per position, 4 blocks of 16 frequencies,
 // each block 16 cosines then the same 16 frequencies' sines. Element index of cos / sin of frequency f:
 PALU_DEVINL int packed_cos_index(int f) { return 32 * (f >> 4) + (f & 15); }
 PALU_DEVINL int packed_sin_index(int f) { return 32 * (f >> 4) + 16 + (f & 15); }

@@ -113,7 +113,7 @@ _PACK_CACHE: dict = {}
 
 
 def pack_cs_table(cs_tab: torch.Tensor) -> torch.Tensor:
-    """[.., S, 256] [cos | sin] (bf16 or fp32, CUDA) -> [S, 64] int32 rows of packed bf16 (per row 4 blocks
+    """[.., S, 256] [cos | sin] (bf16 or fp32, CUDA) -> [S, 64] int32 rows of packed fp16 (per row 4 blocks
     of 16 frequencies: 16 cosines, then the same frequencies' sines),
     computed by the library's pack kernel and cached while the table tensor is unchanged."""
     _lib.require_cuda(cs_tab)
