@@ -219,6 +219,18 @@ PALU_DEVINL void tmem_wait_st_regs(uint32_t (&a)[4], uint32_t (&b)[4], uint32_t 
                : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]),
                  "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3]), "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])::"memory");
 }
+PALU_DEVINL void tmem_wait_ld_regs(uint32_t (&a)[16], uint32_t (&b)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+               : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]),
+                 "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]), "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15]),
+                 "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7]),
+                 "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]), "+r"(b[12]), "+r"(b[13]), "+r"(b[14]), "+r"(b[15])::"memory");
+}
+PALU_DEVINL void tmem_wait_st_regs(uint32_t (&a)[8], uint32_t (&b)[8]) {
+  asm volatile("tcgen05.wait::st.sync.aligned;\n"
+               : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]),
+                 "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7])::"memory");
+}
 PALU_DEVINL __half2 u32_as_half2(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
 PALU_DEVINL uint32_t half2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
@@ -562,7 +574,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int ch = 0; ch < 4; ++ch) {
         const int n = i * 4 + ch, sb = g * T_SLOTS + n % T_SLOTS;
+        // The chunk's D_k columns load while this warp waits for and reads its table chunk.
+        uint32_t ke[16], ko[16];
+        tmem_ld16(trow + kColDk + 16 * ch, ke);
+        tmem_ld16(trow + kColDk + 64 + 16 * ch, ko);
         if (!mbar_wait(bar(B_TF + sb), (n / T_SLOTS) & 1, s_abort, p.status)) {
+          tmem_wait_ld_regs(ke, ko);
           ok = false;
           break;
         }
@@ -580,38 +597,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();  // every lane has read its table values: the slot may refill
         if (lane == 0) mbar_arrive(bar(B_TE + sb));
-        uint32_t ae[2][4], ao[2][4];  // per half chunk: the stores of half 0 overlap the math of half 1
+        tmem_wait_ld_regs(ke, ko);
+        uint32_t ae[8], ao[8];
 #pragma unroll
-        for (int hc = 0; hc < 2; ++hc) {  // 8 frequencies per half chunk
-          uint32_t ke[8], ko[8];
-          tmem_ld8(trow + kColDk + 16 * ch + 8 * hc, ke);
-          tmem_ld8(trow + kColDk + 64 + 16 * ch + 8 * hc, ko);
-          tmem_wait_ld_regs(ke, ko);
-#pragma unroll
-          for (int x = 0; x < 4; ++x) {
-            // half2 math on two adjacent frequencies: K to fp16 first (the A operand is fp16 anyway), then
-            // rot(2f) = k(2f) cos - k(2f+1) sin ; rot(2f+1) = k(2f+1) cos + k(2f) sin
-            const __half2 c = u32_as_half2(cs[4 * hc + x]), sn = u32_as_half2(cs[8 + 4 * hc + x]);
-            const __half2 e = __floats2half2_rn(__uint_as_float(ke[2 * x]), __uint_as_float(ke[2 * x + 1]));
-            const __half2 o = __floats2half2_rn(__uint_as_float(ko[2 * x]), __uint_as_float(ko[2 * x + 1]));
-            ae[hc][x] = half2_as_u32(__hfma2(__hneg2(o), sn, __hmul2(e, c)));
-            ao[hc][x] = half2_as_u32(__hfma2(e, sn, __hmul2(o, c)));
-          }
-          if (ch == 0 && hc == 0 && i >= 1) {
-            // A still feeds QK(i - 1) until that MMA completes; its commit is the scores barrier.
-            const int jq = i - 1;
-            if (!mbar_wait(bar(B_SF + 2 * g + (jq & 1)), (jq >> 1) & 1, s_abort, p.status)) {
-              ok = false;
-              break;
-            }
-            fence_after();
-          }
-          // A column 8 ch + 4 hc + x: K_rot dims (2f, 2f + 2) of f = 16 ch + 8 hc + 2x (reordered elements
-          // f, f + 1); column 32 + the same: the odd dims of those frequencies.
-          tmem_st4(trow + kColA + 8 * ch + 4 * hc, ae[hc]);
-          tmem_st4(trow + kColA + 32 + 8 * ch + 4 * hc, ao[hc]);
+        for (int x = 0; x < 8; ++x) {
+          // half2 math on two adjacent frequencies: K to fp16 first (the A operand is fp16 anyway), then
+          // rot(2f) = k(2f) cos - k(2f+1) sin ; rot(2f+1) = k(2f+1) cos + k(2f) sin
+          const __half2 c = u32_as_half2(cs[x]), sn = u32_as_half2(cs[8 + x]);
+          const __half2 e = __floats2half2_rn(__uint_as_float(ke[2 * x]), __uint_as_float(ke[2 * x + 1]));
+          const __half2 o = __floats2half2_rn(__uint_as_float(ko[2 * x]), __uint_as_float(ko[2 * x + 1]));
+          ae[x] = half2_as_u32(__hfma2(__hneg2(o), sn, __hmul2(e, c)));
+          ao[x] = half2_as_u32(__hfma2(e, sn, __hmul2(o, c)));
         }
-        if (ok) tmem_wait_st_regs(ae[0], ao[0], ae[1], ao[1]);
+        if (ch == 0 && i >= 1) {
+          // A still feeds QK(i - 1) until that MMA completes; its commit is the scores barrier.
+          const int jq = i - 1;
+          if (!mbar_wait(bar(B_SF + 2 * g + (jq & 1)), (jq >> 1) & 1, s_abort, p.status)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+        }
+        // A column 8 ch + x: K_rot dims (2f, 2f + 2) of f = 16 ch + 2x (reordered elements f, f + 1);
+        // column 32 + the same: the odd dims of those frequencies.
+        tmem_st8(trow + kColA + 8 * ch, ae);
+        tmem_st8(trow + kColA + 32 + 8 * ch, ao);
+        tmem_wait_st_regs(ae, ao);
         if (!ok) break;
       }
       if (!ok) break;
