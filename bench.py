@@ -207,7 +207,7 @@ def workload_config(ws, batch=B_PER_GPU):
     return {"workload": name, "model": "Llama-3.1-8B attention layer (M-LRD, absorbed V)",
             "global_batch": batch * ws, "seq_len": S, "rank_k": R, "rank_v": R, "n_q_heads": N_Q,
             "n_kv_heads": N_KV, "kv_heads_per_gpu": N_KV // ws, "parallelism": f"kv-head shard x{ws}",
-            "l2": f"no flush: each step reads {batch * (N_KV // ws) * S * 2 * R * 2 / 1e6:.0f} MB of latents per GPU "
+            "l2": f"no flush: each step reads {batch * ws * (N_KV // ws) * S * 2 * R * 2 / 1e6:.0f} MB of latents per GPU "
                   f"(L2 is 126 MB)"}
 
 
