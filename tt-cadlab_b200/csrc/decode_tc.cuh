@@ -3,7 +3,7 @@
 // One CTA owns (batch row b, KV head h, split s): a contiguous range of 128-token tiles of the positions
 // 0..cur_pos[b]. Two groups work on alternate tiles (group g on tiles t with t % 2 == g), so two tiles are in
 // flight per CTA. Each group has its own warps, rings, barriers and TMEM columns (24 warps in all, see
-// role_of): a K+table TMA producer, a V producer, a QK issuer, a reconstruct+PV issuer (a single thread
+// role_of): a K+table TMA producer, a V producer, a QK+PV issuer, a reconstruct issuer (a single thread
 // issues at most one tcgen05.mma per ~64 cycles whatever its shape, measured on B200, so the MMAs are
 // split over two threads), 4 RoPE warps and 4 softmax warps (a warp of either kind owns the 32 TMEM lanes
 // of its SMSP quarter: 32 token rows of the tile, or 32 latent dims of the PV output).
@@ -11,15 +11,17 @@
 // head dims reordered as [even dims | odd dims], so that D_k holds each rotation pair (2f, 2f+1) in columns
 // f and 64 + f and the rotation of two adjacent frequencies is one packed half2 operation.
 // Per group-local tile j (tile t = g + 2 j):
-//   MMA      D_k[128 tok x 128 dim] (f32) = lat_k (smem, K-major) x U_k (smem, MN-major)
+//   MMA      D_k[128 tok x 128 dim] (f32) = lat_k (smem, K-major) x U_k (smem, MN-major), as two N = 64 halves
+//            (frequencies 0..31 and 32..63, each half its even dims then its odd dims)
 //   RoPE     K row -> fp16, rotated in half2 arithmetic with the fp16 table -> K_rot into its own TMEM
 //            columns: the A operand of QK (fp16 keeps 11 significant bits; q is bf16, exact in fp16)
 //   MMA      D_s[128 tok x 16] (f32) = K_rot (TMEM) x Q^T (smem, fp16)
 //   softmax  online softmax over the query heads (exp2 domain); P^T as bf16 hi + lo -> smem
 //   MMA      D_o[128 lat x 16] (f32) = V^T (smem, MN-major: the V tile exactly as TMA wrote it) x P^T
 //   softmax  thread c (latent dim c) accumulates O[h][c] = O * alpha + hi + lo in registers
-// The reconstruction of tile j + 1 is issued as soon as RoPE(j) has read D_k; RoPE(j + 1) then overlaps
-// softmax(j) and PV(j - 1). D_s, D_o and P are double-buffered by j % 2, and every consumer releases what
+// RoPE works by halves of D_k: as soon as RoPE(j) has finished half h, the reconstruction of half h of
+// tile j + 1 and the QK MMAs of half h of tile j are issued, so the reconstruct latency overlaps the
+// rotation of the other half; RoPE(j + 1) overlaps softmax(j) and PV(j - 1). D_s, D_o and P are double-buffered by j % 2, and every consumer releases what
 // it read with its own barrier, so no barrier runs two phases ahead of a waiter. The two groups merge
 // their (m, l, O) at the end into one split partial (combine.cuh merges the splits). Every wait is bounded
 // (1 s of globaltimer): on expiry the CTA records a status code, all roles stop, copies and MMAs in flight
@@ -38,12 +40,11 @@ constexpr int kTile = 128;
 constexpr int kBox = 16384;             // one TMA box: 128 rows x 128 B
 constexpr int kTmemCols = 512;
 constexpr int kGrpCols = 256;           // TMEM columns reserved per softmax group
-constexpr int kColDk = 0;               // 128 columns: f32 K tile, dims [even | odd] (reconstruct output)
+constexpr int kColDk = 0;               // 128 columns: f32 K tile, two halves of [even | odd] dims (reconstruct output)
 constexpr int kColA = 128;              // 64 columns: fp16 K_rot, the A operand of QK (packed 2 per column)
 constexpr int kColDs = 192;             // 2 x 16 columns: scores, double-buffered
 constexpr int kColDo = 224;             // 2 x 16 columns: PV result, double-buffered
 constexpr unsigned long long kWaitNs = 1000000000ull;  // bound on any single wait
-constexpr uint32_t kSuspendHintNs = 0x989680;          // mbarrier try_wait suspend-time hint
 
 enum : int { kStatusOk = 0, kStatusTimeout = 1 };
 
@@ -102,9 +103,9 @@ PALU_DEVINL void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
 PALU_DEVINL bool mbar_try(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
+      : "r"(bar), "r"(parity)
       : "memory");
   return ok != 0;
 }
@@ -301,8 +302,8 @@ PALU_DEVINL void tmem_st4(uint32_t taddr, const uint32_t (&r)[4]) {
 }
 
 // Warp roles (24 warps). Warps 0..7 are single-lane role warps, two per SMSP (warp w runs on SMSP w % 4):
-//   group 0: 0 = K+table producer, 1 = QK issuer, 2 = reconstruct+PV issuer, 3 = V producer
-//   group 1: 4 = QK issuer, 5 = K+table producer, 6 = V producer, 7 = reconstruct+PV issuer
+//   group 0: 0 = K+table producer, 1 = QK+PV issuer, 2 = reconstruct issuer, 3 = V producer
+//   group 1: 4 = QK+PV issuer, 5 = K+table producer, 6 = V producer, 7 = reconstruct issuer
 // Warps 8..15: RoPE warps (group (w - 8) / 4), warps 16..23: softmax warps (group (w - 16) / 4); warp w of
 // either kind owns TMEM lanes 32 (w % 4) .. + 31, i.e. token rows (tile) or latent dims (PV output).
 enum : int { kRoleKT = 0, kRoleQK = 1, kRoleRP = 2, kRoleV = 3 };
@@ -346,7 +347,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto bar = [&](int i) { return smem_u32(bars + i); };
   // [g][x] pairs are double-buffered by the group-local tile index parity x.
   constexpr int B_KF = 0, B_KE = B_KF + NS_K, B_VF = B_KE + NS_K, B_VE = B_VF + NS_V, B_TF = B_VE + NS_V,
-                B_TE = B_TF + NS_T, B_UF = B_TE + NS_T, B_REC = B_UF + 1, B_AF = B_REC + 2, B_SF = B_AF + 2,
+                B_TE = B_TF + NS_T, B_UF = B_TE + NS_T, B_REC = B_UF + 1, B_AF = B_REC + 4, B_AE = B_AF + 4,
+                B_SF = B_AE + 2,
                 B_SR = B_SF + 4, B_PF = B_SR + 4, B_OF = B_PF + 4, B_OR = B_OF + 4, B_MX = B_OR + 4,
                 B_DRAIN = B_MX + 4, B_COUNT = B_DRAIN + 4;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + B_COUNT);
@@ -370,8 +372,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(bar(B_UF), 8);  // the 8 RoPE warps stage U_k
     for (int g = 0; g < 2; ++g) {
-      mbar_init(bar(B_REC + g), 1);
-      mbar_init(bar(B_AF + g), 4);
+      mbar_init(bar(B_AE + g), 1);
+      for (int h = 0; h < 2; ++h) {
+        mbar_init(bar(B_REC + 2 * g + h), 1);
+        mbar_init(bar(B_AF + 2 * g + h), 4);
+      }
       for (int x = 0; x < 2; ++x) {
         mbar_init(bar(B_SF + 2 * g + x), 1);
         mbar_init(bar(B_SR + 2 * g + x), 4);
@@ -481,42 +486,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tg = tmem + g * kGrpCols;
         const int drain = B_DRAIN + 2 * g + (role == kRoleQK ? 0 : 1);
         if (role == kRoleQK) {
-          // ---- QK(j): D_s[j & 1] = K_rot (TMEM, fp16) x Q^T, once RoPE(j) wrote A and softmax(j - 2) read D_s.
+          // ---- QK(j): D_s[j & 1] = K_rot (TMEM, fp16) x Q^T in two halves, half h once RoPE(j) wrote A half h
+          // (and, first, once softmax(j - 2) read D_s[j & 1]); then PV(j - 1) once softmax(j - 1) wrote P.
           constexpr uint32_t ID_QK = idesc_f16(16, 0, false, false);
+          constexpr uint32_t ID_PV = idesc_f16(16, 1, true, false);  // bf16 V^T (MN-major) x bf16 P
           const uint32_t sQ = sbase + Lay::OFF_Q;
-          for (int j = 0; j < n_g; ++j) {
-            if (!mbar_wait(bar(B_AF + g), j & 1, s_abort, p.status)) break;
-            if (j >= 2 && !mbar_wait(bar(B_SR + 2 * g + (j & 1)), ((j >> 1) - 1) & 1, s_abort, p.status)) break;
-            fence_after();
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)  // K = 16 fp16 (32 bytes, 8 TMEM columns) per MMA
-              mma_ts(tg + kColDs + (j & 1) * 16, tg + kColA + kk * 8,
-                     sdesc(sQ + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), ID_QK, kk > 0);
-            mma_commit(bar(B_SF + 2 * g + (j & 1)));
-          }
-        } else {
-          // ---- reconstruct(j + 1) once RoPE(j) has read D_k; PV(j - 1) once softmax(j - 1) wrote P.
-          constexpr uint32_t ID_REC = idesc_f16(128, 1, false, true);  // bf16 lat x bf16 U (MN-major)
-          constexpr uint32_t ID_PV = idesc_f16(16, 1, true, false);    // bf16 V^T (MN-major) x bf16 P
-          const uint32_t sU = sbase + Lay::OFF_U;
-          const uint32_t u_lbo = p.rk * 128;            // U: stride between the two 64-dim N-blocks
           const uint32_t v_lbo = p.rv > 64 ? kBox : 0;  // V: second 64-dim M-block (or a duplicate of the first)
-          auto recon = [&](int j) -> bool {
-            const int t = g + 2 * j, s = t % NS_K;
-            if (!mbar_wait(bar(B_KF + s), (t / NS_K) & 1, s_abort, p.status)) return false;
-            fence_after();
-            const uint32_t sK = sbase + Lay::OFF_K + s * Lay::K_BYTES;
-            for (int kk = 0; kk < p.rk / 16; ++kk)
-              mma_ss(tg + kColDk, sdesc(sK + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024),
-                     sdesc(sU + kk * 2048, u_lbo, 1024), ID_REC, kk > 0);
-            mma_commit(bar(B_KE + s));
-            mma_commit(bar(B_REC + g));
-            return true;
-          };
-          bool ok = mbar_wait(bar(B_UF), 0, s_abort, p.status) && recon(0);
-          for (int j = 0; ok && j <= n_g; ++j) {
-            if (j + 1 < n_g) {
-              if (!mbar_wait(bar(B_AF + g), j & 1, s_abort, p.status) || !recon(j + 1)) break;
+          for (int j = 0; j <= n_g; ++j) {
+            if (j < n_g) {
+              if (j >= 2 && !mbar_wait(bar(B_SR + 2 * g + (j & 1)), ((j >> 1) - 1) & 1, s_abort, p.status)) break;
+              bool ok = true;
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                if (!mbar_wait(bar(B_AF + 2 * g + h), j & 1, s_abort, p.status)) {
+                  ok = false;
+                  break;
+                }
+                fence_after();
+                // A half h: the 16-element K steps kk = 2h, 2h + 1 (even dims) and 4 + 2h, 5 + 2h (odd dims).
+#pragma unroll
+                for (int x = 0; x < 4; ++x) {
+                  const int kk = (x >> 1) * 4 + 2 * h + (x & 1);
+                  mma_ts(tg + kColDs + (j & 1) * 16, tg + kColA + kk * 8,
+                         sdesc(sQ + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), ID_QK, (h | x) != 0);
+                }
+                mma_commit(bar(h == 0 ? B_AE + g : B_SF + 2 * g + (j & 1)));
+              }
+              if (!ok) break;
             }
             if (j >= 1) {  // PV(j - 1)
               const int jp = j - 1, tp = g + 2 * jp, sv = tp % NS_V;
@@ -534,6 +530,28 @@ __global__ void __launch_bounds__(kThreads, 1)
               mma_commit(bar(B_VE + sv));
             }
           }
+        } else {
+          // ---- reconstruct(j + 1) in two halves: D_k columns 64 h .. 64 h + 63 (frequencies 32 h .. + 31) once
+          // RoPE(j) has read them, so the reconstruction of one half overlaps the rotation of the other.
+          constexpr uint32_t ID_REC = idesc_f16(64, 1, false, true);  // bf16 lat x bf16 U (MN-major), N = 64
+          const uint32_t sU = sbase + Lay::OFF_U;
+          const uint32_t u_lbo = p.rk * 128;  // U: stride between the two 64-column N-blocks
+          auto recon = [&](int j, int h) -> bool {
+            const int t = g + 2 * j, s = t % NS_K;
+            if (h == 0 && !mbar_wait(bar(B_KF + s), (t / NS_K) & 1, s_abort, p.status)) return false;
+            fence_after();
+            const uint32_t sK = sbase + Lay::OFF_K + s * Lay::K_BYTES;
+            for (int kk = 0; kk < p.rk / 16; ++kk)
+              mma_ss(tg + kColDk + 64 * h, sdesc(sK + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024),
+                     sdesc(sU + h * u_lbo + kk * 2048, u_lbo, 1024), ID_REC, kk > 0);
+            if (h == 1) mma_commit(bar(B_KE + s));
+            mma_commit(bar(B_REC + 2 * g + h));
+            return true;
+          };
+          bool ok = mbar_wait(bar(B_UF), 0, s_abort, p.status) && recon(0, 0) && recon(0, 1);
+          for (int j = 0; ok && j + 1 < n_g; ++j)
+            for (int h = 0; ok && h < 2; ++h)
+              ok = mbar_wait(bar(B_AF + 2 * g + h), j & 1, s_abort, p.status) && recon(j + 1, h);
         }
         // Drain: every MMA this thread issued has completed once this barrier flips.
         mma_commit(bar(drain));
@@ -546,9 +564,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int g = (warp - 8) >> 2, quarter = warp & 3, row = quarter * 32 + lane;
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + g * kGrpCols;
     {
-      // U_k -> shared memory as the MN-major SWIZZLE_128B B operand of the reconstruction, its 128 dims
-      // reordered [even | odd]: N-block 0 holds dims 0, 2, .., 126 and N-block 1 dims 1, 3, .., 127.
-      // Item: (latent row r, 16 source dims) -> one 16-byte chunk of each N-block.
+      // U_k -> shared memory as the MN-major SWIZZLE_128B B operand of the reconstruction, one 64-column
+      // N-block per half of the frequencies: N-block h holds the even dims of frequencies 32 h .. 32 h + 31
+      // (columns 0..31), then their odd dims (columns 32..63).
+      // Item: (latent row r, source dims 16 a .. 16 a + 15 = frequencies 8 a .. 8 a + 7) -> 16-byte chunks
+      // a % 4 (even dims) and 4 + a % 4 (odd dims) of row r of N-block a / 4.
       for (int e = (warp - 8) * 32 + lane; e < p.rk * 8; e += 256) {
         const int r = e >> 3, a = e & 7;
         const uint4* src = reinterpret_cast<const uint4*>(p.u_k + ((size_t)kvh * p.rk + r) * p.ld_u + 16 * a);
@@ -557,9 +577,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     __byte_perm(x1.x, x1.y, 0x5410), __byte_perm(x1.z, x1.w, 0x5410));
         const uint4 od = make_uint4(__byte_perm(x0.x, x0.y, 0x7632), __byte_perm(x0.z, x0.w, 0x7632),
                                     __byte_perm(x1.x, x1.y, 0x7632), __byte_perm(x1.z, x1.w, 0x7632));
-        const uint32_t off = r * 128 + ((a ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(smem + Lay::OFF_U + off) = ev;
-        *reinterpret_cast<uint4*>(smem + Lay::OFF_U + p.rk * 128 + off) = od;
+        unsigned char* urow = smem + Lay::OFF_U + (a >> 2) * p.rk * 128 + r * 128;
+        *reinterpret_cast<uint4*>(urow + (((a & 3) ^ (r & 7)) << 4)) = ev;
+        *reinterpret_cast<uint4*>(urow + (((4 + (a & 3)) ^ (r & 7)) << 4)) = od;
       }
       fence_proxy_async();  // generic-proxy writes -> visible to the tensor core's reads
       __syncwarp();
@@ -567,17 +587,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const int n_g = (nt - g + 1) / 2;
     for (int i = 0; i < n_g; ++i) {
-      // ---- RoPE(i): column f of D_k holds dim 2f, column 64 + f dim 2f + 1; K_rot -> fp16 A columns ----
-      if (!mbar_wait(bar(B_REC + g), i & 1, s_abort, p.status)) break;
-      fence_after();
+      // ---- RoPE(i), by halves: D_k columns 64 h .. 64 h + 31 hold the even dims of frequencies 32 h + c,
+      // columns 64 h + 32 + c their odd dims; chunk ch = 2 h + sub rotates frequencies 16 ch .. 16 ch + 15.
+      // K_rot -> fp16 A columns. Finishing half h releases D_k half h (reconstruction of tile i + 1) and
+      // hands A half h to QK(i).
       bool ok = true;
 #pragma unroll 1
       for (int ch = 0; ch < 4; ++ch) {
+        const int h = ch >> 1, sub = ch & 1;
+        if (sub == 0) {
+          if (!mbar_wait(bar(B_REC + 2 * g + h), i & 1, s_abort, p.status)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+        }
         const int n = i * 4 + ch, sb = g * T_SLOTS + n % T_SLOTS;
         // The chunk's D_k columns load while this warp waits for and reads its table chunk.
         uint32_t ke[16], ko[16];
-        tmem_ld16(trow + kColDk + 16 * ch, ke);
-        tmem_ld16(trow + kColDk + 64 + 16 * ch, ko);
+        tmem_ld16(trow + kColDk + 64 * h + 16 * sub, ke);
+        tmem_ld16(trow + kColDk + 64 * h + 32 + 16 * sub, ko);
         if (!mbar_wait(bar(B_TF + sb), (n / T_SLOTS) & 1, s_abort, p.status)) {
           tmem_wait_ld_regs(ke, ko);
           ok = false;
@@ -609,10 +638,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           ae[x] = half2_as_u32(__hfma2(__hneg2(o), sn, __hmul2(e, c)));
           ao[x] = half2_as_u32(__hfma2(e, sn, __hmul2(o, c)));
         }
-        if (ch == 0 && i >= 1) {
-          // A still feeds QK(i - 1) until that MMA completes; its commit is the scores barrier.
+        if (sub == 0 && i >= 1) {
+          // A half h still feeds half h of QK(i - 1) until those MMAs complete: their commit is AE (h = 0)
+          // or the scores barrier (h = 1).
           const int jq = i - 1;
-          if (!mbar_wait(bar(B_SF + 2 * g + (jq & 1)), (jq >> 1) & 1, s_abort, p.status)) {
+          const bool freed = h == 0 ? mbar_wait(bar(B_AE + g), jq & 1, s_abort, p.status)
+                                    : mbar_wait(bar(B_SF + 2 * g + (jq & 1)), (jq >> 1) & 1, s_abort, p.status);
+          if (!freed) {
             ok = false;
             break;
           }
@@ -623,13 +655,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st8(trow + kColA + 8 * ch, ae);
         tmem_st8(trow + kColA + 32 + 8 * ch, ao);
         tmem_wait_st_regs(ae, ao);
-        if (!ok) break;
+        if (sub == 1) {
+          fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(B_AF + 2 * g + h));
+        }
       }
       if (!ok) break;
-      tmem_wait_st();
-      fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_AF + g));
     }
   } else {
     // ============================== softmax warps ==============================
