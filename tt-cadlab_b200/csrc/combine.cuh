@@ -73,4 +73,108 @@ __global__ void __launch_bounds__(kCombineThreads) palu_combine_kernel(const Com
   }
 }
 
+// Merge for the tcgen05 decode's balanced split (decode_tc.cuh): the records of (batch row b, query head)
+// are found from the same cut of the KV head's row-ordered tile list into `ctas` ranges: T tiles in all,
+// row b's tiles are s_b .. s_b + n_b - 1, and tile x lies in range ((x + 1) * ctas - 1) / T. Rows with no
+// tile (cur_pos < 0) come out zero. Launched as a programmatic dependent of the decode kernel: the record
+// lists come from cur_pos alone, so they are built before griddepcontrol.wait, which then waits for the
+// decode grid's completion and memory before any record is read.
+struct CombineTcParams {
+  const float* ws_o;         // records [rec][rep][r_lat]
+  const float* ws_ml;        // records [rec][rep][5]: m, l of the 4 row quarters
+  const int32_t* cur_pos;    // [B]
+  const __nv_bfloat16* u_v;  // optional [n_kv][r_lat][128]
+  void* out;                 // [B][n_q][r_out]
+  int out_f32;
+  int batch, n_q, n_kv, rep, ctas, r_lat, r_out, max_seq;
+};
+constexpr int kMaxTcRecords = 2 * kMaxSplits;
+
+__global__ void __launch_bounds__(kCombineThreads) palu_combine_tc_kernel(const CombineTcParams p) {
+  __shared__ int s_rec[kMaxTcRecords];
+  __shared__ float s_w[kMaxTcRecords];
+  __shared__ int s_nrec;
+  __shared__ float s_inv_l;
+  extern __shared__ float s_lat[];  // r_lat floats (u_v mode only)
+  const int qh = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  const int kvh = qh / p.rep, hl = qh - kvh * p.rep;
+  if (tid < 32) {
+    long long T = 0, sb = 0;
+    for (int bb = tid; bb < p.batch; bb += 32) {
+      const int nb = tc_row_tiles(p.cur_pos, bb, p.max_seq);
+      T += nb;
+      if (bb < b) sb += nb;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      T += __shfl_xor_sync(0xffffffffu, T, o);
+      sb += __shfl_xor_sync(0xffffffffu, sb, o);
+    }
+    if (tid == 0) {
+      const int nb = tc_row_tiles(p.cur_pos, b, p.max_seq);
+      int cnt = 0;
+      if (nb > 0 && T > 0) {
+        const int cf = (int)(((sb + 1) * p.ctas - 1) / T), cl = (int)(((sb + nb) * p.ctas - 1) / T);
+        if (cf == cl) {
+          for (int g = 0; g < 2; ++g) s_rec[cnt++] = (int)tc_rec_direct(b, kvh, p.n_kv, g);
+        } else {
+          for (int g = 0; g < 2; ++g) s_rec[cnt++] = (int)tc_rec_edge(p.batch, p.n_kv, p.ctas, kvh, cf, 1, g);
+          for (int c = cf + 1; c <= cl && cnt + 2 <= kMaxTcRecords; ++c) {
+            if ((long long)c * T / p.ctas == (long long)(c + 1) * T / p.ctas) continue;  // empty range: no records
+            for (int g = 0; g < 2; ++g) s_rec[cnt++] = (int)tc_rec_edge(p.batch, p.n_kv, p.ctas, kvh, c, 0, g);
+          }
+        }
+      }
+      s_nrec = cnt;
+    }
+  }
+  __syncthreads();
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  if (tid < 32) {
+    const int nrec = s_nrec;
+    float M = -INFINITY;
+    for (int i = tid; i < nrec; i += 32) M = fmaxf(M, p.ws_ml[((size_t)s_rec[i] * p.rep + hl) * 5]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float L = 0.f;
+    for (int i = tid; i < nrec; i += 32) {
+      const float* ml = p.ws_ml + ((size_t)s_rec[i] * p.rep + hl) * 5;
+      const float w = (M == -INFINITY || ml[0] == -INFINITY) ? 0.f : fast_exp2(ml[0] - M);
+      s_w[i] = w;
+      L += w * (ml[1] + ml[2] + ml[3] + ml[4]);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    if (tid == 0) s_inv_l = L > 0.f ? 1.f / L : 0.f;
+  }
+  __syncthreads();
+  const int nrec = s_nrec;
+  const float inv_l = s_inv_l;
+  const size_t orow = ((size_t)b * p.n_q + qh) * p.r_out;
+  for (int c = tid; c < p.r_lat; c += kCombineThreads) {
+    float acc = 0.f;
+    for (int i = 0; i < nrec; ++i) acc += p.ws_o[((size_t)s_rec[i] * p.rep + hl) * p.r_lat + c] * s_w[i];
+    acc *= inv_l;
+    if (p.u_v) {
+      s_lat[c] = acc;
+    } else if (p.out_f32) {
+      reinterpret_cast<float*>(p.out)[orow + c] = acc;
+    } else {
+      reinterpret_cast<__nv_bfloat16*>(p.out)[orow + c] = __float2bfloat16_rn(acc);
+    }
+  }
+  if (p.u_v) {
+    __syncthreads();
+    const __nv_bfloat16* u = p.u_v + (size_t)kvh * p.r_lat * kHeadDim;
+    for (int d = tid; d < kHeadDim; d += kCombineThreads) {
+      float acc = 0.f;
+      for (int c = 0; c < p.r_lat; ++c) acc += s_lat[c] * __bfloat162float(u[(size_t)c * kHeadDim + d]);
+      if (p.out_f32)
+        reinterpret_cast<float*>(p.out)[orow + d] = acc;
+      else
+        reinterpret_cast<__nv_bfloat16*>(p.out)[orow + d] = __float2bfloat16_rn(acc);
+    }
+  }
+}
+
 }  // namespace palu

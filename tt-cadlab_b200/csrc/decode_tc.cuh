@@ -1,16 +1,21 @@
-// Split-K flash-decode over Palu latent caches on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+// Flash-decode over Palu latent caches on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
 //
-// One CTA owns (batch row b, KV head h, split s): a contiguous range of 128-token tiles of the positions
-// 0..cur_pos[b]. Two groups work on alternate tiles (group g on tiles t with t % 2 == g), so two tiles are in
-// flight per CTA. Each group has its own warps, rings, barriers and TMEM columns (24 warps in all, see
-// role_of): a K+table TMA producer, a V producer, a QK+PV issuer, a reconstruct issuer (a single thread
-// issues at most one tcgen05.mma per ~64 cycles whatever its shape, measured on B200, so the MMAs are
-// split over two threads), 4 RoPE warps and 4 softmax warps (a warp of either kind owns the 32 TMEM lanes
-// of its SMSP quarter: 32 token rows of the tile, or 32 latent dims of the PV output).
-// At start the softmax warps stage Q^T (fp16) and the RoPE warps U_k (bf16) in shared memory with their
-// head dims reordered as [even dims | odd dims], so that D_k holds each rotation pair (2f, 2f+1) in columns
-// f and 64 + f and the rotation of two adjacent frequencies is one packed half2 operation.
-// Per group-local tile j (tile t = g + 2 j):
+// One CTA per (range, KV head): the KV head's 128-token tiles over all batch rows (positions 0..cur_pos[b]
+// of each row, rows in order) are cut into `ctas` equal contiguous ranges (see TcParams), so every CTA
+// streams the same number of tiles in a single wave whatever the batch and the rows' lengths; the pipeline
+// runs on across row boundaries, where each group writes a partial (O, m, l) for the row it leaves
+// (combine.cuh merges a row's partials). Two groups work on alternate tiles of the range (group g on
+// CTA-local tiles t with t % 2 == g), so two tiles are in flight per CTA. Each group has its own warps,
+// rings, barriers and TMEM columns (24 warps in all, see role_of): a K+table TMA producer, a V producer, a
+// QK+PV issuer, a reconstruct issuer (a single thread issues at most one tcgen05.mma per ~64 cycles
+// whatever its shape, measured on B200, so the MMAs are split over two threads), 4 RoPE warps and 4 softmax
+// warps (a warp of either kind owns the 32 TMEM lanes of its SMSP quarter: 32 token rows of the tile, or
+// 32 latent dims of the PV output).
+// At start the RoPE warps stage U_k (bf16) in shared memory with its head dims reordered as
+// [even dims | odd dims] per half of the frequencies, so that D_k holds each rotation pair (2f, 2f+1) 32
+// columns apart and the rotation of two adjacent frequencies is one packed half2 operation. The softmax
+// warps stage Q^T (fp16, the same reordering) per batch row, double-buffered per group.
+// Per group-local tile j (CTA-local tile t = g + 2 j):
 //   MMA      D_k[128 tok x 128 dim] (f32) = lat_k (smem, K-major) x U_k (smem, MN-major), as two N = 64 halves
 //            (frequencies 0..31 and 32..63, each half its even dims then its odd dims)
 //   RoPE     K row -> fp16, rotated in half2 arithmetic with the fp16 table -> K_rot into its own TMEM
@@ -21,9 +26,9 @@
 //   softmax  thread c (latent dim c) accumulates O[h][c] = O * alpha + hi + lo in registers
 // RoPE works by halves of D_k: as soon as RoPE(j) has finished half h, the reconstruction of half h of
 // tile j + 1 and the QK MMAs of half h of tile j are issued, so the reconstruct latency overlaps the
-// rotation of the other half; RoPE(j + 1) overlaps softmax(j) and PV(j - 1). D_s, D_o and P are double-buffered by j % 2, and every consumer releases what
-// it read with its own barrier, so no barrier runs two phases ahead of a waiter. The two groups merge
-// their (m, l, O) at the end into one split partial (combine.cuh merges the splits). Every wait is bounded
+// rotation of the other half; RoPE(j + 1) overlaps softmax(j) and PV(j - 1). D_s, D_o and P are
+// double-buffered by j % 2, and every consumer releases what it read with its own barrier, so no barrier
+// runs two phases ahead of a waiter. Every wait is bounded
 // (1 s of globaltimer): on expiry the CTA records a status code, all roles stop, copies and MMAs in flight
 // are drained, and TMEM is freed.
 #pragma once
@@ -52,11 +57,80 @@ struct TcParams {
   const __nv_bfloat16* q;   // [B][n_q][128]
   const __nv_bfloat16* u_k; // [n_kv][r_k] rows of ld_u elements (U_k in the first 128)
   const int32_t* cur_pos;   // [B]
-  float* ws_o;              // [B][n_kv][splits][rep][rv]
-  float* ws_ml;             // [B][n_kv][splits][rep][2]
+  float* ws_o;              // partial records (tc_rec_direct / tc_rec_edge), each [rep][rv]
+  float* ws_ml;             // the same records' [rep][5]: m, then the 4 row quarters' l
   int* status;              // device status word, 0 = ok
-  int batch, n_q, n_kv, n_groups, rk, rv, max_seq, splits, rep, ld_u;
+  int batch, n_q, n_kv, n_groups, rk, rv, max_seq, ctas, rep, ld_u;
   float scale_log2;
+};
+
+// Work split: the tiles of one KV head over all batch rows, in row order (row b has ceil(L_b / 128)
+// tiles, L_b = cur_pos[b] + 1 clamped to [0, max_seq]), are cut into `ctas` equal contiguous ranges, one
+// per CTA, so every CTA streams the same number of tiles whatever the rows' lengths. A row's tiles inside
+// one CTA form a segment; each group of the CTA writes one partial record (O, m, l) per segment
+// (tc_rec_direct / tc_rec_edge). The merge (combine.cuh) finds a row's records from the same split.
+PALU_DEVINL int row_len(const TcParams& p, int b) {
+  const int L = p.cur_pos[b] + 1;
+  return L < 0 ? 0 : (L > p.max_seq ? p.max_seq : L);
+}
+PALU_DEVINL int row_tiles(const TcParams& p, int b) { return tc_row_tiles(p.cur_pos, b, p.max_seq); }
+
+// A batch row's tiles inside this CTA's range: tiles ta .. ta + cnt - 1 of row b, which are the CTA's
+// tiles kb .. kb + cnt - 1 (CTA-local order). cnt == 0 marks the end of the range.
+struct RowSeg {
+  int b, ta, cnt, kb;
+};
+PALU_DEVINL RowSeg seg_next(const TcParams& p, int n, const RowSeg& s) {
+  RowSeg r{s.b, 0, 0, s.kb + s.cnt};
+  if (r.kb >= n) return r;
+  int nb = 0;
+  do {
+    if (++r.b >= p.batch) return RowSeg{r.b, 0, 0, n};  // unreachable while cur_pos is unchanged
+    nb = row_tiles(p, r.b);
+  } while (nb == 0);
+  r.cnt = min(nb, n - r.kb);
+  return r;
+}
+// Group g takes the CTA-local tiles k with k % 2 == g: its first tile in segment s and their count.
+PALU_DEVINL int seg_group_first(const RowSeg& s, int g) { return s.kb + ((g - s.kb) & 1); }
+PALU_DEVINL int seg_group_count(const RowSeg& s, int g) {
+  const int kf = seg_group_first(s, g);
+  return kf < s.kb + s.cnt ? (s.kb + s.cnt - kf + 1) / 2 : 0;
+}
+// Group g's tiles in order, with their row, tile within the row and group-segment index (segments in which
+// the group has tiles, counted from 0).
+struct GroupTiles {
+  RowSeg s;
+  int g, n, x, cnt, kf, sigma, len;  // len: positions the current row attends
+  PALU_DEVINL void init(const TcParams& p, const RowSeg& s0, int g_, int n_) {
+    s = s0;
+    g = g_;
+    n = n_;
+    sigma = -1;
+    settle(p);
+  }
+  PALU_DEVINL void settle(const TcParams& p) {
+    while (s.cnt > 0 && (cnt = seg_group_count(s, g)) == 0) s = seg_next(p, n, s);
+    if (s.cnt > 0) {
+      kf = seg_group_first(s, g);
+      x = 0;
+      ++sigma;
+      len = row_len(p, s.b);
+    }
+  }
+  PALU_DEVINL bool valid() const { return s.cnt > 0; }
+  PALU_DEVINL int tile() const { return s.ta + (kf - s.kb) + 2 * x; }
+  PALU_DEVINL bool first() const { return x == 0; }
+  PALU_DEVINL void next(const TcParams& p) {
+    if (++x >= cnt) {
+      s = seg_next(p, n, s);
+      settle(p);
+    }
+  }
+  PALU_DEVINL void next_segment(const TcParams& p) {
+    s = seg_next(p, n, s);
+    settle(p);
+  }
 };
 
 template <int KBK, int KBV>
@@ -65,11 +139,10 @@ struct Layout {
   static constexpr int V_BYTES = KBV * kBox;
   static constexpr int TCH_BYTES = 8192;              // table chunk: 128 rows x 16 pairs x 4 B (SWIZZLE_64B)
   static constexpr int U_BYTES = KBK * 2 * 64 * 128;  // 2 N-blocks x (<= 64 KBK rows) x 128 B
-  static constexpr int Q_BYTES = 2 * 2048;            // 2 K-blocks x 16 rows x 128 B (fp16)
+  static constexpr int Q_BYTES = 2 * 2048;            // one buffer: 2 K-blocks x 16 rows x 128 B (fp16)
   static constexpr int P_BYTES = 2 * 2048;            // one buffer: 2 K-blocks x 16 rows x 128 B (bf16)
-  static constexpr int O_BYTES = 2 * 4 * 128 * 4;     // merge area [2 groups][4 heads][128] fp32
   static constexpr int MISC_BYTES = 2048;
-  static constexpr int FIXED = U_BYTES + Q_BYTES + 4 * P_BYTES + O_BYTES + MISC_BYTES + 1024;
+  static constexpr int FIXED = U_BYTES + 4 * Q_BYTES + 4 * P_BYTES + MISC_BYTES + 1024;
   static constexpr int BUDGET = 227 * 1024;
   // Rings, all group-private: stage i of a ring only holds tiles of group (i % 2) (K, V) or chunks of
   // group (i / T_SLOTS) (table). V: one stage per group. Table: 4 chunk slots per group (a whole tile)
@@ -82,9 +155,8 @@ struct Layout {
   static constexpr int OFF_TAB = OFF_V + NS_V * V_BYTES;
   static constexpr int OFF_U = OFF_TAB + 2 * T_SLOTS * TCH_BYTES;
   static constexpr int OFF_Q = OFF_U + U_BYTES;
-  static constexpr int OFF_P = OFF_Q + Q_BYTES;
-  static constexpr int OFF_O = OFF_P + 4 * P_BYTES;
-  static constexpr int OFF_MISC = OFF_O + O_BYTES;
+  static constexpr int OFF_P = OFF_Q + 4 * Q_BYTES;  // Q: [group][segment parity], P: [group][tile parity]
+  static constexpr int OFF_MISC = OFF_P + 4 * P_BYTES;
   static constexpr int TOTAL = OFF_MISC + MISC_BYTES + 1024;  // + slack to align the base to 1024
   static_assert(TOTAL <= BUDGET, "shared memory budget");
 };
@@ -331,31 +403,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
 
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int cta = blockIdx.x, kvh = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int item_lat = b * p.n_groups + kvh / (p.n_kv / p.n_groups);
-
-  int L = p.cur_pos[b] + 1;
-  L = L < 0 ? 0 : (L > p.max_seq ? p.max_seq : L);
-  const int n_tiles = (L + kTile - 1) / kTile;
-  const int per = (n_tiles + p.splits - 1) / p.splits;
-  const int tile0 = split * per;
-  const int nt = max(0, min(n_tiles, tile0 + per) - tile0);
+  const int lat_head = kvh / (p.n_kv / p.n_groups);  // latent head of this KV head (its group)
 
   // ---- barriers and scalars (misc area) ----
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Lay::OFF_MISC);
   auto bar = [&](int i) { return smem_u32(bars + i); };
   // [g][x] pairs are double-buffered by the group-local tile index parity x.
-  constexpr int B_KF = 0, B_KE = B_KF + NS_K, B_VF = B_KE + NS_K, B_VE = B_VF + NS_V, B_TF = B_VE + NS_V,
+  // V-full barriers are per (slot, use parity), so a parity wait is never more than one phase behind.
+  constexpr int B_KF = 0, B_KE = B_KF + NS_K, B_VF = B_KE + NS_K, B_VE = B_VF + 2 * NS_V, B_TF = B_VE + NS_V,
                 B_TE = B_TF + NS_T, B_UF = B_TE + NS_T, B_REC = B_UF + 1, B_AF = B_REC + 4, B_AE = B_AF + 4,
-                B_SF = B_AE + 2,
-                B_SR = B_SF + 4, B_PF = B_SR + 4, B_OF = B_PF + 4, B_OR = B_OF + 4, B_MX = B_OR + 4,
-                B_DRAIN = B_MX + 4, B_COUNT = B_DRAIN + 4;
+                B_SF = B_AE + 2, B_SR = B_SF + 4, B_PF = B_SR + 4, B_OF = B_PF + 4, B_OR = B_OF + 4,
+                B_MX = B_OR + 4, B_QF = B_MX + 4, B_DRAIN = B_QF + 4, B_COUNT = B_DRAIN + 4;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + B_COUNT);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
-  float* s_max = reinterpret_cast<float*>(s_tmem + 4);  // [2 groups][2 bufs][4 warps][4 heads]
-  float* s_lsum = s_max + 64;                             // [2 groups][4 warps][4 heads]
-  float* s_m = s_lsum + 32;                               // [2 groups][4 heads]
+  int* s_range = reinterpret_cast<int*>(s_tmem + 4);      // n, b0, t0, cnt0 of this CTA's range
+  float* s_max = reinterpret_cast<float*>(s_tmem + 8);    // [2 groups][2 bufs][4 warps][4 heads]
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS_K; ++s) {
@@ -363,7 +427,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(B_KE + s), 1);
     }
     for (int s = 0; s < NS_V; ++s) {
-      mbar_init(bar(B_VF + s), 1);
+      mbar_init(bar(B_VF + 2 * s), 1);
+      mbar_init(bar(B_VF + 2 * s + 1), 1);
       mbar_init(bar(B_VE + s), 1);
     }
     for (int s = 0; s < NS_T; ++s) {
@@ -384,6 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(bar(B_OF + 2 * g + x), 1);
         mbar_init(bar(B_OR + 2 * g + x), 4);
         mbar_init(bar(B_MX + 2 * g + x), 4);
+        mbar_init(bar(B_QF + 2 * g + x), 4);  // the group's 4 softmax warps stage Q
       }
     }
     for (int x = 0; x < 4; ++x) mbar_init(bar(B_DRAIN + x), 1);
@@ -396,43 +462,51 @@ __global__ void __launch_bounds__(kThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
   }
-  if (warp >= 16) {
-    const int t = (warp - 16) * 32 + lane;  // 0..255 over the 8 softmax warps
-    // Q^T operand, fp16, K-major SWIZZLE_128B: 16 rows (this KV head's query heads, zero padded) x 128
-    // dims in [even | odd] order: K-block 0 = even dims, K-block 1 = odd dims (64 fp16 per 128-B row).
-    // Thread: (row, 16-byte chunk of 8 reordered dims); bf16 q is exact in fp16.
-    {
-      const int row = t >> 4, chunk = t & 15;
-      uint32_t w[4] = {0u, 0u, 0u, 0u};
-      if (row < p.rep) {
-        const uint4* qr = reinterpret_cast<const uint4*>(p.q + ((size_t)b * p.n_q + kvh * p.rep + row) * kHeadDim +
-                                                         16 * (chunk & 7));
-        const uint4 x0 = qr[0], x1 = qr[1];  // source dims 16 (chunk & 7) .. + 15
-        const uint32_t sel = chunk < 8 ? 0x5410u : 0x7632u;  // even (low) or odd (high) halves
-        const uint32_t bw[4] = {__byte_perm(x0.x, x0.y, sel), __byte_perm(x0.z, x0.w, sel),
-                                __byte_perm(x1.x, x1.y, sel), __byte_perm(x1.z, x1.w, sel)};
+  if (warp == 2) {
+    // This CTA's range of the KV head's tiles, and where it starts (row b0, tile t0 of that row).
+    long long T = 0;
+    for (int bb = lane; bb < p.batch; bb += 32) T += row_tiles(p, bb);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = unpack_bf16(bw[i]);
-          w[i] = pack_half2(f.x, f.y);
+    for (int o = 16; o; o >>= 1) T += __shfl_xor_sync(0xffffffffu, T, o);
+    if (lane == 0) {
+      const long long k0 = (long long)cta * T / p.ctas, k1 = (long long)(cta + 1) * T / p.ctas;
+      const int n = (int)(k1 - k0);
+      int b0 = 0, t0 = 0, cnt0 = 0;
+      if (n > 0) {
+        long long acc = 0;
+        for (b0 = 0; b0 < p.batch; ++b0) {
+          const int nb = row_tiles(p, b0);
+          if (acc + nb > k0) break;
+          acc += nb;
+        }
+        if (b0 < p.batch) {
+          t0 = (int)(k0 - acc);
+          cnt0 = min(row_tiles(p, b0) - t0, n);
         }
       }
-      const uint32_t off = (chunk >> 3) * 2048 + row * 128 + (((chunk & 7) ^ (row & 7)) << 4);
-      *reinterpret_cast<uint4*>(smem + Lay::OFF_Q + off) = make_uint4(w[0], w[1], w[2], w[3]);
+      s_range[0] = cnt0 > 0 ? n : 0;
+      s_range[1] = b0;
+      s_range[2] = t0;
+      s_range[3] = cnt0;
     }
-    for (int e = t; e < 4 * Lay::P_BYTES / 16; e += 256)
-      reinterpret_cast<uint4*>(smem + Lay::OFF_P)[e] = make_uint4(0, 0, 0, 0);
+  }
+  if (warp >= 16) {
+    // Q buffers (4 x 4 KB) and P buffers (4 x 4 KB): rows past the query heads stay zero throughout.
+    for (int e = (warp - 16) * 32 + lane; e < (4 * Lay::Q_BYTES + 4 * Lay::P_BYTES) / 16; e += 256)
+      reinterpret_cast<uint4*>(smem + Lay::OFF_Q)[e] = make_uint4(0, 0, 0, 0);
     fence_proxy_async();
   }
   fence_before();
   __syncthreads();
   fence_after();
   const uint32_t tmem = *s_tmem;
+  const int n = s_range[0];                                  // tiles of this CTA
+  const RowSeg seg0{s_range[1], s_range[2], s_range[3], 0};  // its first segment
 
   if (warp < 8) {
     // ============================== single-lane role warps ==============================
     const int g = warp < 4 ? 0 : 1, role = role_of(warp);
-    const int n_g = (nt - g + 1) / 2;  // this group's tiles: t = g + 2 j, j < n_g
+    const int n_g = (n - g + 1) / 2;  // this group's tiles: CTA-local t = g + 2 j, j < n_g
     if (lane == 0 && n_g > 0) {
       if (role == kRoleKT || role == kRoleV) {
         // ---- TMA producers: K tile then its 4 table chunks (KT), or the V tile (V), per group tile.
@@ -440,10 +514,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_prefetch_map(kt ? &tm_k : &tm_v);
         if (kt) tma_prefetch_map(&tm_tab);
         int issued_kv = 0, issued_t = 0;
-        for (int j = 0; j < n_g; ++j) {
-          const int t = g + 2 * j, row = (tile0 + t) * kTile;
+        GroupTiles it;
+        it.init(p, seg0, g, n);
+        for (int j = 0; j < n_g && it.valid(); ++j, it.next(p)) {
+          const int t = g + 2 * j, row = it.tile() * kTile, item_lat = it.s.b * p.n_groups + lat_head;
           const int sb = kt ? t % NS_K : t % NS_V, use = kt ? t / NS_K : t / NS_V;
-          const uint32_t full = bar((kt ? B_KF : B_VF) + sb), empty = bar((kt ? B_KE : B_VE) + sb);
+          const uint32_t full = kt ? bar(B_KF + sb) : bar(B_VF + 2 * sb + (use & 1));
+          const uint32_t empty = bar((kt ? B_KE : B_VE) + sb);
           if (use >= 1 && !mbar_wait(empty, (use - 1) & 1, s_abort, p.status)) break;
           if (kt) {
             mbar_expect_tx(full, Lay::K_BYTES);
@@ -460,14 +537,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (kt) {
             bool ok = true;
             for (int c = 0; c < 4; ++c) {
-              const int n = 4 * j + c, ts = g * T_SLOTS + n % T_SLOTS, tuse = n / T_SLOTS;
+              const int nc = 4 * j + c, ts = g * T_SLOTS + nc % T_SLOTS, tuse = nc / T_SLOTS;
               if (tuse >= 1 && !mbar_wait(bar(B_TE + ts), (tuse - 1) & 1, s_abort, p.status)) {
                 ok = false;
                 break;
               }
               mbar_expect_tx(bar(B_TF + ts), Lay::TCH_BYTES);
               tma_load_2d(sbase + Lay::OFF_TAB + ts * Lay::TCH_BYTES, &tm_tab, bar(B_TF + ts), c * 16, row);
-              issued_t = n + 1;
+              issued_t = nc + 1;
             }
             if (!ok) break;
           }
@@ -477,10 +554,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = max(0, issued_kv - ring); j < issued_kv; ++j) {
             const int t = g + 2 * j;
             if (kt) mbar_drain(bar(B_KF + t % NS_K), (t / NS_K) & 1);
-            else mbar_drain(bar(B_VF + t % NS_V), (t / NS_V) & 1);
+            else mbar_drain(bar(B_VF + 2 * (t % NS_V) + ((t / NS_V) & 1)), (t / NS_V >> 1) & 1);
           }
-          for (int n = max(0, issued_t - T_SLOTS); n < issued_t; ++n)
-            mbar_drain(bar(B_TF + g * T_SLOTS + n % T_SLOTS), (n / T_SLOTS) & 1);
+          for (int nc = max(0, issued_t - T_SLOTS); nc < issued_t; ++nc)
+            mbar_drain(bar(B_TF + g * T_SLOTS + nc % T_SLOTS), (nc / T_SLOTS) & 1);
         }
       } else {
         const uint32_t tg = tmem + g * kGrpCols;
@@ -488,13 +565,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (role == kRoleQK) {
           // ---- QK(j): D_s[j & 1] = K_rot (TMEM, fp16) x Q^T in two halves, half h once RoPE(j) wrote A half h
           // (and, first, once softmax(j - 2) read D_s[j & 1]); then PV(j - 1) once softmax(j - 1) wrote P.
+          // (PV first measured slower on B200: waiting for P(j - 1) then delays QK(j) and the RoPE chain.)
+          // Q: the group's buffer of the tile's row, staged by the softmax warps per group segment.
           constexpr uint32_t ID_QK = idesc_f16(16, 0, false, false);
           constexpr uint32_t ID_PV = idesc_f16(16, 1, true, false);  // bf16 V^T (MN-major) x bf16 P
-          const uint32_t sQ = sbase + Lay::OFF_Q;
           const uint32_t v_lbo = p.rv > 64 ? kBox : 0;  // V: second 64-dim M-block (or a duplicate of the first)
+          GroupTiles it, pit;  // QK(j) and PV(j - 1) tiles
+          it.init(p, seg0, g, n);
+          pit.init(p, seg0, g, n);
           for (int j = 0; j <= n_g; ++j) {
             if (j < n_g) {
+              const int qb = it.sigma & 1;
+              if (it.first() && !mbar_wait(bar(B_QF + 2 * g + qb), (it.sigma >> 1) & 1, s_abort, p.status)) break;
               if (j >= 2 && !mbar_wait(bar(B_SR + 2 * g + (j & 1)), ((j >> 1) - 1) & 1, s_abort, p.status)) break;
+              const uint32_t sQ = sbase + Lay::OFF_Q + (2 * g + qb) * Lay::Q_BYTES;
+              it.next(p);
               bool ok = true;
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
@@ -518,14 +603,36 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int jp = j - 1, tp = g + 2 * jp, sv = tp % NS_V;
               if (!mbar_wait(bar(B_PF + 2 * g + (jp & 1)), (jp >> 1) & 1, s_abort, p.status)) break;
               if (jp >= 2 && !mbar_wait(bar(B_OR + 2 * g + (jp & 1)), ((jp >> 1) - 1) & 1, s_abort, p.status)) break;
-              if (!mbar_wait(bar(B_VF + sv), (tp / NS_V) & 1, s_abort, p.status)) break;
-              fence_after();
+              if (!mbar_wait(bar(B_VF + 2 * sv + ((tp / NS_V) & 1)), (tp / NS_V >> 1) & 1, s_abort, p.status)) break;
+              // A row's last tile may be partial. V rows past cur_pos may hold anything (NaN included) and
+              // 0 * NaN is not 0, so for such a tile the MMA takes only the 16-token K-steps that hold valid
+              // rows, and the invalid rows inside the last of them are zeroed here first: by this thread, whose
+              // proxy fence orders its own writes before its MMAs. (Zeroing them from the softmax warps, with a
+              // proxy fence and an mbarrier hand-off, let the zeros land in the slot's next tile on B200.)
+              const int nv = pit.len - pit.tile() * kTile;  // valid rows (> 0)
+              pit.next(p);
               const uint32_t sV = sbase + Lay::OFF_V + sv * Lay::V_BYTES;
               const uint32_t sP = sbase + Lay::OFF_P + (2 * g + (jp & 1)) * Lay::P_BYTES;
+              if (nv >= kTile) {
+                fence_after();
 #pragma unroll
-              for (int kk = 0; kk < 8; ++kk)
-                mma_ss(tg + kColDo + (jp & 1) * 16, sdesc(sV + kk * 2048, v_lbo, 1024),
-                       sdesc(sP + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), ID_PV, kk > 0);
+                for (int kk = 0; kk < 8; ++kk)
+                  mma_ss(tg + kColDo + (jp & 1) * 16, sdesc(sV + kk * 2048, v_lbo, 1024),
+                         sdesc(sP + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), ID_PV, kk > 0);
+              } else {
+                const int ksteps = (nv + 15) >> 4;
+                for (int rr = nv; rr < ksteps * 16; ++rr)
+                  for (int vb = 0; vb < KBV; ++vb)
+#pragma unroll
+                    for (int c = 0; c < 8; ++c)
+                      reinterpret_cast<uint4*>(smem + Lay::OFF_V + sv * Lay::V_BYTES + vb * kBox + rr * 128)[c] =
+                          make_uint4(0, 0, 0, 0);
+                fence_proxy_async();
+                fence_after();
+                for (int kk = 0; kk < ksteps; ++kk)
+                  mma_ss(tg + kColDo + (jp & 1) * 16, sdesc(sV + kk * 2048, v_lbo, 1024),
+                         sdesc(sP + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), ID_PV, kk > 0);
+              }
               mma_commit(bar(B_OF + 2 * g + (jp & 1)));
               mma_commit(bar(B_VE + sv));
             }
@@ -585,7 +692,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(B_UF));
     }
-    const int n_g = (nt - g + 1) / 2;
+    const int n_g = (n - g + 1) / 2;
     for (int i = 0; i < n_g; ++i) {
       // ---- RoPE(i), by halves: D_k columns 64 h .. 64 h + 31 hold the even dims of frequencies 32 h + c,
       // columns 64 h + 32 + c their odd dims; chunk ch = 2 h + sub rotates frequencies 16 ch .. 16 ch + 15.
@@ -624,8 +731,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           cs[4 * c4 + 2] = w.z;
           cs[4 * c4 + 3] = w.w;
         }
-        __syncwarp();  // every lane has read its table values: the slot may refill
-        if (lane == 0) mbar_arrive(bar(B_TE + sb));
         tmem_wait_ld_regs(ke, ko);
         uint32_t ae[8], ao[8];
 #pragma unroll
@@ -638,6 +743,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           ae[x] = half2_as_u32(__hfma2(__hneg2(o), sn, __hmul2(e, c)));
           ao[x] = half2_as_u32(__hfma2(e, sn, __hmul2(o, c)));
         }
+        // Every lane has used its table values: the slot may refill. (An arrive issued while this warp's
+        // tcgen05.ld is in flight waits for that load, measured at ~260 cycles on B200, hence after the math.)
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_TE + sb));
         if (sub == 0 && i >= 1) {
           // A half h still feeds half h of QK(i - 1) until those MMAs complete: their commit is AE (h = 0)
           // or the scores barrier (h = 1).
@@ -667,137 +776,168 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ============================== softmax warps ==============================
     const int g = (warp - 16) >> 2, quarter = warp & 3, row = quarter * 32 + lane;
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + g * kGrpCols;
-    float m_run[4], l_run[4], o_acc[4], alpha0[4], alpha1[4];  // alphaN: softmax scale of tiles j with j%2 == N
+    // Q^T of a batch row into the group's Q buffer `buf`: fp16, K-major SWIZZLE_128B, 16 rows (this KV
+    // head's query heads; the rest stay zero) x 128 dims in [even | odd] order: K-block 0 = even dims,
+    // K-block 1 = odd dims (64 fp16 per 128-B row). Item (row, 16-byte chunk of 8 reordered dims); bf16
+    // q is exact in fp16. The QK issuer waits for the buffer's barrier.
+    auto stage_q = [&](int b_row, int buf) {
+      const int tq = quarter * 32 + lane;
+      if (tq < p.rep * 16) {
+        const int r = tq >> 4, chunk = tq & 15;
+        const uint4* qr = reinterpret_cast<const uint4*>(p.q + ((size_t)b_row * p.n_q + kvh * p.rep + r) * kHeadDim +
+                                                         16 * (chunk & 7));
+        const uint4 x0 = qr[0], x1 = qr[1];  // source dims 16 (chunk & 7) .. + 15
+        const uint32_t sel = chunk < 8 ? 0x5410u : 0x7632u;  // even (low) or odd (high) halves
+        const uint32_t bw[4] = {__byte_perm(x0.x, x0.y, sel), __byte_perm(x0.z, x0.w, sel),
+                                __byte_perm(x1.x, x1.y, sel), __byte_perm(x1.z, x1.w, sel)};
+        uint32_t w[4];
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      m_run[h] = -INFINITY;
-      l_run[h] = 0.f;
-      o_acc[h] = 0.f;
-      alpha0[h] = alpha1[h] = 1.f;
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = unpack_bf16(bw[i]);
+          w[i] = pack_half2(f.x, f.y);
+        }
+        const uint32_t off = (chunk >> 3) * 2048 + r * 128 + (((chunk & 7) ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(smem + Lay::OFF_Q + (2 * g + buf) * Lay::Q_BYTES + off) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_QF + 2 * g + buf));
+    };
+    // Q for the group's first two segments now; at the start of segment sigma >= 1, the one after it
+    // (buffer (sigma + 1) & 1 last fed QK of segment sigma - 1, all of whose scores are read by then).
+    GroupTiles qa;
+    qa.init(p, seg0, g, n);
+    if (qa.valid()) {
+      stage_q(qa.s.b, 0);
+      qa.next_segment(p);
+      if (qa.valid()) stage_q(qa.s.b, 1);
     }
-    const int n_g = (nt - g + 1) / 2;
-    for (int j = 0; j <= n_g; ++j) {
-      // ---- softmax(j) ---------------------------------------------------------------------------------
-      if (j < n_g) {
-        const int t = g + 2 * j;
-        if (!mbar_wait(bar(B_SF + 2 * g + (j & 1)), (j >> 1) & 1, s_abort, p.status)) break;
-        fence_after();
-        uint32_t sc[4];
-        tmem_ld4(trow + kColDs + (j & 1) * 16, sc);
-        tmem_wait_ld_regs(sc);
-        fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_SR + 2 * g + (j & 1)));  // D_s[j & 1] may be overwritten
-        const int tile_start = (tile0 + t) * kTile;
-        const bool valid = tile_start + row < L;
-        float x[4], mx[4];
+    float m_run[4], l_run[4], o_acc[4], alpha0[4], alpha1[4];  // alphaN: softmax scale of tiles j with j%2 == N
+    int j0 = 0, sigma = 0;
+    bool ok = true;
+    for (RowSeg sg = seg0; sg.cnt > 0; sg = seg_next(p, n, sg)) {
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          x[h] = (valid && h < p.rep) ? __uint_as_float(sc[h]) * p.scale_log2 : -INFINITY;
-          mx[h] = warp_max(x[h]);
+      for (int h = 0; h < 4; ++h) {
+        m_run[h] = -INFINITY;
+        l_run[h] = 0.f;
+        o_acc[h] = 0.f;
+        alpha0[h] = alpha1[h] = 1.f;
+      }
+      const int cnt = seg_group_count(sg, g), kf = seg_group_first(sg, g);
+      if (cnt > 0) {
+        if (sigma >= 1) {
+          qa.next_segment(p);
+          if (qa.valid()) stage_q(qa.s.b, (sigma + 1) & 1);
         }
-        // The 4 warps' maxima meet through a double-buffered mbarrier (bounded wait, unlike bar.sync).
-        float* smx = s_max + ((g * 2 + (j & 1)) * 4) * 4;
-        if (lane == 0) {
+        const int L = row_len(p, sg.b);
+        // softmax(j) then accumulate(j - 1) per step; the segment's last tile is accumulated before its
+        // record is written (the QK+PV issuer issues each PV as soon as its P is written, so this waits
+        // for one PV only).
+        for (int x = 0; x <= cnt; ++x) {
+          // ---- softmax(j) -------------------------------------------------------------------------------
+          if (x < cnt) {
+            const int j = j0 + x;
+            if (!mbar_wait(bar(B_SF + 2 * g + (j & 1)), (j >> 1) & 1, s_abort, p.status)) {
+              ok = false;
+              break;
+            }
+            fence_after();
+            uint32_t sc[4];
+            tmem_ld4(trow + kColDs + (j & 1) * 16, sc);
+            tmem_wait_ld_regs(sc);
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_SR + 2 * g + (j & 1)));  // D_s[j & 1] may be overwritten
+            const int tile_start = (sg.ta + (kf - sg.kb) + 2 * x) * kTile;
+            const bool valid = tile_start + row < L;
+            float xs[4], mx[4];
 #pragma unroll
-          for (int h = 0; h < 4; ++h) smx[quarter * 4 + h] = mx[h];
-          mbar_arrive(bar(B_MX + 2 * g + (j & 1)));
-        }
-        if (!mbar_wait(bar(B_MX + 2 * g + (j & 1)), (j >> 1) & 1, s_abort, p.status)) break;
-        unsigned char* sP = smem + Lay::OFF_P + (2 * g + (j & 1)) * Lay::P_BYTES;
+            for (int h = 0; h < 4; ++h) {
+              xs[h] = (valid && h < p.rep) ? __uint_as_float(sc[h]) * p.scale_log2 : -INFINITY;
+              mx[h] = warp_max(xs[h]);
+            }
+            // The 4 warps' maxima meet through a double-buffered mbarrier (bounded wait, unlike bar.sync).
+            float* smx = s_max + ((g * 2 + (j & 1)) * 4) * 4;
+            if (lane == 0) {
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const float tmax = fmaxf(fmaxf(smx[h], smx[4 + h]), fmaxf(smx[8 + h], smx[12 + h]));
-          const float m_new = fmaxf(m_run[h], tmax);
-          const float alpha = (m_new == -INFINITY) ? 1.f : fast_exp2(m_run[h] - m_new);
-          const float pv = (m_new == -INFINITY) ? 0.f : fast_exp2(x[h] - m_new);
-          if (j & 1)
-            alpha1[h] = alpha;
-          else
-            alpha0[h] = alpha;
-          l_run[h] = l_run[h] * alpha + pv;
-          m_run[h] = m_new;
-          const __nv_bfloat16 hi = __float2bfloat16_rn(pv);
-          const __nv_bfloat16 lo = __float2bfloat16_rn(pv - __bfloat162float(hi));
-          *reinterpret_cast<__nv_bfloat16*>(sP + sw128_offset(h, row, 16)) = hi;
-          *reinterpret_cast<__nv_bfloat16*>(sP + sw128_offset(4 + h, row, 16)) = lo;
-        }
-        if (tile_start + kTile > L) {
-          // V rows past cur_pos may hold anything (NaN included): P is 0 there, but 0 * NaN is not.
-          const int sv = t % NS_V;
-          if (!mbar_wait(bar(B_VF + sv), (t / NS_V) & 1, s_abort, p.status)) break;
-          if (!valid) {
-            unsigned char* vrow = smem + Lay::OFF_V + sv * Lay::V_BYTES + row * 128;
+              for (int h = 0; h < 4; ++h) smx[quarter * 4 + h] = mx[h];
+              mbar_arrive(bar(B_MX + 2 * g + (j & 1)));
+            }
+            if (!mbar_wait(bar(B_MX + 2 * g + (j & 1)), (j >> 1) & 1, s_abort, p.status)) {
+              ok = false;
+              break;
+            }
+            unsigned char* sP = smem + Lay::OFF_P + (2 * g + (j & 1)) * Lay::P_BYTES;
 #pragma unroll
-            for (int vb = 0; vb < KBV; ++vb)
+            for (int h = 0; h < 4; ++h) {
+              const float tmax = fmaxf(fmaxf(smx[h], smx[4 + h]), fmaxf(smx[8 + h], smx[12 + h]));
+              const float m_new = fmaxf(m_run[h], tmax);
+              const float alpha = (m_new == -INFINITY) ? 1.f : fast_exp2(m_run[h] - m_new);
+              const float pv = (m_new == -INFINITY) ? 0.f : fast_exp2(xs[h] - m_new);
+              if (j & 1)
+                alpha1[h] = alpha;
+              else
+                alpha0[h] = alpha;
+              l_run[h] = l_run[h] * alpha + pv;
+              m_run[h] = m_new;
+              const __nv_bfloat16 hi = __float2bfloat16_rn(pv);
+              const __nv_bfloat16 lo = __float2bfloat16_rn(pv - __bfloat162float(hi));
+              *reinterpret_cast<__nv_bfloat16*>(sP + sw128_offset(h, row, 16)) = hi;
+              *reinterpret_cast<__nv_bfloat16*>(sP + sw128_offset(4 + h, row, 16)) = lo;
+            }
+            fence_proxy_async();
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_PF + 2 * g + (j & 1)));
+          }
+          // ---- accumulate(j - 1) --------------------------------------------------------------------------
+          if (x >= 1) {
+            const int ja = j0 + x - 1;
+            if (!mbar_wait(bar(B_OF + 2 * g + (ja & 1)), (ja >> 1) & 1, s_abort, p.status)) {
+              ok = false;
+              break;
+            }
+            fence_after();
+            uint32_t ov[8];
+            tmem_ld8(trow + kColDo + (ja & 1) * 16, ov);
+            tmem_wait_ld_regs(ov);
 #pragma unroll
-              for (int c = 0; c < 8; ++c) reinterpret_cast<uint4*>(vrow + vb * kBox)[c] = make_uint4(0, 0, 0, 0);
+            for (int h = 0; h < 4; ++h)
+              o_acc[h] = o_acc[h] * ((ja & 1) ? alpha1[h] : alpha0[h]) + __uint_as_float(ov[h]) + __uint_as_float(ov[4 + h]);
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_OR + 2 * g + (ja & 1)));
           }
         }
-        fence_proxy_async();
-        fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_PF + 2 * g + (j & 1)));
+        if (!ok) break;
+        j0 += cnt;
+        ++sigma;
       }
-      // ---- accumulate(j - 1) ------------------------------------------------------------------------
-      if (j >= 1) {
-        const int ja = j - 1;
-        if (!mbar_wait(bar(B_OF + 2 * g + (ja & 1)), (ja >> 1) & 1, s_abort, p.status)) break;
-        fence_after();
-        uint32_t ov[8];
-        tmem_ld8(trow + kColDo + (ja & 1) * 16, ov);
-        tmem_wait_ld_regs(ov);
+      // ---- this group's partial of the segment (empty when the group had no tile in it) ----------------
+      const bool starts_before = sg.kb == 0 && sg.ta > 0;
+      const bool ends_after = sg.kb + sg.cnt == n && sg.ta + sg.cnt < row_tiles(p, sg.b);
+      const size_t rec = (!starts_before && !ends_after)
+                             ? tc_rec_direct(sg.b, kvh, p.n_kv, g)
+                             : tc_rec_edge(p.batch, p.n_kv, p.ctas, kvh, cta, starts_before ? 0 : 1, g);
+      float* wo = p.ws_o + rec * p.rep * p.rv;
+      float* wml = p.ws_ml + rec * p.rep * 5;
 #pragma unroll
-        for (int h = 0; h < 4; ++h)
-          o_acc[h] = o_acc[h] * ((ja & 1) ? alpha1[h] : alpha0[h]) + __uint_as_float(ov[h]) + __uint_as_float(ov[4 + h]);
-        fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_OR + 2 * g + (ja & 1)));
+      for (int h = 0; h < 4; ++h) {
+        float v = l_run[h];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (h < p.rep) {
+          if (lane == 0) wml[h * 5 + 1 + quarter] = v;
+          if (quarter == 0 && lane == 0) wml[h * 5] = m_run[h];
+          if (row < p.rv) wo[h * p.rv + row] = o_acc[h];
+        }
       }
-    }
-    // ---- this group's partial -> shared memory -----------------------------------------------------
-    float* s_o = reinterpret_cast<float*>(smem + Lay::OFF_O);
-#pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      float v = l_run[h];
-#pragma unroll
-      for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0) s_lsum[(g * 4 + quarter) * 4 + h] = v;
-      s_o[(g * 4 + h) * 128 + row] = o_acc[h];
-    }
-    if (quarter == 0 && lane == 0) {
-#pragma unroll
-      for (int h = 0; h < 4; ++h) s_m[g * 4 + h] = m_run[h];
     }
   }
   // every role reaches this point warp-converged
   fence_before();
   __syncthreads();
-
-  // ---- merge the two groups and write this split's partial (unnormalised O, m, l) ----------------
-  if (warp >= 16) {
-    const float* s_o = reinterpret_cast<const float*>(smem + Lay::OFF_O);
-    const size_t item = ((size_t)(b * p.n_kv + kvh) * p.splits + split) * p.rep;
-    for (int idx = (warp - 16) * 32 + lane; idx < p.rep * p.rv; idx += 256) {
-      const int h = idx / p.rv, c = idx - h * p.rv;
-      const float m0 = s_m[h], m1 = s_m[4 + h];
-      const float M = fmaxf(m0, m1);
-      float acc = 0.f, lsum = 0.f;
-      if (M != -INFINITY) {
-        const float w0 = m0 == -INFINITY ? 0.f : fast_exp2(m0 - M);
-        const float w1 = m1 == -INFINITY ? 0.f : fast_exp2(m1 - M);
-        const float l0 = s_lsum[h] + s_lsum[4 + h] + s_lsum[8 + h] + s_lsum[12 + h];
-        const float l1 = s_lsum[16 + h] + s_lsum[20 + h] + s_lsum[24 + h] + s_lsum[28 + h];
-        acc = s_o[h * 128 + c] * w0 + s_o[(4 + h) * 128 + c] * w1;
-        lsum = l0 * w0 + l1 * w1;
-      }
-      p.ws_o[(item + h) * p.rv + c] = acc;
-      if (c == 0) {
-        p.ws_ml[(item + h) * 2 + 0] = M;
-        p.ws_ml[(item + h) * 2 + 1] = lsum;
-      }
-    }
-  }
   if (warp == 1) {
     fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols) : "memory");

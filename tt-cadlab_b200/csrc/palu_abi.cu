@@ -124,26 +124,26 @@ bool use_tc(const palu_decode_dims* d, bool recon) {
   return tc_supported(d, recon);
 }
 
-// One CTA per SM. A CTA costs its tiles plus a fixed setup/drain share worth about 3.3 tiles (TMEM and
-// barrier setup, U load, pipeline fill and drain, the partial's epilogue; measured on B200 at r = 64:
-// ~1.36 us per 128-token tile, ~4.4 us fixed). Pick the split count that minimises
-// waves x (tiles per split + 3.3), fewer splits on ties (the merge also reads every split).
+// CTAs per KV head for the tcgen05 kernel, whose CTAs split each KV head's row-ordered tiles into equal
+// ranges: one CTA per SM in a single wave (SMs / n_kv per KV head), but at least 4 tiles per CTA when every
+// row attends the whole cache.
 int choose_splits_tc(const palu_decode_dims* d) {
   if (d->splits > 0) return d->splits < palu::kMaxSplits ? d->splits : palu::kMaxSplits;
-  const long items = (long)d->batch * d->n_kv_heads;
-  const long tiles = (d->max_seq + palu::tc::kTile - 1) / palu::tc::kTile;
-  const long G = device_sms();
-  int best = 1;
-  long best_cost = -1;
-  for (long s = 1; s <= 64 && s <= tiles; ++s) {
-    const long waves = (items * s + G - 1) / G;
-    const long cost = waves * (10 * ((tiles + s - 1) / s) + 33);
-    if (best_cost < 0 || cost < best_cost) {
-      best_cost = cost;
-      best = (int)s;
-    }
-  }
-  return best;
+  const long tiles = (long)d->batch * ((d->max_seq + palu::tc::kTile - 1) / palu::tc::kTile);
+  long c = device_sms() / d->n_kv_heads;
+  if (c > tiles / 4) c = tiles / 4;
+  if (c < 1) c = 1;
+  if (c > palu::kMaxSplits) c = palu::kMaxSplits;
+  return (int)c;
+}
+
+// Workspace of the tcgen05 path: [256 B status header][O records][(m, l x 4) records].
+size_t ws_tc_o_bytes(const palu_decode_dims* d, int ctas) {
+  return (palu::tc_n_records(d->batch, d->n_kv_heads, ctas) * rep_of(d) * d->r_v * 4 + 255) / 256 * 256;
+}
+size_t ws_tc_bytes(const palu_decode_dims* d, int ctas) {
+  return kWsHeader + ws_tc_o_bytes(d, ctas) + palu::tc_n_records(d->batch, d->n_kv_heads, ctas) * rep_of(d) * 5 * 4 +
+         256;
 }
 
 int splits_for(const palu_decode_dims* d, bool recon) {
@@ -188,7 +188,7 @@ int launch_tc(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& m
   auto kern = palu::tc::palu_decode_tc_kernel<KBK, KBV>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::TOTAL) != cudaSuccess)
     return cuda_check("cudaFuncSetAttribute(decode tc)");
-  kern<<<dim3(p.splits, p.n_kv, p.batch), palu::tc::kThreads, Lay::TOTAL, stream>>>(mk, mv, mt, p);
+  kern<<<dim3(p.ctas, p.n_kv, 1), palu::tc::kThreads, Lay::TOTAL, stream>>>(mk, mv, mt, p);
   return cuda_check("decode tc kernel launch");
 }
 
@@ -232,7 +232,7 @@ int run_tc(const void* q, const void* k, const void* v, const void* u_k, int64_t
   p.rk = d->r_k;
   p.rv = d->r_v;
   p.max_seq = d->max_seq;
-  p.splits = splits;
+  p.ctas = splits;
   p.rep = rep_of(d);
   p.scale_log2 = scale * palu::kLog2e;
   const int kbk = d->r_k > 64 ? 2 : 1, kbv = d->r_v > 64 ? 2 : 1;
@@ -293,16 +293,17 @@ int run_decode(bool recon, const void* q, const void* k, const void* v, const vo
   if (out_dtype != PALU_BF16 && out_dtype != PALU_F32) return fail(PALU_ERR_INVALID, "out_dtype must be bf16 or f32");
   const bool tc = use_tc(d, recon);
   const int splits = tc ? choose_splits_tc(d) : choose_splits(d);
-  if (!workspace || workspace_bytes < ws_bytes(d, splits))
+  const size_t need = tc ? ws_tc_bytes(d, splits) : ws_bytes(d, splits);
+  if (!workspace || workspace_bytes < need)
     return fail(PALU_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu bytes needed", workspace_bytes,
-                ws_bytes(d, splits));
+                need);
   if (tc && reinterpret_cast<uintptr_t>(cs_pairs) % 16 != 0)
     return fail(PALU_ERR_INVALID, "cs_tab (packed) must be 16-byte aligned");
   if (tc && reinterpret_cast<uintptr_t>(u_k) % 16 != 0)
     return fail(PALU_ERR_INVALID, "w_rot/u_k must be 16-byte aligned");
   float* ws_o = reinterpret_cast<float*>(static_cast<char*>(workspace) + kWsHeader);
   float* ws_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + kWsHeader +
-                                          (ws_floats_o(d, splits) * 4 + 255) / 256 * 256);
+                                          (tc ? ws_tc_o_bytes(d, splits) : (ws_floats_o(d, splits) * 4 + 255) / 256 * 256));
 
   palu::DecodeParams p;
   p.q = static_cast<const __nv_bfloat16*>(q);
@@ -324,10 +325,39 @@ int run_decode(bool recon, const void* q, const void* k, const void* v, const vo
   p.ld_u = (int)u_k_ld;
   p.rep = rep_of(d);
   p.scale_log2 = scale * palu::kLog2e;
-  if (tc)
+  if (tc) {
     st = run_tc(q, k, v, u_k, u_k_ld, cs_pairs, cur_pos, workspace, ws_o, ws_ml, d, splits, scale, stream);
-  else
-    st = recon ? dispatch_rv<true>(p, stream) : dispatch_rv<false>(p, stream);
+    if (st) return st;
+    palu::CombineTcParams c;
+    c.ws_o = ws_o;
+    c.ws_ml = ws_ml;
+    c.cur_pos = cur_pos;
+    c.u_v = static_cast<const __nv_bfloat16*>(u_v);
+    c.out = out;
+    c.out_f32 = out_dtype == PALU_F32;
+    c.batch = d->batch;
+    c.n_q = d->n_q_heads;
+    c.n_kv = d->n_kv_heads;
+    c.rep = p.rep;
+    c.ctas = splits;
+    c.r_lat = d->r_v;
+    c.r_out = u_v ? 128 : d->r_v;
+    c.max_seq = d->max_seq;
+    // Programmatic dependent launch: the merge's prologue overlaps the decode kernel's tail.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(d->n_q_heads, d->batch);
+    cfg.blockDim = dim3(palu::kCombineThreads);
+    cfg.dynamicSmemBytes = u_v ? d->r_v * 4 : 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, palu::palu_combine_tc_kernel, c) != cudaSuccess) return cuda_check("combine kernel launch");
+    return cuda_check("combine kernel launch");
+  }
+  st = recon ? dispatch_rv<true>(p, stream) : dispatch_rv<false>(p, stream);
   if (st) return st;
 
   palu::CombineParams c;
@@ -398,8 +428,9 @@ int32_t palu_choose_splits(const palu_decode_dims* dims) {
 
 size_t palu_workspace_bytes(const palu_decode_dims* dims) {
   if (!dims || dims->n_kv_heads <= 0 || dims->n_q_heads <= 0) return 0;
-  const int a = choose_splits(dims), b = choose_splits_tc(dims);
-  return ws_bytes(dims, a > b ? a : b);
+  // enough for either kernel family, so palu_set_kernel may switch between calls
+  const size_t a = ws_bytes(dims, choose_splits(dims)), b = ws_tc_bytes(dims, choose_splits_tc(dims));
+  return a > b ? a : b;
 }
 
 int palu_set_kernel(int32_t which) {
@@ -441,7 +472,7 @@ int palu_decode_attn_static(const void* q, const void* k_lat, const void* v_lat,
   g_err.clear();
   int st = validate(dims, true, u_v != nullptr);
   if (st) return st;
-  const size_t need = ws_bytes(dims, splits_for(dims, true));
+  const size_t need = use_tc(dims, true) ? ws_tc_bytes(dims, choose_splits_tc(dims)) : ws_bytes(dims, choose_splits(dims));
   if (need > kStaticScratchBytes)
     return fail(PALU_ERR_WORKSPACE, "palu_decode_attn_static: these shapes need %zu bytes of scratch, more than the "
                 "%zu-byte static scratch; use palu_decode_attn with a caller workspace", need, kStaticScratchBytes);

@@ -73,6 +73,26 @@ PALU_DEVINL float2 unpack_bf16(uint32_t v) {
   return __bfloat1622float2(b);
 }
 
+// Partial records of the tcgen05 decode (decode_tc.cuh: one CTA per (tile range, KV head), two groups
+// per CTA): a batch row wholly inside one CTA has a direct pair (one record per group); a CTA's first
+// segment, when its row began in an earlier CTA (side 0), and its last segment, when its row continues in
+// a later one (side 1), have the CTA's edge pairs. Each record: O [rep][r_v] and (m, l x 4) [rep][5].
+__host__ __device__ inline size_t tc_rec_direct(int b, int kvh, int n_kv, int g) {
+  return ((size_t)b * n_kv + kvh) * 2 + g;
+}
+__host__ __device__ inline size_t tc_rec_edge(int batch, int n_kv, int ctas, int kvh, int c, int side, int g) {
+  return (size_t)batch * n_kv * 2 + (((size_t)kvh * ctas + c) * 2 + side) * 2 + g;
+}
+__host__ __device__ inline size_t tc_n_records(int batch, int n_kv, int ctas) {
+  return (size_t)batch * n_kv * 2 + (size_t)n_kv * ctas * 4;
+}
+// 128-token tiles of a row that attends positions 0..cur_pos (clamped to [0, max_seq)).
+PALU_DEVINL int tc_row_tiles(const int32_t* cur_pos, int b, int max_seq) {
+  int L = cur_pos[b] + 1;
+  L = L < 0 ? 0 : (L > max_seq ? max_seq : L);
+  return (L + 127) / 128;
+}
+
 PALU_DEVINL float fast_exp2(float x) {  // ex2.approx: exp2(-inf) = 0
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
