@@ -330,8 +330,8 @@ def main():
     achieved = alg_bytes / (per_launch_ms * 1e-3) / 1e9
     peak, peak_kind = peaks()
     tr = traffic_record()
-    kernel_name = ("palu_decode_tc_kernel" if _lib.kernel_for(d) == _lib.PALU_KERNEL_TC
-                   else "palu_decode_mma_kernel")
+    kernel_name = ("palu_decode_tc_kernel + palu_combine_tc_kernel" if _lib.kernel_for(d) == _lib.PALU_KERNEL_TC
+                   else "palu_decode_mma_kernel + palu_combine_kernel")
 
     if rank == 0:
         cpu = None
@@ -349,7 +349,7 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": (tr or {}).get("bytes_per_launch"),
-                         "kernel": kernel_name + " + palu_combine_kernel (one decode op)",
+                         "kernel": kernel_name + " (one decode op)",
                          "algorithmic_bytes": alg_bytes},
             "cpu_baseline": cpu,
             "gpu_launches": 2 * args.steps,
