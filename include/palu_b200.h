@@ -57,7 +57,9 @@ typedef struct palu_decode_dims {
   int32_t r_k;        /* K latent width: a multiple of 16 up to 128, or of 32 up to 256 */
   int32_t r_v;        /* V latent width: a multiple of 16 up to 128, or of 32 up to 256 */
   int32_t max_seq;    /* cache rows per (batch row, latent head) */
-  int32_t splits;     /* split-K partitions per (batch row, KV head); 0 = choose for this GPU */
+  int32_t splits;     /* work partitions; 0 = choose for this GPU. tcgen05 kernel: CTAs per KV head, each
+                         taking an equal share of the KV head's 128-token tiles over all batch rows;
+                         mma.sync kernel: split-K partitions per (batch row, KV head) */
 } palu_decode_dims;
 
 /*
@@ -101,10 +103,11 @@ int palu_decode_attn_static(const void* q, const void* k_lat, const void* v_lat,
                             const void* u_v, const void* cs_pairs, const int32_t* cur_pos, void* out,
                             int32_t out_dtype, const palu_decode_dims* dims, float scale, palu_stream_t stream);
 
-/* Device bytes palu_decode_attn / palu_plain_gqa_decode need for their split-K partials. */
+/* Device bytes palu_decode_attn / palu_plain_gqa_decode need for their partial results (enough for either
+ * kernel family, so palu_set_kernel may change between calls). */
 size_t palu_workspace_bytes(const palu_decode_dims* dims);
 
-/* The split count a call with dims->splits == 0 uses on the current device. */
+/* The partition count (see palu_decode_dims.splits) a call with dims->splits == 0 uses on the current device. */
 int32_t palu_choose_splits(const palu_decode_dims* dims);
 
 /*
