@@ -289,29 +289,47 @@ def main():
     value = B / (ms * 1e-3)   # global batch rows per second (each rank does the same per-rank work)
 
     # ---- e2e through the C ABI with host buffers ---------------------------------------------------
-    q_h = torch.randn(B, n_q, 128).to(torch.bfloat16).pin_memory()
-    nk_h = torch.randn(B, n_kv, R).to(torch.bfloat16).pin_memory()
-    nv_h = torch.randn(B, n_kv, R).to(torch.bfloat16).pin_memory()
-    pos_h = torch.full((B,), S - 1, dtype=torch.int32).pin_memory()
+    # One step = the step's inputs (q, new K/V latents, positions) from one pinned host buffer to the GPU in
+    # one copy, append, decode + merge, and the output back to pinned host memory; steps run back to back
+    # (each step's inputs would depend on the previous step's output in a decode loop, so nothing overlaps
+    # across steps). The step is captured once as a CUDA graph and replayed, as a serving loop would.
+    sizes = [B * n_q * 128 * 2, B * n_kv * R * 2, B * n_kv * R * 2, B * 4]
+    offs = [0]
+    for n_b in sizes:
+        offs.append(offs[-1] + (n_b + 255) // 256 * 256)
+    in_h = torch.empty(offs[-1], dtype=torch.uint8).pin_memory()
+    in_d = torch.empty(offs[-1], dtype=torch.uint8, device=dev)
+    views = lambda buf: (buf[offs[0]:offs[0] + sizes[0]].view(torch.bfloat16).view(B, n_q, 128),
+                         buf[offs[1]:offs[1] + sizes[1]].view(torch.bfloat16).view(B, n_kv, R),
+                         buf[offs[2]:offs[2] + sizes[2]].view(torch.bfloat16).view(B, n_kv, R),
+                         buf[offs[3]:offs[3] + sizes[3]].view(torch.int32))
+    q_h, nk_h, nv_h, pos_h = views(in_h)
+    q_h.copy_(torch.randn(B, n_q, 128).to(torch.bfloat16))
+    nk_h.copy_(torch.randn(B, n_kv, R).to(torch.bfloat16))
+    nv_h.copy_(torch.randn(B, n_kv, R).to(torch.bfloat16))
+    pos_h.fill_(S - 1)
+    q_d, nk_d, nv_d, pos_d = views(in_d)
     out_h = torch.empty(B, n_q, R, dtype=torch.bfloat16).pin_memory()
-    q_d, nk_d, nv_d, pos_d = (torch.empty_like(t, device=dev) for t in (q_h, nk_h, nv_h, pos_h))
 
     def e2e_step():
-        q_d.copy_(q_h, non_blocking=True)
-        nk_d.copy_(nk_h, non_blocking=True)
-        nv_d.copy_(nv_h, non_blocking=True)
-        pos_d.copy_(pos_h, non_blocking=True)
+        in_d.copy_(in_h, non_blocking=True)
         fused.append_latents(nk_d, nv_d, pos_d, L["k"], L["v"])
         fused.decode(q_d, L["k"], L["v"], L["u"], L["cs"], pos_d, out=out, workspace=ws_buf)
         out_h.copy_(out, non_blocking=True)
 
     for _ in range(3):
         e2e_step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        e2e_step()
+    for _ in range(3):
+        graph.replay()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        e2e_step()
+        graph.replay()
     e1.record(stream)
     barrier()
     e2e_ms = e0.elapsed_time(e1) / args.steps
@@ -319,7 +337,8 @@ def main():
         tt = torch.tensor([e2e_ms], device=dev)
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
         e2e_ms = float(tt.item())
-    h2d = sum(t.numel() * t.element_size() for t in (q_h, nk_h, nv_h, pos_h))
+    del graph
+    h2d = in_h.numel()
     d2h = out_h.numel() * out_h.element_size()
 
     # ---- roofline of the op on this rank -----------------------------------------------------------
