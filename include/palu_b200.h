@@ -89,13 +89,19 @@ int palu_decode_attn(const void* q, const void* k_lat, const void* v_lat, const 
                      palu_stream_t stream);
 
 /*
- * palu_decode_attn without a caller workspace: allocates nothing. No reference counterpart (the Tensix
- * op sizes its own circular buffers); for callers that cannot hand over device memory.
- * Arguments and results as palu_decode_attn. The split-K partials and status word live in a static
- * 8 MiB device array, one per device: shapes whose palu_workspace_bytes() exceeds 8 MiB are rejected
- * with PALU_ERR_WORKSPACE. Calls that overlap in time on one device (other streams, other host
- * threads) race on that array; calls in one stream are ordered and safe. The first call on each
- * device sets the array up with synchronous CUDA calls, so make it before any stream capture.
+ * palu_decode_attn without a caller workspace: allocates nothing. No counterpart in the reference (the
+ * Tensix op sizes its own circular buffers). It is for callers that hold only the tensors a framework
+ * hands them and have no device allocator of their own, e.g. a plugin bound over a plain C FFI inside a
+ * framework whose caching allocator owns most of device memory (a raw cudaMalloc there can fail, and
+ * would bypass the framework's accounting), or a decode loop that must not call cudaMalloc/cudaFree per
+ * step because those calls can synchronize the device.
+ * Arguments and results as palu_decode_attn. The partial results and status word live in a static
+ * 8 MiB device array, one per device, held until the process exits: shapes whose palu_workspace_bytes()
+ * exceeds 8 MiB are rejected with PALU_ERR_WORKSPACE. Every call rewrites each partial result that its
+ * merge reads, so stale contents from the previous call are never used. Calls that overlap in time on
+ * one device (other streams, other host threads) race on that array; calls in one stream are ordered
+ * and safe. The first call on each device sets the array up (its address, and a zeroed status word) with
+ * synchronous CUDA calls, so make it before any stream capture.
  * A bounded device wait that expires is recorded in the array's status word, which this entry point
  * does not report; use palu_decode_attn + palu_read_status where that report is needed.
  */

@@ -1,7 +1,9 @@
 """palu_decode_attn_static (the entry point that allocates nothing) against palu_decode_attn.
 
-Both are called through the C ABI with the same arguments; the static variant keeps its split-K
-partials in the library's static device scratch instead of a caller workspace. Two calls in a row with
+The static variant serves callers that cannot allocate a workspace: a plugin that only holds the tensors
+its framework passes in, or a decode loop that must not call cudaMalloc per step. Both entry points are
+called through the C ABI with the same arguments; the static variant keeps its partial results in the
+library's static device scratch instead of a caller workspace. Two calls in a row with
 different queries and positions must each match the workspace entry point within the parity bar the
 other GPU tests use (max-abs relative <= 2e-2, mean-abs relative <= 1e-3), so stale scratch contents
 from the first call cannot leak into the second. This file is collected last so that it runs both

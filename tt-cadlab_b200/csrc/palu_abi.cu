@@ -379,11 +379,11 @@ int run_decode(bool recon, const void* q, const void* k, const void* v, const vo
 
 // ---- static-scratch variant (palu_decode_attn_static) ----------------------------------------------
 
-// The split-K partials and status word of palu_decode_attn_static live in this module-global array, one
+// The partial results and status word of palu_decode_attn_static live in this module-global array, one
 // copy per device, so that entry point allocates nothing. 8 MiB holds every call whose
-// palu_workspace_bytes() fits it, e.g. B = 32, 8 KV heads, 4 query heads each, r_v = 64 at up to
-// 28 splits. All calls on one device share it: calls that overlap in time (other streams, other
-// host threads) race on it.
+// palu_workspace_bytes() fits it, e.g. B = 32, 8 KV heads, 4 query heads each, r_v = 64 (1.2 MB of
+// partial records for the tcgen05 kernel). All calls on one device share it: calls that overlap in time
+// (other streams, other host threads) race on it.
 constexpr size_t kStaticScratchBytes = size_t(8) << 20;
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
