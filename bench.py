@@ -211,6 +211,74 @@ def workload_config(ws, batch=B_PER_GPU):
                   f"(L2 is 126 MB)"}
 
 
+def run_decoder(args, ws, rank, local):
+    """``--workload decoder``: greedy decode steps of the 32-layer Llama-3.1-8B-shaped Palu decoder
+    (palu_b200/model.py; the reference's decode loop, palu_tt/generate.py:40-62) at batch 64 per GPU
+    group with 4096 cached positions, per-layer ranks drawn from {32, 48, 64, 96, 128} (seed 7). Weights
+    random (seeded); the latent caches hold seeded N(0, 1) values for positions 0..4095 (a step's cost does
+    not depend on them); the step (all layers, LM head, argmax) is one CUDA graph, replayed with the step's
+    tokens and positions. Tensor parallel over N GPUs: KV heads and the MLP hidden dimension sharded, two
+    all-reduces per layer. Prints one JSON line with decode tokens/s for the whole job."""
+    from palu_b200.model import DecoderConfig, PaluDecoder, mixed_ranks
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    cfg = DecoderConfig()
+    B, ctx = args.batch, 4096
+    ranks = mixed_ranks(cfg.n_layers, seed=7)
+    model = PaluDecoder(cfg, ranks, max_batch=B, max_seq=ctx + args.steps + args.warmup + 8, seed=11,
+                        device=str(dev), rank=rank, world=ws)
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    for L in model.layers:
+        a = L["attn"]
+        a.k_cache[:, :, :ctx].normal_(generator=g)
+        a.v_cache[:, :, :ctx].normal_(generator=g)
+    graph = model.capture_decode(B)
+    tok = torch.randint(0, cfg.vocab, (B,), generator=g, device=dev)
+    graph.tokens.copy_(tok)
+
+    def step(i):
+        graph.pos.fill_(ctx + i)
+        nxt = graph.replay()
+        graph.tokens.copy_(nxt)
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record()
+        for i in range(args.steps):
+            step(args.warmup + 3 + i)
+        e1.record()
+        if ws > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if ws > 1:
+        tt = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        ms = float(tt.item())
+    del graph
+    if rank == 0:
+        print(json.dumps({
+            "metric": "decode tokens/s, 32-layer Llama-3.1-8B-shaped Palu decoder (greedy, CUDA graph per step)",
+            "value": B / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random weights, seeded latent caches)",
+            "config": {"workload": "decoder_32l_b64_ctx4096", "layers": cfg.n_layers, "batch": B,
+                       "context": ctx, "ranks_seed": 7, "parallelism": f"tp{ws} (KV heads + MLP hidden)"},
+            "gpu_launches": None, "clocks": clk.summary()}), flush=True)
+    if ws > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -220,12 +288,19 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--clock-soak", type=float, default=2.0, help="seconds of untimed steps sampled for clocks")
     ap.add_argument("--batch", type=int, default=B_PER_GPU, help="batch rows per GPU (profiling cases)")
+    ap.add_argument("--workload", default="decode_op", choices=["decode_op", "decoder"],
+                    help="decode_op: the fused decode-attention op (the default bench line); decoder: the "
+                         "32-layer Palu decoder's greedy decode steps")
     ap.add_argument("--kernel", default="auto", choices=["auto", "tc", "mma"],
                     help="decode kernel family: tcgen05 (tc), legacy mma.sync (mma) or the library's choice")
     args = ap.parse_args()
     ws, rank, local = dist_env()
     if args.impl == "reference":
         return run_reference(args, ws, rank)
+    if args.workload == "decoder":
+        if args.batch == B_PER_GPU:
+            args.batch = 64
+        return run_decoder(args, ws, rank, local)
 
     from palu_b200 import _lib, fused
     _lib.set_kernel({"auto": _lib.PALU_KERNEL_AUTO, "tc": _lib.PALU_KERNEL_TC, "mma": _lib.PALU_KERNEL_MMA}[args.kernel])

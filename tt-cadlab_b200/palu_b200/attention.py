@@ -38,12 +38,15 @@ class PaluAttention:
     factors (``convert.LowRank``: k_VT [n_kv, r_k, dim], k_U [n_kv, head_dim, r_k], v_VT, v_U, with
     G-LRD groups repeated per head as ``load_palu_dir`` returns them). ``shard`` selects this rank's
     KV heads (``shard.KVShard``); the layer output is then all-reduced over the default process group.
+    ``proj_dtype`` is the dtype of the q / latent / output projections: fp32 (default) keeps the checkpoint
+    values exact, bf16 halves their weight traffic (the reference's device weights are bf16).
     """
 
     def __init__(self, wq: torch.Tensor, wo: torch.Tensor, lowrank: LowRank, n_heads: int, n_kv_heads: int, *,
                  max_batch: int, max_seq: int, head_dim: int = 128, rope_theta: float = 500000.0,
                  rope_scaling: Optional[dict] = LLAMA3_SCALING, shard: Optional[KVShard] = None,
-                 device: str = "cuda", cache_dtype: torch.dtype = torch.bfloat16):
+                 device: str = "cuda", cache_dtype: torch.dtype = torch.bfloat16,
+                 proj_dtype: torch.dtype = torch.float32):
         if head_dim != fused.HEAD_DIM:
             raise RuntimeError(f"head_dim must be {fused.HEAD_DIM}, got {head_dim}")
         gs = lowrank.group_size
@@ -61,9 +64,10 @@ class PaluAttention:
 
         qs, ks = sh.q, sh.kv
         wq_meta = reverse_permute(wq.float(), n_heads, n_heads * head_dim, dim)
-        # Projections are kept (and applied) in fp32: the checkpoint values are exact in it, and the only
-        # rounding left on the path is the bf16 of q and of the cached latents, as on the device.
-        f32 = torch.float32
+        # Projections in proj_dtype (fp32 by default: the checkpoint values are exact in it, and the only
+        # rounding left on the path is the bf16 of q and of the cached latents, as on the device).
+        f32 = proj_dtype
+        self.proj_dtype = proj_dtype
         self.wq = wq_meta[qs.start * head_dim:qs.stop * head_dim].to(dev, f32)           # [nh*hd, dim]
         # one latent projection per local group: the group's first head carries its VT (convert.py:266-276)
         first = [g * gs for g in sh.groups]
@@ -127,10 +131,11 @@ class PaluAttention:
         if B > self.max_batch:
             raise RuntimeError(f"batch {B} exceeds the cache's {self.max_batch} rows")
         pos = current_pos.to(self.device, torch.int32).reshape(B)
-        q = (xb @ self.wq.T).view(B, self.nh, self.head_dim)
+        xp = xb.to(self.proj_dtype)
+        q = (xp @ self.wq.T).float().view(B, self.nh, self.head_dim)
         q = self._rotate(q, pos.clamp(min=0).long()).to(torch.bfloat16)
-        k_new = (xb @ self.wk_lat.T).view(B, self.ng, self.r_k).to(self.k_cache.dtype)
-        v_new = (xb @ self.wv_lat.T).view(B, self.ng, self.r_v).to(self.v_cache.dtype)
+        k_new = (xp @ self.wk_lat.T).view(B, self.ng, self.r_k).to(self.k_cache.dtype)
+        v_new = (xp @ self.wv_lat.T).view(B, self.ng, self.r_v).to(self.v_cache.dtype)
         kc, vc = self.k_cache[:B], self.v_cache[:B]
         self.append_op(k_new, v_new, pos, kc, vc)
         attn = self.attend_op(q[None], kc, self.w_rot, self.cs_tab, vc, self.head_dim_v, pos, u_v=self.u_v,
@@ -150,8 +155,9 @@ class PaluAttention:
         rows = slice(user_id, user_id + 1) if shape4 else slice(0, B)
         if P > self.max_seq or rows.stop > self.max_batch:
             raise RuntimeError(f"prompt of {P} tokens / cache rows {rows} exceed the cache")
-        lat_k = (xb @ self.wk_lat.T).view(B, P, self.ng, self.r_k).transpose(1, 2)
-        lat_v = (xb @ self.wv_lat.T).view(B, P, self.ng, self.r_v).transpose(1, 2)
+        xp = xb.to(self.proj_dtype)
+        lat_k = (xp @ self.wk_lat.T).float().view(B, P, self.ng, self.r_k).transpose(1, 2)
+        lat_v = (xp @ self.wv_lat.T).float().view(B, P, self.ng, self.r_v).transpose(1, 2)
         self.k_cache[rows, :, :P] = lat_k.to(self.k_cache.dtype)
         self.v_cache[rows, :, :P] = lat_v.to(self.v_cache.dtype)
         gs_local = self.nkv // self.ng
@@ -162,7 +168,7 @@ class PaluAttention:
         V = torch.einsum("bhpr,hrd->bhpd", lv, self._u_v32) if self.grouped else lv
         p_idx = torch.arange(P, device=self.device)
         K = self._rotate(K.transpose(1, 2), p_idx[None]).transpose(1, 2)                # [B, nkv, P, hd]
-        q = (xb @ self.wq.T).view(B, P, self.nh, self.head_dim)
+        q = (xp @ self.wq.T).float().view(B, P, self.nh, self.head_dim)
         q = self._rotate(q, p_idx[None]).transpose(1, 2)                               # [B, nh, P, hd]
         attn = torch.nn.functional.scaled_dot_product_attention(
             q, K.repeat_interleave(rep, dim=1), V.repeat_interleave(rep, dim=1), is_causal=True, scale=self.scale)

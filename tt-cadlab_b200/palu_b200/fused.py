@@ -50,7 +50,7 @@ def trans_mat_tile() -> torch.Tensor:
 
 def w_rot_from_u_k(u_k: torch.Tensor) -> torch.Tensor:
     """u_k [n_kv, r_k, hd] -> w_rot [n_kv, r_k, 2 hd] = [u_k | u_k @ T] (fused.py:49-51)."""
-    return torch.cat([u_k, u_k @ rope_transformation_matrix(u_k.shape[-1]).to(u_k.dtype)], dim=-1)
+    return torch.cat([u_k, u_k @ rope_transformation_matrix(u_k.shape[-1]).to(u_k.device, u_k.dtype)], dim=-1)
 
 
 def chunk_size(seq_len: int) -> int:
@@ -130,7 +130,7 @@ def pack_cs_table(cs_tab: torch.Tensor) -> torch.Tensor:
     dt = _lib.PALU_F32 if t.dtype == torch.float32 else _lib.PALU_BF16
     _lib.check(_lib.load().palu_pack_cs_table(t.data_ptr(), t.stride(0), dt, out.data_ptr(), t.shape[0],
                                               _lib.stream_handle(t.device)))
-    if len(_PACK_CACHE) > 16:
+    if len(_PACK_CACHE) > 256:  # one entry per distinct table (a model holds one per layer)
         _PACK_CACHE.clear()
     _PACK_CACHE[key] = out
     return out

@@ -1,0 +1,178 @@
+"""Palu decoder on B200: a Llama-3.1-8B-shaped decoder whose attention layers are ``PaluAttention``.
+
+The reference assembles its model from tt_transformers (palu_tt/model.py:52-95, ``build_model``) and
+decodes greedily (palu_tt/generate.py:40-62: ``decode_step`` runs one token for every batch row at a
+position, ``greedy`` takes the argmax). This module is the B200 counterpart of that loop around the hot
+path: per layer RMSNorm -> Palu attention (latent caches + the fused decode op) -> residual -> RMSNorm ->
+SwiGLU MLP -> residual; then the final RMSNorm, the LM head and the argmax.
+
+Parallelism across ranks (one process per GPU, ``torch.distributed`` over NCCL): attention shards KV heads
+(``shard.KVShard``), the MLP shards its hidden dimension (w1 / w3 rows, w2 columns); each layer
+all-reduces its attention output and its MLP output, [B, dim] each. Embedding and LM head are replicated.
+
+Weights are random (seeded), in the checkpoint layouts ``PaluAttention`` takes (HF head order for wq / wo,
+``convert.LowRank`` factors); no checkpoint is read. GEMMs outside the fused op run in bf16 through torch
+(cuBLAS): library GEMMs, not this package's kernels.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+
+from palu_b200.attention import LLAMA3_SCALING, PaluAttention
+from palu_b200.convert import LowRank
+from palu_b200.shard import KVShard
+
+
+@dataclass
+class DecoderConfig:
+    """Model shape (Llama-3.1-8B by default)."""
+    dim: int = 4096
+    n_layers: int = 32
+    n_heads: int = 32
+    n_kv_heads: int = 8
+    ffn_dim: int = 14336
+    vocab: int = 128256
+    norm_eps: float = 1e-5
+    rope_theta: float = 500000.0
+    rope_scaling: Optional[dict] = field(default_factory=lambda: dict(LLAMA3_SCALING))
+    head_dim: int = 128
+
+
+def mixed_ranks(n_layers: int, seed: int, choices: Sequence[int] = (32, 48, 64, 96, 128)) -> List[Tuple[int, int]]:
+    """Per-layer (r_k, r_v), drawn from ``choices`` with ``seed``: the mixed-rank decoder config. The
+    reference pads a layer's per-head ranks to the layer maximum (convert.py:148-199), so one rank pair
+    per layer describes it."""
+    g = torch.Generator().manual_seed(seed)
+    pick = lambda: int(choices[int(torch.randint(len(choices), (1,), generator=g))])
+    return [(pick(), pick()) for _ in range(n_layers)]
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """x [..., dim] fp32 -> x / rms(x) * w, fp32."""
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+
+
+class PaluDecoder:
+    """Decoder of ``cfg.n_layers`` layers with Palu attention, random weights from ``seed``.
+
+    ``ranks``: per-layer (r_k, r_v) (``mixed_ranks``); ``world`` / ``rank``: tensor-parallel ranks (the
+    default process group, when world > 1). Caches hold ``max_batch`` rows of ``max_seq`` positions.
+    ``proj_dtype``: dtype of every weight matrix (bf16 for the full model; fp32 for exact comparisons).
+    ``keep_source`` keeps each layer's checkpoint-layout weights (wq, wo, LowRank, full w1 / w3 / w2) in
+    ``layers[i]["src"]``, for comparisons against a reference model built from the same weights.
+    """
+
+    def __init__(self, cfg: DecoderConfig, ranks: Sequence[Tuple[int, int]], *, max_batch: int, max_seq: int,
+                 seed: int = 0, device: str = "cuda", rank: int = 0, world: int = 1,
+                 proj_dtype: torch.dtype = torch.bfloat16, keep_source: bool = False):
+        if len(ranks) != cfg.n_layers:
+            raise ValueError(f"{len(ranks)} rank pairs for {cfg.n_layers} layers")
+        if cfg.ffn_dim % world or cfg.n_kv_heads % world:
+            raise ValueError(f"ffn_dim {cfg.ffn_dim} and n_kv_heads {cfg.n_kv_heads} must divide by world {world}")
+        self.cfg, self.rank, self.world = cfg, rank, world
+        self.device, self.dtype = torch.device(device), proj_dtype
+        dev, dt = self.device, proj_dtype
+        g = torch.Generator(device=dev).manual_seed(seed)
+        D, hd = cfg.dim, cfg.head_dim
+
+        def randn(*shape, scale):
+            # drawn on the model's device from one seed: every rank of a run draws the same weights
+            return (torch.randn(*shape, generator=g, device=dev) * scale).to(dt)
+
+        self.embed = randn(cfg.vocab, D, scale=1.0)
+        self.layers = []
+        f_lo, f_hi = rank * cfg.ffn_dim // world, (rank + 1) * cfg.ffn_dim // world
+        for (r_k, r_v) in ranks:
+            wq = randn(cfg.n_heads * hd, D, scale=D ** -0.5)          # q_proj weight [n_heads * hd, dim]
+            wo = randn(D, cfg.n_heads * hd, scale=(cfg.n_heads * hd) ** -0.5)  # o_proj weight [dim, n_heads * hd]
+            lr = LowRank(k_VT=randn(cfg.n_kv_heads, r_k, D, scale=D ** -0.5).float(),
+                         k_U=randn(cfg.n_kv_heads, hd, r_k, scale=r_k ** -0.5).float(),
+                         v_VT=randn(cfg.n_kv_heads, r_v, D, scale=D ** -0.5).float(),
+                         v_U=randn(cfg.n_kv_heads, hd, r_v, scale=r_v ** -0.5).float())
+            shard = KVShard(rank, world, cfg.n_kv_heads, cfg.n_heads, cfg.n_kv_heads) if world > 1 else None
+            attn = PaluAttention(wq, wo, lr, cfg.n_heads, cfg.n_kv_heads, max_batch=max_batch,
+                                 max_seq=max_seq, head_dim=hd, rope_theta=cfg.rope_theta,
+                                 rope_scaling=cfg.rope_scaling, shard=shard, device=device, proj_dtype=dt)
+            w1f = randn(cfg.ffn_dim, D, scale=D ** -0.5)
+            w3f = randn(cfg.ffn_dim, D, scale=D ** -0.5)
+            w2f = randn(D, cfg.ffn_dim, scale=cfg.ffn_dim ** -0.5)
+            layer = dict(attn=attn, attn_norm=torch.ones(D, device=dev), ffn_norm=torch.ones(D, device=dev),
+                         w1=w1f[f_lo:f_hi].contiguous(), w3=w3f[f_lo:f_hi].contiguous(),
+                         w2=w2f[:, f_lo:f_hi].contiguous())
+            if keep_source:
+                layer["src"] = dict(wq=wq, wo=wo, lowrank=lr, w1=w1f, w3=w3f, w2=w2f)
+            self.layers.append(layer)
+        self.norm = torch.ones(D, device=dev)
+        self.lm_head = randn(cfg.vocab, D, scale=D ** -0.5)
+
+    # ---- pieces -------------------------------------------------------------------------------------
+    def _mlp(self, L: dict, x: torch.Tensor) -> torch.Tensor:
+        """SwiGLU on this rank's hidden slice, summed over ranks: x [N, dim] fp32 -> [N, dim] fp32."""
+        h = x.to(self.dtype)
+        a = torch.nn.functional.silu(h @ L["w1"].t()) * (h @ L["w3"].t())
+        y = (a @ L["w2"].t()).float()
+        if self.world > 1:
+            torch.distributed.all_reduce(y)
+        return y
+
+    def _logits(self, h: torch.Tensor) -> torch.Tensor:
+        """Final norm and LM head: h [N, dim] fp32 -> logits [N, vocab] fp32."""
+        return (rms_norm(h, self.norm, self.cfg.norm_eps).to(self.dtype) @ self.lm_head.t()).float()
+
+    # ---- decode ---------------------------------------------------------------------------------------
+    @torch.no_grad()
+    def decode_logits(self, tokens: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        """One decode step for every batch row (generate.py:40-50): tokens [B] at positions pos [B] ->
+        logits [B, vocab] fp32. Appends the step's latents to every layer's caches."""
+        h = self.embed[tokens.to(self.device)].float()
+        for L in self.layers:
+            h = h + L["attn"].forward_decode(rms_norm(h, L["attn_norm"], self.cfg.norm_eps), pos)
+            h = h + self._mlp(L, rms_norm(h, L["ffn_norm"], self.cfg.norm_eps))
+        return self._logits(h)
+
+    @torch.no_grad()
+    def decode_step(self, tokens: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        """Greedy next tokens [B] (generate.py:53-62)."""
+        return self.decode_logits(tokens, pos).argmax(-1)
+
+    # ---- prefill --------------------------------------------------------------------------------------
+    @torch.no_grad()
+    def prefill_logits(self, tokens: torch.Tensor) -> torch.Tensor:
+        """Prompt tokens [B, P] at positions 0..P-1 (cache rows 0..B-1): fills every layer's caches and
+        returns the logits of the last prompt position [B, vocab] fp32 (generate.py:28-37)."""
+        tokens = tokens.to(self.device)
+        B, P = tokens.shape
+        h = self.embed[tokens].float()                                   # [B, P, dim]
+        for L in self.layers:
+            h = h + L["attn"].forward_prefill(rms_norm(h, L["attn_norm"], self.cfg.norm_eps))
+            h = h + self._mlp(L, rms_norm(h, L["ffn_norm"], self.cfg.norm_eps).reshape(B * P, -1)).view(B, P, -1)
+        return self._logits(h[:, -1])
+
+    # ---- CUDA graph of one decode step ------------------------------------------------------------------
+    def capture_decode(self, batch: int) -> "DecodeGraph":
+        """A CUDA graph of ``decode_step`` for ``batch`` rows: set ``graph.tokens`` / ``graph.pos`` and call
+        ``graph.replay()``; the next tokens land in ``graph.next``. The warm-up call (which builds the
+        library's packed tables and workspaces outside the capture) runs every row at position -1, which
+        the append and the decode op skip, so it leaves the caches as they were."""
+        return DecodeGraph(self, batch)
+
+
+class DecodeGraph:
+    """One captured decode step (see ``PaluDecoder.capture_decode``)."""
+
+    def __init__(self, model: PaluDecoder, batch: int):
+        dev = model.device
+        self.tokens = torch.zeros(batch, dtype=torch.long, device=dev)
+        self.pos = torch.full((batch,), -1, dtype=torch.int32, device=dev)
+        self.next = model.decode_step(self.tokens, self.pos)  # warm-up: position -1 writes nothing
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.next = model.decode_step(self.tokens, self.pos)
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.next

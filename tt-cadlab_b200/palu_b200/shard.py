@@ -71,13 +71,14 @@ def shard_layer_inputs(shard: KVShard, q, k_lat, v_lat, u_k, wo_fused, u_v=None)
 def layer_output_partial(o_local: torch.Tensor, wo_local: torch.Tensor) -> torch.Tensor:
     """This rank's share of the layer output: attention output [B, n_q_local, w] (w = r_v for absorbed V,
     128 with V rebuilt) laid into head_dim slots (``wo_fused`` keeps the first r_v columns of each head
-    slot, attention.py:718-727) and multiplied by the rank's ``wo`` column block -> [B, dim] fp32."""
+    slot, attention.py:718-727) and multiplied by the rank's ``wo`` column block -> [B, dim] fp32. The
+    product runs in ``wo_local``'s dtype (fp32 weights: fp32 throughout; bf16 weights: a bf16 GEMM)."""
     B, nq, w = o_local.shape
     if w > HEAD_DIM:
         raise ValueError(f"attention output width {w} > head_dim {HEAD_DIM}")
-    slots = o_local.new_zeros(B, nq, HEAD_DIM, dtype=torch.float32)
-    slots[..., :w] = o_local.float()
-    return slots.reshape(B, nq * HEAD_DIM) @ wo_local.float().t()
+    slots = o_local.new_zeros(B, nq, HEAD_DIM, dtype=wo_local.dtype)
+    slots[..., :w] = o_local.to(wo_local.dtype)
+    return (slots.reshape(B, nq * HEAD_DIM) @ wo_local.t()).float()
 
 
 def all_reduce_layer_output(partial: torch.Tensor, group=None) -> torch.Tensor:
