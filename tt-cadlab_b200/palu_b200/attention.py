@@ -73,6 +73,11 @@ class PaluAttention:
         first = [g * gs for g in sh.groups]
         self.wk_lat = torch.cat([lowrank.k_VT[h].float() for h in first]).to(dev, f32)  # [ng*r_k, dim]
         self.wv_lat = torch.cat([lowrank.v_VT[h].float() for h in first]).to(dev, f32)  # [ng*r_v, dim]
+        # one GEMM per decode step for q and both latents: wq, wk_lat, wv_lat become views of w_qkv
+        self.w_qkv = torch.cat([self.wq, self.wk_lat, self.wv_lat])
+        nq_rows, nk_rows = self.wq.shape[0], self.wk_lat.shape[0]
+        self.wq, self.wk_lat, self.wv_lat = (self.w_qkv[:nq_rows], self.w_qkv[nq_rows:nq_rows + nk_rows],
+                                             self.w_qkv[nq_rows + nk_rows:])
         u_k = torch.stack([reverse_permute(lowrank.k_U[h].float(), 1, head_dim, self.r_k).T for h in ks])
         self.u_k = u_k.to(dev, bf)                                                        # [nkv, r_k, hd]
         self.w_rot = fused.w_rot_from_u_k(u_k)[None].to(dev, bf)                          # [1, nkv, r_k, 2hd]
@@ -95,6 +100,11 @@ class PaluAttention:
             self.u_v = None
             self.wo = wf.to(dev, f32)
             self.head_dim_v = self.r_v
+        # M-LRD: only the first r_v columns of each head slot of wo_fused are nonzero; the decode step
+        # multiplies the [B, nh * r_v] attention output by those columns alone
+        self.wo_compact = (None if self.grouped else
+                           self.wo.view(dim, self.nh, head_dim)[:, :, :self.r_v].reshape(dim, self.nh * self.r_v)
+                           .contiguous())
 
         cos, sin = fused.cos_sin_tables(head_dim, max_seq, rope_theta, rope_scaling)
         self.cos, self.sin = cos.to(dev), sin.to(dev)                                      # fp32 [>= S, hd]
@@ -118,7 +128,10 @@ class PaluAttention:
 
     def _out(self, attn: torch.Tensor) -> torch.Tensor:
         """[B, nh_local, w] attention output -> [B, dim] layer output (summed over ranks)."""
-        y = layer_output_partial(attn, self.wo)
+        if self.wo_compact is not None and attn.shape[-1] == self.r_v:
+            y = (attn.reshape(attn.shape[0], -1).to(self.wo_compact.dtype) @ self.wo_compact.t()).float()
+        else:
+            y = layer_output_partial(attn, self.wo)
         return all_reduce_layer_output(y) if self.shard.world > 1 else y
 
     @torch.no_grad()
@@ -131,11 +144,12 @@ class PaluAttention:
         if B > self.max_batch:
             raise RuntimeError(f"batch {B} exceeds the cache's {self.max_batch} rows")
         pos = current_pos.to(self.device, torch.int32).reshape(B)
-        xp = xb.to(self.proj_dtype)
-        q = (xp @ self.wq.T).float().view(B, self.nh, self.head_dim)
+        qkv = xb.to(self.proj_dtype) @ self.w_qkv.T
+        nq, nk = self.nh * self.head_dim, self.ng * self.r_k
+        q = qkv[:, :nq].float().view(B, self.nh, self.head_dim)
         q = self._rotate(q, pos.clamp(min=0).long()).to(torch.bfloat16)
-        k_new = (xp @ self.wk_lat.T).view(B, self.ng, self.r_k).to(self.k_cache.dtype)
-        v_new = (xp @ self.wv_lat.T).view(B, self.ng, self.r_v).to(self.v_cache.dtype)
+        k_new = qkv[:, nq:nq + nk].reshape(B, self.ng, self.r_k).to(self.k_cache.dtype)
+        v_new = qkv[:, nq + nk:].reshape(B, self.ng, self.r_v).to(self.v_cache.dtype)
         kc, vc = self.k_cache[:B], self.v_cache[:B]
         self.append_op(k_new, v_new, pos, kc, vc)
         attn = self.attend_op(q[None], kc, self.w_rot, self.cs_tab, vc, self.head_dim_v, pos, u_v=self.u_v,
