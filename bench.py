@@ -202,9 +202,14 @@ def run_reference(args, ws, rank):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(ws, batch=B_PER_GPU):
+def workload_config(ws, batch=B_PER_GPU, paged=0):
     name = "mlrd_r64_b32_s8192" if batch == B_PER_GPU else f"mlrd_r64_b{batch}_s8192"
-    return {"workload": name, "model": "Llama-3.1-8B attention layer (M-LRD, absorbed V)",
+    extra = {}
+    if paged:
+        name += f"_paged{paged}"
+        extra = {"cache": f"paged: blocks of {paged} positions, each row's blocks a seeded random permutation "
+                          f"of the physical blocks"}
+    return {"workload": name, **extra, "model": "Llama-3.1-8B attention layer (M-LRD, absorbed V)",
             "global_batch": batch * ws, "seq_len": S, "rank_k": R, "rank_v": R, "n_q_heads": N_Q,
             "n_kv_heads": N_KV, "kv_heads_per_gpu": N_KV // ws, "parallelism": f"kv-head shard x{ws}",
             "l2": f"no flush: each step reads {batch * ws * (N_KV // ws) * S * 2 * R * 2 / 1e6:.0f} MB of latents per GPU "
@@ -291,6 +296,8 @@ def main():
     ap.add_argument("--workload", default="decode_op", choices=["decode_op", "decoder"],
                     help="decode_op: the fused decode-attention op (the default bench line); decoder: the "
                          "32-layer Palu decoder's greedy decode steps")
+    ap.add_argument("--paged", type=int, default=0, metavar="BLOCK",
+                    help="decode_op over paged caches with blocks of BLOCK positions (0: contiguous caches)")
     ap.add_argument("--kernel", default="auto", choices=["auto", "tc", "mma"],
                     help="decode kernel family: tcgen05 (tc), legacy mma.sync (mma) or the library's choice")
     args = ap.parse_args()
@@ -316,12 +323,25 @@ def main():
     n_kv = N_KV // ws
     n_q = N_Q // ws
     L = make_layer(dev, B, n_q, n_kv, seed=1234 + rank)
+    pt = None
+    if args.paged:
+        # the same latents, each row's blocks scattered over the physical blocks by a seeded permutation
+        bs = args.paged
+        per_row = S // bs
+        g = torch.Generator(device=dev).manual_seed(99 + rank)
+        pt = torch.randperm(B * per_row, generator=g, device=dev).view(B, per_row).to(torch.int32)
+        for name in ("k", "v"):
+            c = L[name]
+            paged = torch.empty(B * per_row, n_kv, bs, R, dtype=c.dtype, device=dev)
+            paged[pt.long().view(-1)] = c.view(B, n_kv, per_row, bs, R).transpose(1, 2).reshape(-1, n_kv, bs, R)
+            L[name] = paged
+            del c, paged
     out = torch.empty(B, n_q, R, dtype=torch.bfloat16, device=dev)
     d = _lib.dims(B, n_q, n_kv, n_kv, R, R, S)
     ws_buf = _lib.new_workspace(d, dev)
 
     def step():
-        fused.decode(L["q"], L["k"], L["v"], L["u"], L["cs"], L["pos"], out=out, workspace=ws_buf)
+        fused.decode(L["q"], L["k"], L["v"], L["u"], L["cs"], L["pos"], out=out, workspace=ws_buf, page_table=pt)
 
     stream = torch.cuda.current_stream(dev)
     for _ in range(max(3, args.warmup)):
@@ -388,8 +408,8 @@ def main():
 
     def e2e_step():
         in_d.copy_(in_h, non_blocking=True)
-        fused.append_latents(nk_d, nv_d, pos_d, L["k"], L["v"])
-        fused.decode(q_d, L["k"], L["v"], L["u"], L["cs"], pos_d, out=out, workspace=ws_buf)
+        fused.append_latents(nk_d, nv_d, pos_d, L["k"], L["v"], page_table=pt)
+        fused.decode(q_d, L["k"], L["v"], L["u"], L["cs"], pos_d, out=out, workspace=ws_buf, page_table=pt)
         out_h.copy_(out, non_blocking=True)
 
     for _ in range(3):
@@ -436,7 +456,7 @@ def main():
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, on device)",
-            "config": workload_config(ws, args.batch),
+            "config": workload_config(ws, args.batch, args.paged),
             "us_per_layer": ms * 1e3, "latent_GBps": achieved,
             "e2e": {"value": B / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},

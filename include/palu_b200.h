@@ -21,6 +21,13 @@
  *                             scaled_dot_product_attention_decode on full K, palu_tt/attention.py:703-706,
  *                             tests/test_palu_sdpa_device.py:58-65, 238-241
  *   palu_pack_cs_table     <- the cs_tab upload of palu_tt/attention.py:70-72 (fused.py:62-73 layout)
+ *   palu_decode_attn_paged / palu_append_latents_paged
+ *                          <- the paged variant of palu_sdpa_decode and paged_update_cache with a page
+ *                             table, which the reference plans but has not built (HANDOFF.md:54-55,
+ *                             126-127; palu_tt/attention.py:86 and :586 assert a non-paged cache). The
+ *                             page-table convention is the stock paged flash-decode op's the plan names
+ *                             as its template: caches [n_blocks][heads][block_size][width], a table
+ *                             [B][blocks per row] of physical block indices.
  */
 #ifndef PALU_B200_H
 #define PALU_B200_H
@@ -108,6 +115,43 @@ int palu_decode_attn(const void* q, const void* k_lat, const void* v_lat, const 
 int palu_decode_attn_static(const void* q, const void* k_lat, const void* v_lat, const void* u_k, int64_t u_k_ld,
                             const void* u_v, const void* cs_pairs, const int32_t* cur_pos, void* out,
                             int32_t out_dtype, const palu_decode_dims* dims, float scale, palu_stream_t stream);
+
+/*
+ * Paged latent caches: fixed-size blocks of positions shared by all rows through a page table.
+ *   table       [batch][table_ld] int32: entry j of row b is the physical block that holds the row's
+ *               positions j*block_size .. (j+1)*block_size - 1
+ *   table_ld    entries per table row, >= ceil(dims->max_seq / block_size)
+ *   block_size  positions per block: 16, 32, 64 or 128
+ *   n_blocks    physical blocks in each cache
+ * The caches are then k_cache [n_blocks][n_groups][block_size][r_k] and v_cache
+ * [n_blocks][n_groups][block_size][r_v] bf16; dims->max_seq is the positions a row may hold. A decode
+ * call reads only the entries that cover positions 0..cur_pos[b]; an entry outside [0, n_blocks) reads
+ * as zero latents (decode) or drops the write (append) rather than touching memory outside the caches.
+ */
+typedef struct palu_page_table {
+  const int32_t* table;
+  int32_t table_ld;
+  int32_t block_size;
+  int32_t n_blocks;
+} palu_page_table;
+
+/*
+ * palu_decode_attn over paged caches: every other argument, the workspace and the output as
+ * palu_decode_attn (same palu_workspace_bytes(dims)). With the same latents at the same logical
+ * positions the result is bit-identical to palu_decode_attn on contiguous caches.
+ */
+int palu_decode_attn_paged(const void* q, const void* k_cache, const void* v_cache, const void* u_k, int64_t u_k_ld,
+                           const void* u_v, const void* cs_pairs, const int32_t* cur_pos,
+                           const palu_page_table* pages, void* out, int32_t out_dtype, void* workspace,
+                           size_t workspace_bytes, const palu_decode_dims* dims, float scale, palu_stream_t stream);
+
+/*
+ * palu_append_latents into paged caches: row b's latents go to row cur_pos[b] % block_size of block
+ * table[b][cur_pos[b] / block_size]. Rows with cur_pos outside [0, max_seq) are skipped.
+ */
+int palu_append_latents_paged(const void* new_k, const void* new_v, const int32_t* cur_pos,
+                              const palu_page_table* pages, void* k_cache, void* v_cache,
+                              const palu_decode_dims* dims, palu_stream_t stream);
 
 /* Device bytes palu_decode_attn / palu_plain_gqa_decode need for their partial results (enough for either
  * kernel family, so palu_set_kernel may change between calls). */

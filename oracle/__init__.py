@@ -29,3 +29,4 @@ from oracle.palu_ref import (  # noqa: F401
     reverse_permute,
 )
 from oracle.metrics import rel_errors, rowwise_rel_errors  # noqa: F401
+from oracle.paged import paged_append, paged_gather, paged_scatter, shuffled_page_table  # noqa: F401

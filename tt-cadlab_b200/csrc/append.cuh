@@ -1,6 +1,6 @@
 // Small bandwidth kernels around the decode op:
-//  * palu_append_kernel: write one decode step's latents into the caches at cur_pos[b]
-//    (the reference's paged_update_cache calls, attention.py:612-625);
+//  * palu_append_kernel: write one decode step's latents into the caches at cur_pos[b], contiguous or
+//    through a page table (the reference's paged_update_cache calls, attention.py:612-625);
 //  * palu_pack_cs_kernel: turn the reference's [S, 256] [cos | sin] table (pair-duplicated,
 //    Meta-interleaved, fused.py:62-73) into the packed 256-byte rows the decode kernels read (half the
 //    bytes): per row, 4 blocks of 16 frequencies, each block 16 fp16 cosines then their 16 sines. One
@@ -21,6 +21,10 @@ struct AppendParams {
   __nv_bfloat16* k_cache;      // [B][n_groups][max_seq][r_k]
   __nv_bfloat16* v_cache;      // [B][n_groups][max_seq][r_v]
   int batch, n_groups, r_k, r_v, max_seq;
+  // Paged caches (null page_table: the layouts above): position pos of row b goes to row pos % bs of
+  // block page_table[b * table_ld + pos / bs] of [n_blocks][n_groups][bs][r] (bs = 1 << blk_shift).
+  const int32_t* page_table;
+  int table_ld, blk_shift, n_blocks;
 };
 
 // One thread per 16-byte chunk of the step's K and V latents.
@@ -33,12 +37,18 @@ __global__ void palu_append_kernel(const AppendParams p) {
     const int b = (int)(bg / p.n_groups);
     const int pos = p.cur_pos[b];
     if (pos < 0 || pos >= p.max_seq) continue;
+    long row = bg * p.max_seq + pos;  // cache row, in rows of r elements
+    if (p.page_table) {
+      const int e = p.page_table[(long)b * p.table_ld + (pos >> p.blk_shift)];
+      if ((unsigned)e >= (unsigned)p.n_blocks) continue;  // an entry outside the caches drops the write
+      row = (((long)e * p.n_groups + (bg - (long)b * p.n_groups)) << p.blk_shift) + (pos & ((1 << p.blk_shift) - 1));
+    }
     if (c < kc) {
       const uint4 v = reinterpret_cast<const uint4*>(p.new_k + bg * p.r_k)[c];
-      reinterpret_cast<uint4*>(p.k_cache + (bg * p.max_seq + pos) * p.r_k)[c] = v;
+      reinterpret_cast<uint4*>(p.k_cache + row * p.r_k)[c] = v;
     } else {
       const uint4 v = reinterpret_cast<const uint4*>(p.new_v + bg * p.r_v)[c - kc];
-      reinterpret_cast<uint4*>(p.v_cache + (bg * p.max_seq + pos) * p.r_v)[c - kc] = v;
+      reinterpret_cast<uint4*>(p.v_cache + row * p.r_v)[c - kc] = v;
     }
   }
 }

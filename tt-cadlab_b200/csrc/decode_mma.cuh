@@ -35,6 +35,10 @@ struct DecodeParams {
   float* ws_ml;             // [B][n_kv][splits][rep][2]  (m in log2 units, l)
   int batch, n_q, n_kv, n_groups, rk, rv, max_seq, splits, ld_u, rep;
   float scale_log2;         // softmax scale * log2(e)
+  // Paged caches (null page_table: the contiguous layouts above): row b's position t sits at row t % bs of
+  // physical block page_table[b * table_ld + t / bs] (bs = 1 << blk_shift) of [n_blocks][n_lat][bs][r].
+  const int32_t* page_table;
+  int table_ld, blk_shift, n_blocks;
 };
 
 constexpr int kMmaThreads = 128;
@@ -85,6 +89,18 @@ __global__ void __launch_bounds__(kMmaThreads, 2) palu_decode_mma_kernel(const D
   unsigned char* sStages = smem + lay.u_bytes();
   __nv_bfloat16* sP = reinterpret_cast<__nv_bfloat16*>(sStages + NS * lay.stage_bytes()) + warp * 8 * 24;
 
+  // Cache row of position tok (tok < L), as an offset in rows of r elements; -1 for a page-table entry
+  // outside [0, n_blocks), whose rows are read as zeros.
+  const int32_t* page_row = p.page_table ? p.page_table + (size_t)b * p.table_ld : nullptr;
+  auto cache_row = [&](int tok) -> long {
+    if (!page_row) return tok;
+    const int e = __ldg(page_row + (tok >> p.blk_shift));
+    if ((unsigned)e >= (unsigned)p.n_blocks) return -1;
+    return (((long)e * n_lat + group) << p.blk_shift) + (tok & ((1 << p.blk_shift) - 1));
+  };
+  const __nv_bfloat16* k_rows = page_row ? p.k : k_base;
+  const __nv_bfloat16* v_rows = page_row ? p.v : v_base;
+
   auto load_tile = [&](int tile, int stage) {
     unsigned char* st = sStages + stage * lay.stage_bytes();
     const uint32_t sK = smem_u32(st), sV = smem_u32(st + lay.k_bytes());
@@ -92,14 +108,16 @@ __global__ void __launch_bounds__(kMmaThreads, 2) palu_decode_mma_kernel(const D
     const int kc = rk / 8;
     for (int c = tid; c < kMmaTile * kc; c += kMmaThreads) {
       const int r = c / kc, col = c - r * kc, tok = row0 + r;
-      const bool ok = tok < L;
-      cp_async16(sK + (r * ldk + col * 8) * 2, k_base + (size_t)(ok ? tok : 0) * rk + col * 8, ok ? 16 : 0);
+      const long cr = tok < L ? cache_row(tok) : -1;
+      const bool ok = cr >= 0;
+      cp_async16(sK + (r * ldk + col * 8) * 2, k_rows + (size_t)(ok ? cr : 0) * rk + col * 8, ok ? 16 : 0);
     }
     constexpr int vc = rv / 8;
     for (int c = tid; c < kMmaTile * vc; c += kMmaThreads) {
       const int r = c / vc, col = c - r * vc, tok = row0 + r;
-      const bool ok = tok < L;
-      cp_async16(sV + (r * ldv + col * 8) * 2, v_base + (size_t)(ok ? tok : 0) * rv + col * 8, ok ? 16 : 0);
+      const long cr = tok < L ? cache_row(tok) : -1;
+      const bool ok = cr >= 0;
+      cp_async16(sV + (r * ldv + col * 8) * 2, v_rows + (size_t)(ok ? cr : 0) * rv + col * 8, ok ? 16 : 0);
     }
     if constexpr (RECON) {
       const uint32_t sT = smem_u32(st + lay.k_bytes() + MmaSmem<RV16, RECON>::v_bytes);

@@ -62,6 +62,11 @@ struct TcParams {
   int* status;              // device status word, 0 = ok
   int batch, n_q, n_kv, n_groups, rk, rv, max_seq, ctas, rep, ld_u;
   float scale_log2;
+  // Paged caches (null page_table: contiguous [B][n_groups][max_seq][r] caches). Row b's positions
+  // j*bs .. j*bs+bs-1 (bs = 1 << blk_shift) sit in physical block page_table[b * table_ld + j] of the
+  // [n_blocks][n_groups][bs][r] caches; the tensor maps then have boxes of bs rows.
+  const int32_t* page_table;
+  int table_ld, blk_shift, n_blocks;
 };
 
 // Work split: the tiles of one KV head over all batch rows, in row order (row b has ceil(L_b / 128)
@@ -521,17 +526,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int sb = kt ? t % NS_K : t % NS_V, use = kt ? t / NS_K : t / NS_V;
           const uint32_t full = kt ? bar(B_KF + sb) : bar(B_VF + 2 * sb + (use & 1));
           const uint32_t empty = bar((kt ? B_KE : B_VE) + sb);
+          // Paged caches: the tile's blocks, looked up before the wait so the loads overlap it. Blocks
+          // past the row's last position repeat its last block (those rows are masked), so no table
+          // entry beyond the row's length is read; an entry outside [0, n_blocks) becomes a coordinate
+          // past the tensor map, which the copy fills with zeros.
+          int blk[kTile / 16];
+          if (p.page_table) {
+            const int32_t* pt = p.page_table + (size_t)it.s.b * p.table_ld;
+            const int last = (it.len - 1) >> p.blk_shift, lb0 = row >> p.blk_shift;
+#pragma unroll
+            for (int i = 0; i < kTile / 16; ++i)
+              if (i < (kTile >> p.blk_shift)) {
+                const int e = __ldg(pt + min(lb0 + i, last));
+                blk[i] = (unsigned)e < (unsigned)p.n_blocks ? e * p.n_groups + lat_head : p.n_blocks * p.n_groups;
+              }
+          }
           if (use >= 1 && !mbar_wait(empty, (use - 1) & 1, s_abort, p.status)) break;
-          if (kt) {
-            mbar_expect_tx(full, Lay::K_BYTES);
-            const uint32_t dst = sbase + Lay::OFF_K + sb * Lay::K_BYTES;
-#pragma unroll
-            for (int kb = 0; kb < KBK; ++kb) tma_load_3d(dst + kb * kBox, &tm_k, full, kb * 64, row, item_lat);
+          const CUtensorMap* tm = kt ? &tm_k : &tm_v;
+          const uint32_t dst = sbase + (kt ? Lay::OFF_K + sb * Lay::K_BYTES : Lay::OFF_V + sb * Lay::V_BYTES);
+          const int nbox = kt ? KBK : KBV;
+          mbar_expect_tx(full, kt ? Lay::K_BYTES : Lay::V_BYTES);
+          if (!p.page_table) {
+            for (int c = 0; c < nbox; ++c) tma_load_3d(dst + c * kBox, tm, full, c * 64, row, item_lat);
           } else {
-            mbar_expect_tx(full, Lay::V_BYTES);
-            const uint32_t dst = sbase + Lay::OFF_V + sb * Lay::V_BYTES;
+            // one box of bs rows per block; bs * 128 B is a whole number of 1 KB swizzle atoms, so the
+            // rows land exactly where one 128-row box would put them
+            const int nsub = kTile >> p.blk_shift, sub_bytes = 128 << p.blk_shift;
 #pragma unroll
-            for (int vb = 0; vb < KBV; ++vb) tma_load_3d(dst + vb * kBox, &tm_v, full, vb * 64, row, item_lat);
+            for (int i = 0; i < kTile / 16; ++i)
+              if (i < nsub)
+                for (int c = 0; c < nbox; ++c) tma_load_3d(dst + c * kBox + i * sub_bytes, tm, full, c * 64, 0, blk[i]);
           }
           issued_kv = j + 1;
           if (kt) {

@@ -181,6 +181,16 @@ int encode(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, c
   return PALU_OK;
 }
 
+// Page-table fields of the kernel parameters (all zero for contiguous caches).
+template <class Params>
+void set_pages(Params& p, const palu_page_table* pg) {
+  p.page_table = pg ? pg->table : nullptr;
+  p.table_ld = pg ? pg->table_ld : 0;
+  p.n_blocks = pg ? pg->n_blocks : 0;
+  p.blk_shift = 0;
+  while (pg && (1 << p.blk_shift) < pg->block_size) ++p.blk_shift;
+}
+
 template <int KBK, int KBV>
 int launch_tc(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mt, const palu::tc::TcParams& p,
               cudaStream_t stream) {
@@ -194,19 +204,23 @@ int launch_tc(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& m
 
 int run_tc(const void* q, const void* k, const void* v, const void* u_k, int64_t u_k_ld, const void* cs_pairs,
            const int32_t* cur_pos, void* workspace, float* ws_o, float* ws_ml, const palu_decode_dims* d, int splits,
-           float scale, cudaStream_t stream) {
+           float scale, const palu_page_table* pg, cudaStream_t stream) {
   CUtensorMap mk, mv, mt;
-  const cuuint64_t items = (cuuint64_t)d->batch * d->n_groups;
+  // Contiguous caches: one item per (batch row, latent head) of max_seq rows, 128-row boxes. Paged caches:
+  // one item per (physical block, latent head) of block_size rows, one block per box.
+  const cuuint64_t items = pg ? (cuuint64_t)pg->n_blocks * d->n_groups : (cuuint64_t)d->batch * d->n_groups;
+  const cuuint64_t rows = pg ? (cuuint64_t)pg->block_size : (cuuint64_t)d->max_seq;
+  const cuuint32_t box_rows = pg ? (cuuint32_t)pg->block_size : 128;
   {
-    const cuuint64_t dims[3] = {(cuuint64_t)d->r_k, (cuuint64_t)d->max_seq, items};
-    const cuuint64_t str[2] = {(cuuint64_t)d->r_k * 2, (cuuint64_t)d->max_seq * d->r_k * 2};
-    const cuuint32_t box[3] = {64, 128, 1};
+    const cuuint64_t dims[3] = {(cuuint64_t)d->r_k, rows, items};
+    const cuuint64_t str[2] = {(cuuint64_t)d->r_k * 2, rows * d->r_k * 2};
+    const cuuint32_t box[3] = {64, box_rows, 1};
     if (int st = encode(&mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, k, dims, str, box, "k_lat")) return st;
   }
   {
-    const cuuint64_t dims[3] = {(cuuint64_t)d->r_v, (cuuint64_t)d->max_seq, items};
-    const cuuint64_t str[2] = {(cuuint64_t)d->r_v * 2, (cuuint64_t)d->max_seq * d->r_v * 2};
-    const cuuint32_t box[3] = {64, 128, 1};
+    const cuuint64_t dims[3] = {(cuuint64_t)d->r_v, rows, items};
+    const cuuint64_t str[2] = {(cuuint64_t)d->r_v * 2, rows * d->r_v * 2};
+    const cuuint32_t box[3] = {64, box_rows, 1};
     if (int st = encode(&mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, v, dims, str, box, "v_lat")) return st;
   }
   {
@@ -235,6 +249,7 @@ int run_tc(const void* q, const void* k, const void* v, const void* u_k, int64_t
   p.ctas = splits;
   p.rep = rep_of(d);
   p.scale_log2 = scale * palu::kLog2e;
+  set_pages(p, pg);
   const int kbk = d->r_k > 64 ? 2 : 1, kbv = d->r_v > 64 ? 2 : 1;
   if (kbk == 1 && kbv == 1) return launch_tc<1, 1>(mk, mv, mt, p, stream);
   if (kbk == 1 && kbv == 2) return launch_tc<1, 2>(mk, mv, mt, p, stream);
@@ -283,7 +298,7 @@ int dispatch_rv(const palu::DecodeParams& p, cudaStream_t s) {
 int run_decode(bool recon, const void* q, const void* k, const void* v, const void* u_k, int64_t u_k_ld,
                const void* u_v, const void* cs_pairs, const int32_t* cur_pos, void* out, int32_t out_dtype,
                void* workspace, size_t workspace_bytes, const palu_decode_dims* d, float scale,
-               cudaStream_t stream) {
+               cudaStream_t stream, const palu_page_table* pg = nullptr) {
   int st = validate(d, recon, u_v != nullptr);
   if (st) return st;
   if (!q || !k || !v || !cur_pos || !out) return fail(PALU_ERR_INVALID, "q, caches, cur_pos and out must be set");
@@ -325,8 +340,9 @@ int run_decode(bool recon, const void* q, const void* k, const void* v, const vo
   p.ld_u = (int)u_k_ld;
   p.rep = rep_of(d);
   p.scale_log2 = scale * palu::kLog2e;
+  set_pages(p, pg);
   if (tc) {
-    st = run_tc(q, k, v, u_k, u_k_ld, cs_pairs, cur_pos, workspace, ws_o, ws_ml, d, splits, scale, stream);
+    st = run_tc(q, k, v, u_k, u_k_ld, cs_pairs, cur_pos, workspace, ws_o, ws_ml, d, splits, scale, pg, stream);
     if (st) return st;
     palu::CombineTcParams c;
     c.ws_o = ws_o;
@@ -413,6 +429,51 @@ int static_scratch(void** out) {
   return PALU_OK;
 }
 
+// Page-table checks shared by the paged decode and append entry points.
+int validate_pages(const palu_page_table* pg, const palu_decode_dims* d) {
+  if (!pg) return fail(PALU_ERR_INVALID, "pages is NULL");
+  if (!pg->table) return fail(PALU_ERR_INVALID, "page table pointer is NULL");
+  if (reinterpret_cast<uintptr_t>(pg->table) % 4 != 0) return fail(PALU_ERR_INVALID, "page table must be 4-byte aligned");
+  const int bs = pg->block_size;
+  if (bs != 16 && bs != 32 && bs != 64 && bs != 128)
+    return fail(PALU_ERR_INVALID, "block_size must be 16, 32, 64 or 128, got %d", bs);
+  if (pg->n_blocks <= 0) return fail(PALU_ERR_INVALID, "n_blocks must be positive, got %d", pg->n_blocks);
+  if ((long long)pg->n_blocks * d->n_groups * bs > 0x7fffffffLL)
+    return fail(PALU_ERR_INVALID, "n_blocks %d x n_groups %d x block_size %d cache rows exceed 2^31", pg->n_blocks,
+                d->n_groups, bs);
+  const long long need = ((long long)d->max_seq + bs - 1) / bs;
+  if (pg->table_ld < need)
+    return fail(PALU_ERR_INVALID, "table_ld %d is below the %lld blocks max_seq %d needs", pg->table_ld, need,
+                d->max_seq);
+  return PALU_OK;
+}
+
+int append(const void* new_k, const void* new_v, const int32_t* cur_pos, void* k_cache, void* v_cache,
+           const palu_decode_dims* d, const palu_page_table* pg, palu_stream_t stream) {
+  if (!new_k || !new_v || !cur_pos || !k_cache || !v_cache)
+    return fail(PALU_ERR_INVALID, "append: every pointer must be set");
+  if (d->batch <= 0 || d->n_groups <= 0 || d->max_seq <= 0)
+    return fail(PALU_ERR_INVALID, "append: batch, n_groups and max_seq must be positive");
+  if (d->r_k % 8 != 0 || d->r_v % 8 != 0 || d->r_k <= 0 || d->r_v <= 0)
+    return fail(PALU_ERR_INVALID, "append: r_k and r_v must be positive multiples of 8 (got %d, %d)", d->r_k, d->r_v);
+  palu::AppendParams p;
+  p.new_k = static_cast<const __nv_bfloat16*>(new_k);
+  p.new_v = static_cast<const __nv_bfloat16*>(new_v);
+  p.cur_pos = cur_pos;
+  p.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  p.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  p.batch = d->batch;
+  p.n_groups = d->n_groups;
+  p.r_k = d->r_k;
+  p.r_v = d->r_v;
+  p.max_seq = d->max_seq;
+  set_pages(p, pg);
+  const long total = (long)d->batch * d->n_groups * (d->r_k / 8 + d->r_v / 8);
+  const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  palu::palu_append_kernel<<<blocks, 256, 0, stream>>>(p);
+  return cuda_check("append kernel launch");
+}
+
 }  // namespace
 
 extern "C" {
@@ -483,6 +544,17 @@ int palu_decode_attn_static(const void* q, const void* k_lat, const void* v_lat,
                     kStaticScratchBytes, dims, scale, stream);
 }
 
+int palu_decode_attn_paged(const void* q, const void* k_cache, const void* v_cache, const void* u_k, int64_t u_k_ld,
+                           const void* u_v, const void* cs_pairs, const int32_t* cur_pos, const palu_page_table* pages,
+                           void* out, int32_t out_dtype, void* workspace, size_t workspace_bytes,
+                           const palu_decode_dims* dims, float scale, palu_stream_t stream) {
+  g_err.clear();
+  if (!dims) return fail(PALU_ERR_INVALID, "dims is NULL");
+  if (int st = validate_pages(pages, dims)) return st;
+  return run_decode(true, q, k_cache, v_cache, u_k, u_k_ld, u_v, cs_pairs, cur_pos, out, out_dtype, workspace,
+                    workspace_bytes, dims, scale, stream, pages);
+}
+
 int palu_plain_gqa_decode(const void* q, const void* k, const void* v, const int32_t* cur_pos, void* out,
                           int32_t out_dtype, void* workspace, size_t workspace_bytes, const palu_decode_dims* dims,
                           float scale, palu_stream_t stream) {
@@ -491,31 +563,22 @@ int palu_plain_gqa_decode(const void* q, const void* k, const void* v, const int
                     workspace_bytes, dims, scale, stream);
 }
 
+
 int palu_append_latents(const void* new_k, const void* new_v, const int32_t* cur_pos, void* k_cache, void* v_cache,
                         const palu_decode_dims* d, palu_stream_t stream) {
   g_err.clear();
   if (!d) return fail(PALU_ERR_INVALID, "dims is NULL");
-  if (!new_k || !new_v || !cur_pos || !k_cache || !v_cache)
-    return fail(PALU_ERR_INVALID, "append: every pointer must be set");
-  if (d->batch <= 0 || d->n_groups <= 0 || d->max_seq <= 0)
-    return fail(PALU_ERR_INVALID, "append: batch, n_groups and max_seq must be positive");
-  if (d->r_k % 8 != 0 || d->r_v % 8 != 0 || d->r_k <= 0 || d->r_v <= 0)
-    return fail(PALU_ERR_INVALID, "append: r_k and r_v must be positive multiples of 8 (got %d, %d)", d->r_k, d->r_v);
-  palu::AppendParams p;
-  p.new_k = static_cast<const __nv_bfloat16*>(new_k);
-  p.new_v = static_cast<const __nv_bfloat16*>(new_v);
-  p.cur_pos = cur_pos;
-  p.k_cache = static_cast<__nv_bfloat16*>(k_cache);
-  p.v_cache = static_cast<__nv_bfloat16*>(v_cache);
-  p.batch = d->batch;
-  p.n_groups = d->n_groups;
-  p.r_k = d->r_k;
-  p.r_v = d->r_v;
-  p.max_seq = d->max_seq;
-  const long total = (long)d->batch * d->n_groups * (d->r_k / 8 + d->r_v / 8);
-  const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
-  palu::palu_append_kernel<<<blocks, 256, 0, stream>>>(p);
-  return cuda_check("append kernel launch");
+  return append(new_k, new_v, cur_pos, k_cache, v_cache, d, nullptr, stream);
+}
+
+int palu_append_latents_paged(const void* new_k, const void* new_v, const int32_t* cur_pos,
+                              const palu_page_table* pages, void* k_cache, void* v_cache, const palu_decode_dims* d,
+                              palu_stream_t stream) {
+  g_err.clear();
+  if (!d) return fail(PALU_ERR_INVALID, "dims is NULL");
+  if (d->n_groups <= 0 || d->max_seq <= 0) return fail(PALU_ERR_INVALID, "append: n_groups and max_seq must be positive");
+  if (int st = validate_pages(pages, d)) return st;
+  return append(new_k, new_v, cur_pos, k_cache, v_cache, d, pages, stream);
 }
 
 int palu_pack_cs_table(const void* cs_tab, int64_t ld, int32_t in_dtype, void* cs_pairs, int32_t rows,

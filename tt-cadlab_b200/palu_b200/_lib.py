@@ -18,7 +18,8 @@ PALU_OK, PALU_ERR_INVALID, PALU_ERR_WORKSPACE, PALU_ERR_CUDA = 0, 1, 2, 3
 PALU_BF16, PALU_F32 = 0, 1
 
 # Every symbol include/palu_b200.h declares (checked by the CPU test suite).
-EXPORTED = ("palu_decode_attn", "palu_decode_attn_static", "palu_workspace_bytes", "palu_choose_splits", "palu_append_latents",
+EXPORTED = ("palu_decode_attn", "palu_decode_attn_static", "palu_decode_attn_paged", "palu_append_latents_paged",
+            "palu_workspace_bytes", "palu_choose_splits", "palu_append_latents",
             "palu_plain_gqa_decode", "palu_pack_cs_table", "palu_set_kernel", "palu_kernel_for", "palu_read_status",
             "palu_last_error", "palu_version")
 PALU_KERNEL_AUTO, PALU_KERNEL_MMA, PALU_KERNEL_TC = 0, 1, 2
@@ -28,6 +29,11 @@ class DecodeDims(ctypes.Structure):
     _fields_ = [("batch", ctypes.c_int32), ("n_q_heads", ctypes.c_int32), ("n_kv_heads", ctypes.c_int32),
                 ("n_groups", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("r_k", ctypes.c_int32),
                 ("r_v", ctypes.c_int32), ("max_seq", ctypes.c_int32), ("splits", ctypes.c_int32)]
+
+
+class PageTable(ctypes.Structure):
+    _fields_ = [("table", ctypes.c_void_p), ("table_ld", ctypes.c_int32), ("block_size", ctypes.c_int32),
+                ("n_blocks", ctypes.c_int32)]
 
 
 _lib = None
@@ -47,6 +53,11 @@ def load() -> ctypes.CDLL:
     lib.palu_decode_attn.restype = ctypes.c_int
     lib.palu_decode_attn_static.argtypes = [vp, vp, vp, vp, i64, vp, vp, vp, vp, i32, dims_p, f32, vp]
     lib.palu_decode_attn_static.restype = ctypes.c_int
+    pages_p = ctypes.POINTER(PageTable)
+    lib.palu_decode_attn_paged.argtypes = [vp, vp, vp, vp, i64, vp, vp, vp, pages_p, vp, i32, vp, sz, dims_p, f32, vp]
+    lib.palu_decode_attn_paged.restype = ctypes.c_int
+    lib.palu_append_latents_paged.argtypes = [vp, vp, vp, pages_p, vp, vp, dims_p, vp]
+    lib.palu_append_latents_paged.restype = ctypes.c_int
     lib.palu_plain_gqa_decode.argtypes = [vp, vp, vp, vp, vp, i32, vp, sz, dims_p, f32, vp]
     lib.palu_plain_gqa_decode.restype = ctypes.c_int
     lib.palu_workspace_bytes.argtypes = [dims_p]
@@ -96,6 +107,14 @@ def stream_handle(device: torch.device) -> int:
 def dims(batch, n_q, n_kv, n_groups, r_k, r_v, max_seq, splits=0) -> DecodeDims:
     return DecodeDims(int(batch), int(n_q), int(n_kv), int(n_groups), 128, int(r_k), int(r_v), int(max_seq),
                       int(splits))
+
+
+def pages(table: torch.Tensor, block_size: int, n_blocks: int) -> PageTable:
+    """palu_page_table for an int32 [B, table_ld] page table (contiguous rows)."""
+    if table.dtype != torch.int32 or table.dim() != 2 or table.stride(1) != 1:
+        raise RuntimeError(f"page table must be a row-major int32 [B, blocks per row] tensor, got "
+                           f"{table.dtype} {tuple(table.shape)}")
+    return PageTable(table.data_ptr(), int(table.stride(0)), int(block_size), int(n_blocks))
 
 
 def workspace_bytes(d: DecodeDims) -> int:

@@ -14,11 +14,17 @@ Per decode step (attention.py:585-733):
 ``forward_prefill`` fills the caches for a prompt and returns the prompt's attention output with torch
 SDPA on the rebuilt K / V (the reference runs its prefill on full K / V too, attention.py:382-516).
 
+Paged caches: with ``paged_attention_config`` (tt_transformers' argument, which the reference accepts and
+asserts is None, attention.py:83-86) the caches are [max_num_blocks, n_groups, block_size, r] and the
+forward methods take the ``page_table`` [B, blocks per row] int32 (attention.py:585-586); the decode
+step then runs palu_decode_attn_paged / palu_append_latents_paged.
+
 Weights follow the reference's layout (palu_tt/convert.py): q / K in Meta (interleaved-pair) head order
 so they meet the interleaved RoPE tables, ``u_k`` = U_kᵀ in Meta order, ``wo_fused`` absorbing U_v.
 """
 from __future__ import annotations
 
+from dataclasses import dataclass
 from typing import Optional
 
 import torch
@@ -29,6 +35,13 @@ from palu_b200.shard import KVShard, all_reduce_layer_output, layer_output_parti
 
 LLAMA3_SCALING = {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
                   "original_max_position_embeddings": 8192}
+
+
+@dataclass
+class PagedAttentionConfig:
+    """Paged cache geometry (the fields of tt_transformers' PagedAttentionConfig)."""
+    block_size: int = 64
+    max_num_blocks: int = 2048
 
 
 class PaluAttention:
@@ -46,7 +59,8 @@ class PaluAttention:
                  max_batch: int, max_seq: int, head_dim: int = 128, rope_theta: float = 500000.0,
                  rope_scaling: Optional[dict] = LLAMA3_SCALING, shard: Optional[KVShard] = None,
                  device: str = "cuda", cache_dtype: torch.dtype = torch.bfloat16,
-                 proj_dtype: torch.dtype = torch.float32):
+                 proj_dtype: torch.dtype = torch.float32,
+                 paged_attention_config: Optional[PagedAttentionConfig] = None):
         if head_dim != fused.HEAD_DIM:
             raise RuntimeError(f"head_dim must be {fused.HEAD_DIM}, got {head_dim}")
         gs = lowrank.group_size
@@ -106,11 +120,19 @@ class PaluAttention:
                            self.wo.view(dim, self.nh, head_dim)[:, :, :self.r_v].reshape(dim, self.nh * self.r_v)
                            .contiguous())
 
-        cos, sin = fused.cos_sin_tables(head_dim, max_seq, rope_theta, rope_scaling)
+        self.paged = paged_attention_config
+        # a paged row holds whole blocks: the tables cover max_seq rounded up to a block
+        tab_len = max_seq if self.paged is None else -(-max_seq // self.paged.block_size) * self.paged.block_size
+        cos, sin = fused.cos_sin_tables(head_dim, tab_len, rope_theta, rope_scaling)
         self.cos, self.sin = cos.to(dev), sin.to(dev)                                      # fp32 [>= S, hd]
-        self.cs_tab = fused.cs_table(cos, sin, max_seq)[None, None].to(dev, bf)           # [1, 1, S, 2hd]
-        self.k_cache = torch.zeros(max_batch, self.ng, max_seq, self.r_k, dtype=cache_dtype, device=dev)
-        self.v_cache = torch.zeros(max_batch, self.ng, max_seq, self.r_v, dtype=cache_dtype, device=dev)
+        self.cs_tab = fused.cs_table(cos, sin, tab_len)[None, None].to(dev, bf)           # [1, 1, S, 2hd]
+        if self.paged is None:
+            self.k_cache = torch.zeros(max_batch, self.ng, max_seq, self.r_k, dtype=cache_dtype, device=dev)
+            self.v_cache = torch.zeros(max_batch, self.ng, max_seq, self.r_v, dtype=cache_dtype, device=dev)
+        else:
+            nb, bs = self.paged.max_num_blocks, self.paged.block_size
+            self.k_cache = torch.zeros(nb, self.ng, bs, self.r_k, dtype=cache_dtype, device=dev)
+            self.v_cache = torch.zeros(nb, self.ng, bs, self.r_v, dtype=cache_dtype, device=dev)
         self.scale = head_dim ** -0.5
         # The two device ops of a decode step (the CUDA library; the tests substitute CPU models here to
         # check the layer algebra on a machine without a GPU).
@@ -134,10 +156,21 @@ class PaluAttention:
             y = layer_output_partial(attn, self.wo)
         return all_reduce_layer_output(y) if self.shard.world > 1 else y
 
+    def _check_pages(self, page_table: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+        if (page_table is None) != (self.paged is None):
+            raise RuntimeError("page_table is required with paged caches and refused without them")
+        if page_table is None:
+            return None
+        if page_table.shape[-1] * self.paged.block_size < self.max_seq:
+            raise RuntimeError(f"page_table rows of {page_table.shape[-1]} blocks of {self.paged.block_size} "
+                               f"cannot hold max_seq {self.max_seq}")
+        return page_table.to(self.device, torch.int32).contiguous()
+
     @torch.no_grad()
-    def forward_decode(self, x: torch.Tensor, current_pos: torch.Tensor) -> torch.Tensor:
-        """x [B, dim] or [1, 1, B, dim]; current_pos [B] ints (each row's position; < 0 skips the row).
-        Returns the layer output in x's layout, fp32."""
+    def forward_decode(self, x: torch.Tensor, current_pos: torch.Tensor,
+                       page_table: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """x [B, dim] or [1, 1, B, dim]; current_pos [B] ints (each row's position; < 0 skips the row);
+        page_table [B, blocks per row] with paged caches. Returns the layer output in x's layout, fp32."""
         shape4 = x.dim() == 4
         xb = (x.reshape(-1, x.shape[-1]) if shape4 else x).to(self.device, torch.float32)
         B = xb.shape[0]
@@ -150,19 +183,28 @@ class PaluAttention:
         q = self._rotate(q, pos.clamp(min=0).long()).to(torch.bfloat16)
         k_new = qkv[:, nq:nq + nk].reshape(B, self.ng, self.r_k).to(self.k_cache.dtype)
         v_new = qkv[:, nq + nk:].reshape(B, self.ng, self.r_v).to(self.v_cache.dtype)
-        kc, vc = self.k_cache[:B], self.v_cache[:B]
-        self.append_op(k_new, v_new, pos, kc, vc)
-        attn = self.attend_op(q[None], kc, self.w_rot, self.cs_tab, vc, self.head_dim_v, pos, u_v=self.u_v,
-                                      scale=self.scale, out_dtype=torch.float32)[0]
+        pt = self._check_pages(page_table)
+        if pt is None:
+            kc, vc = self.k_cache[:B], self.v_cache[:B]
+            self.append_op(k_new, v_new, pos, kc, vc)
+            attn = self.attend_op(q[None], kc, self.w_rot, self.cs_tab, vc, self.head_dim_v, pos, u_v=self.u_v,
+                                  scale=self.scale, out_dtype=torch.float32)[0]
+        else:
+            pt = pt[:B, :(self.max_seq + self.paged.block_size - 1) // self.paged.block_size]
+            self.append_op(k_new, v_new, pos, self.k_cache, self.v_cache, page_table=pt)
+            attn = self.attend_op(q[None], self.k_cache, self.w_rot, self.cs_tab, self.v_cache, self.head_dim_v, pos,
+                                  u_v=self.u_v, scale=self.scale, out_dtype=torch.float32, page_table_tensor=pt)[0]
         y = self._out(attn)
         return y.view(1, 1, B, self.dim) if shape4 else y
 
     @torch.no_grad()
-    def forward_prefill(self, x: torch.Tensor, user_id: Optional[int] = None) -> torch.Tensor:
+    def forward_prefill(self, x: torch.Tensor, user_id: Optional[int] = None,
+                        page_table: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Prompt of P tokens at positions 0..P-1: x [B, P, dim] (cache rows 0..B-1), or [1, 1, P, dim] for
         cache row ``user_id`` (the reference's per-user prefill). Writes the prompt's latents into the
         caches and returns its causal attention output (fp32, x's layout) computed with torch SDPA on K and
-        V rebuilt from the cached (bf16) latents."""
+        V rebuilt from the cached (bf16) latents. With paged caches, ``page_table`` is the whole batch's
+        table [max_batch or B, blocks per row] and the rows' latents go through it (paged_fill_cache)."""
         shape4 = x.dim() == 4
         xb = (x.reshape(1, x.shape[-2], x.shape[-1]) if shape4 else x).to(self.device, torch.float32)
         B, P, _ = xb.shape
@@ -172,12 +214,24 @@ class PaluAttention:
         xp = xb.to(self.proj_dtype)
         lat_k = (xp @ self.wk_lat.T).float().view(B, P, self.ng, self.r_k).transpose(1, 2)
         lat_v = (xp @ self.wv_lat.T).float().view(B, P, self.ng, self.r_v).transpose(1, 2)
-        self.k_cache[rows, :, :P] = lat_k.to(self.k_cache.dtype)
-        self.v_cache[rows, :, :P] = lat_v.to(self.v_cache.dtype)
+        pt = self._check_pages(page_table)
+        if pt is None:
+            self.k_cache[rows, :, :P] = lat_k.to(self.k_cache.dtype)
+            self.v_cache[rows, :, :P] = lat_v.to(self.v_cache.dtype)
+            ck, cv = self.k_cache[rows, :, :P], self.v_cache[rows, :, :P]
+        else:
+            # position t of a row: row t % bs of block table[row, t // bs]; [B, P] indices
+            bs = self.paged.block_size
+            t = torch.arange(P, device=self.device)
+            blk = pt[rows][:, t // bs].long()
+            off = (t % bs)[None].expand(B, P)
+            self.k_cache[blk, :, off] = lat_k.transpose(1, 2).to(self.k_cache.dtype)
+            self.v_cache[blk, :, off] = lat_v.transpose(1, 2).to(self.v_cache.dtype)
+            ck, cv = self.k_cache[blk, :, off].transpose(1, 2), self.v_cache[blk, :, off].transpose(1, 2)
         gs_local = self.nkv // self.ng
         rep = self.nh // self.nkv
-        lk = self.k_cache[rows, :, :P].float().repeat_interleave(gs_local, dim=1)        # [B, nkv, P, r_k]
-        lv = self.v_cache[rows, :, :P].float().repeat_interleave(gs_local, dim=1)
+        lk = ck.float().repeat_interleave(gs_local, dim=1)                               # [B, nkv, P, r_k]
+        lv = cv.float().repeat_interleave(gs_local, dim=1)
         K = torch.einsum("bhpr,hrd->bhpd", lk, self._u_k32)
         V = torch.einsum("bhpr,hrd->bhpd", lv, self._u_v32) if self.grouped else lv
         p_idx = torch.arange(P, device=self.device)

@@ -184,16 +184,21 @@ def workspace_status() -> int:
 
 
 def decode(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, *, u_k_ld=HEAD_DIM, u_v=None, scale=None,
-           out=None, out_dtype=torch.bfloat16, splits=0, workspace=None) -> torch.Tensor:
+           out=None, out_dtype=torch.bfloat16, splits=0, workspace=None, page_table=None) -> torch.Tensor:
     """Low-level entry (no reference-surface validation): the arrays are already in the library's layout.
 
     q [B, nh, 128] bf16; k_latent [B, n_groups, S, r_k]; v_latent [B, n_groups, S, r_v]; u_k rows of
     ``u_k_ld`` elements ([n_kv, r_k, u_k_ld]); cs_pairs [>= S, 64] int32 from ``pack_cs_table``;
-    cur_pos [B] int32; u_v [n_kv, r_v, 128] or None. Returns [B, nh, r_v or 128]."""
-    _lib.require_cuda(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, u_v)
+    cur_pos [B] int32; u_v [n_kv, r_v, 128] or None. Returns [B, nh, r_v or 128].
+    Paged caches: ``page_table`` [B, blocks per row] int32 and k_latent [n_blocks, n_groups, block_size,
+    r_k], v_latent [n_blocks, n_groups, block_size, r_v]; a row then holds blocks per row x block_size
+    positions (palu_decode_attn_paged)."""
+    _lib.require_cuda(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, u_v, page_table)
     B, nh = q.shape[0], q.shape[1]
     n_groups, S, r_k = k_latent.shape[1], k_latent.shape[2], k_latent.shape[3]
     r_v = v_latent.shape[3]
+    if page_table is not None:
+        S = page_table.shape[1] * k_latent.shape[2]
     n_kv = u_k.shape[0]
     d = _lib.dims(B, nh, n_kv, n_groups, r_k, r_v, S, splits or _lib.env_splits())
     width = HEAD_DIM if u_v is not None else r_v
@@ -203,23 +208,35 @@ def decode(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, *, u_k_ld=HEAD_DIM, u_
         workspace = _workspace_for(d, q.device)
     odt = _lib.PALU_F32 if out.dtype == torch.float32 else _lib.PALU_BF16
     sc = HEAD_DIM ** -0.5 if scale is None else float(scale)
-    _lib.check(_lib.load().palu_decode_attn(
-        q.data_ptr(), k_latent.data_ptr(), v_latent.data_ptr(), u_k.data_ptr(), int(u_k_ld), _lib.ptr(u_v),
-        cs_pairs.data_ptr(), cur_pos.data_ptr(), out.data_ptr(), odt, workspace.data_ptr(), workspace.numel(),
-        ctypes.byref(d), sc, _lib.stream_handle(q.device)))
+    if page_table is None:
+        _lib.check(_lib.load().palu_decode_attn(
+            q.data_ptr(), k_latent.data_ptr(), v_latent.data_ptr(), u_k.data_ptr(), int(u_k_ld), _lib.ptr(u_v),
+            cs_pairs.data_ptr(), cur_pos.data_ptr(), out.data_ptr(), odt, workspace.data_ptr(), workspace.numel(),
+            ctypes.byref(d), sc, _lib.stream_handle(q.device)))
+    else:
+        pg = _lib.pages(page_table, k_latent.shape[2], k_latent.shape[0])
+        _lib.check(_lib.load().palu_decode_attn_paged(
+            q.data_ptr(), k_latent.data_ptr(), v_latent.data_ptr(), u_k.data_ptr(), int(u_k_ld), _lib.ptr(u_v),
+            cs_pairs.data_ptr(), cur_pos.data_ptr(), ctypes.byref(pg), out.data_ptr(), odt, workspace.data_ptr(),
+            workspace.numel(), ctypes.byref(d), sc, _lib.stream_handle(q.device)))
     return out
 
 
 def palu_sdpa_decode(q, k_latent, w_rot, cs_tab, v_latent, head_dim_v, cur_pos_tensor, *, rot_step=None,
                      trans_mat=None, u_v=None, scale=None, heads_per_core=None, rot_mode="dst", table_mcast=True,
                      program_config=None, compute_kernel_config=None, memory_config=None,
-                     out_dtype=torch.bfloat16, splits=0) -> torch.Tensor:
+                     out_dtype=torch.bfloat16, splits=0, page_table_tensor=None) -> torch.Tensor:
     """B200 implementation of ``ttnn.transformer.palu_sdpa_decode`` (same positional / keyword surface).
 
     q [1, B, nh, 128] (rotated), k_latent [B, n_groups, S, r_k], w_rot [1, n_kv, r_k, 256],
     cs_tab [1, 1, >= S, 256], v_latent [B, n_groups, S, r_v], cur_pos_tensor [B] ints,
     u_v [1, n_kv, r_v, 128] (in-kernel V). Returns [1, B, nh, head_dim_v]. Raises RuntimeError with
-    the reference's message substrings on envelope violations."""
+    the reference's message substrings on envelope violations.
+
+    ``page_table_tensor`` [B, blocks per row] int32 (the stock paged decode op's keyword; the paged
+    variant the reference plans, HANDOFF.md:126-127): the caches are then paged, k_latent
+    [n_blocks, n_groups, block_size, r_k] and v_latent [n_blocks, n_groups, block_size, r_v], and
+    S = blocks per row x block_size."""
     if rot_mode not in ROT_MODES:
         raise RuntimeError(f"rot_mode must be one of {ROT_MODES}, got {rot_mode!r}")
     if (rot_step is None) != (trans_mat is None):
@@ -234,8 +251,16 @@ def palu_sdpa_decode(q, k_latent, w_rot, cs_tab, v_latent, head_dim_v, cur_pos_t
         raise RuntimeError("k_latent and v_latent must be [B, n_groups, S, r]")
     n_groups, S, r_k = k_latent.shape[1], k_latent.shape[2], k_latent.shape[3]
     r_v = v_latent.shape[3]
-    if k_latent.shape[0] != B or v_latent.shape[:3] != k_latent.shape[:3]:
-        raise RuntimeError("k_latent / v_latent batch, group or sequence dims do not match q")
+    if page_table_tensor is None:
+        if k_latent.shape[0] != B or v_latent.shape[:3] != k_latent.shape[:3]:
+            raise RuntimeError("k_latent / v_latent batch, group or sequence dims do not match q")
+    else:
+        pt = page_table_tensor
+        if pt.dim() != 2 or pt.shape[0] != B:
+            raise RuntimeError(f"page_table_tensor must be [B={B}, blocks per row], got {tuple(pt.shape)}")
+        if v_latent.shape[:3] != k_latent.shape[:3]:
+            raise RuntimeError("paged k_latent / v_latent block, group or block_size dims do not match")
+        S = pt.shape[1] * k_latent.shape[2]
     w = w_rot.reshape(-1, *w_rot.shape[-2:]) if w_rot.dim() >= 3 else w_rot
     if w.dim() != 3 or w.shape[-1] != 2 * HEAD_DIM:
         raise RuntimeError(f"w_rot must be [1, n_kv, r_k, 256] = [u_k | u_k T], got {tuple(w_rot.shape)}")
@@ -279,9 +304,10 @@ def palu_sdpa_decode(q, k_latent, w_rot, cs_tab, v_latent, head_dim_v, cur_pos_t
         raise RuntimeError(f"cur_pos_tensor must hold {B} positions, got {pos.numel()}")
     pos = pos.to(torch.int32).contiguous()
     wb = _bf16(w)
+    pt = None if page_table_tensor is None else page_table_tensor.to(torch.int32).contiguous()
     out = decode(_bf16(q[0]), k_latent.contiguous(), v_latent.contiguous(), wb, pack_cs_table(cs_tab), pos,
                  u_k_ld=wb.shape[-1], u_v=_bf16(u_v.reshape(n_kv, r_v, HEAD_DIM)) if u_v is not None else None,
-                 scale=scale, out_dtype=out_dtype, splits=splits)
+                 scale=scale, out_dtype=out_dtype, splits=splits, page_table=pt)
     return out.unsqueeze(0)
 
 
@@ -304,10 +330,13 @@ def plain_gqa_decode(q, k, v, cur_pos, *, scale=None, out_dtype=torch.bfloat16, 
     return out.unsqueeze(0)
 
 
-def append_latents(new_k, new_v, cur_pos, k_cache, v_cache) -> None:
+def append_latents(new_k, new_v, cur_pos, k_cache, v_cache, page_table=None) -> None:
     """Write one step's latents [B, n_groups, r] into the caches [B, n_groups, S, r] at cur_pos[b]
-    (the reference's paged_update_cache pair, attention.py:622-623)."""
-    _lib.require_cuda(new_k, new_v, cur_pos, k_cache, v_cache)
+    (the reference's paged_update_cache pair, attention.py:622-623). With ``page_table`` [B, blocks per
+    row] int32 (paged_update_cache's keyword) the caches are paged, [n_blocks, n_groups, block_size, r]."""
+    _lib.require_cuda(new_k, new_v, cur_pos, k_cache, v_cache, page_table)
+    if page_table is not None:
+        return _append_paged(new_k, new_v, cur_pos, k_cache, v_cache, page_table)
     B, G, S, r_k = k_cache.shape
     r_v = v_cache.shape[-1]
     if tuple(new_k.shape[-3:]) != (B, G, r_k) or tuple(new_v.shape[-3:]) != (B, G, r_v):
@@ -318,3 +347,21 @@ def append_latents(new_k, new_v, cur_pos, k_cache, v_cache) -> None:
                                                cur_pos.to(torch.int32).contiguous().data_ptr(),
                                                k_cache.data_ptr(), v_cache.data_ptr(), ctypes.byref(d),
                                                _lib.stream_handle(k_cache.device)))
+
+
+def _append_paged(new_k, new_v, cur_pos, k_cache, v_cache, page_table) -> None:
+    n_blocks, G, bs, r_k = k_cache.shape
+    r_v = v_cache.shape[-1]
+    B = page_table.shape[0]
+    if tuple(new_k.shape[-3:]) != (B, G, r_k) or tuple(new_v.shape[-3:]) != (B, G, r_v):
+        raise RuntimeError(f"new latents must be [B, n_groups, r]: got {tuple(new_k.shape)}, {tuple(new_v.shape)}")
+    if tuple(v_cache.shape[:3]) != (n_blocks, G, bs):
+        raise RuntimeError("paged k / v caches must share n_blocks, n_groups and block_size")
+    pt = page_table.to(torch.int32).contiguous()
+    d = _lib.dims(B, G, G, G, r_k, r_v, pt.shape[1] * bs)
+    pg = _lib.pages(pt, bs, n_blocks)
+    nk, nv = _bf16(new_k), _bf16(new_v)
+    _lib.check(_lib.load().palu_append_latents_paged(nk.data_ptr(), nv.data_ptr(),
+                                                     cur_pos.to(torch.int32).contiguous().data_ptr(), ctypes.byref(pg),
+                                                     k_cache.data_ptr(), v_cache.data_ptr(), ctypes.byref(d),
+                                                     _lib.stream_handle(k_cache.device)))
