@@ -223,7 +223,10 @@ def run_decoder(args, ws, rank, local):
     random (seeded); the latent caches hold seeded N(0, 1) values for positions 0..4095 (a step's cost does
     not depend on them); the step (all layers, LM head, argmax) is one CUDA graph, replayed with the step's
     tokens and positions. Tensor parallel over N GPUs: KV heads and the MLP hidden dimension sharded, two
-    all-reduces per layer. Prints one JSON line with decode tokens/s for the whole job."""
+    all-reduces per layer. With ``--paged BLOCK`` every layer's caches are paged (each row's blocks a seeded
+    random permutation of the physical blocks; the page table is a buffer the graph reads). Prints one JSON
+    line with decode tokens/s for the whole job."""
+    from palu_b200.attention import PagedAttentionConfig
     from palu_b200.model import DecoderConfig, PaluDecoder, mixed_ranks
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -234,14 +237,25 @@ def run_decoder(args, ws, rank, local):
     cfg = DecoderConfig()
     B, ctx = args.batch, 4096
     ranks = mixed_ranks(cfg.n_layers, seed=7)
-    model = PaluDecoder(cfg, ranks, max_batch=B, max_seq=ctx + args.steps + args.warmup + 8, seed=11,
-                        device=str(dev), rank=rank, world=ws)
+    max_seq = ctx + args.steps + args.warmup + 8
+    pc, pt = None, None
+    if args.paged:
+        per_row = -(-max_seq // args.paged)
+        pc = PagedAttentionConfig(block_size=args.paged, max_num_blocks=B * per_row)
+        gp = torch.Generator(device=dev).manual_seed(99)
+        pt = torch.randperm(B * per_row, generator=gp, device=dev).view(B, per_row).to(torch.int32)
+    model = PaluDecoder(cfg, ranks, max_batch=B, max_seq=max_seq, seed=11, device=str(dev), rank=rank, world=ws,
+                        paged_attention_config=pc)
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     for L in model.layers:
         a = L["attn"]
-        a.k_cache[:, :, :ctx].normal_(generator=g)
-        a.v_cache[:, :, :ctx].normal_(generator=g)
-    graph = model.capture_decode(B)
+        if pc is None:
+            a.k_cache[:, :, :ctx].normal_(generator=g)
+            a.v_cache[:, :, :ctx].normal_(generator=g)
+        else:
+            a.k_cache.normal_(generator=g)  # every block holds seeded latents (positions past ctx are rewritten)
+            a.v_cache.normal_(generator=g)
+    graph = model.capture_decode(B, page_table=pt)
     tok = torch.randint(0, cfg.vocab, (B,), generator=g, device=dev)
     graph.tokens.copy_(tok)
 
@@ -276,8 +290,10 @@ def run_decoder(args, ws, rank, local):
             "value": B / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random weights, seeded latent caches)",
-            "config": {"workload": "decoder_32l_b64_ctx4096", "layers": cfg.n_layers, "batch": B,
-                       "context": ctx, "ranks_seed": 7, "parallelism": f"tp{ws} (KV heads + MLP hidden)"},
+            "config": {"workload": "decoder_32l_b64_ctx4096" + (f"_paged{args.paged}" if args.paged else ""),
+                       "layers": cfg.n_layers, "batch": B, "context": ctx, "ranks_seed": 7,
+                       "parallelism": f"tp{ws} (KV heads + MLP hidden)",
+                       "cache": f"paged, blocks of {args.paged}" if args.paged else "contiguous"},
             "gpu_launches": None, "clocks": clk.summary()}), flush=True)
     if ws > 1:
         torch.distributed.barrier()

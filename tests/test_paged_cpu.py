@@ -128,3 +128,30 @@ def test_paged_call_applies_the_decode_envelope():
     d = _lib.dims(2, 32, 8, 8, 40, 64, 256)
     st, msg = _paged_call(lib, d, _lib.PageTable(16, 8, 32, 64))
     assert st == _lib.PALU_ERR_INVALID and "r_k" in msg, msg
+
+
+def test_paged_decoder_equals_contiguous_decoder_on_cpu_models():
+    """The decoder with paged caches in every layer (one page table for the batch) gives the contiguous
+    decoder's logits for a prefill and two greedy decode steps."""
+    from palu_b200.attention import PagedAttentionConfig
+    from palu_b200.model import DecoderConfig, PaluDecoder
+    cfg = DecoderConfig(dim=256, n_layers=2, n_heads=4, n_kv_heads=2, ffn_dim=384, vocab=200)
+    B, P, S, bs = 2, 12, 48, 16
+    pc = PagedAttentionConfig(block_size=bs, max_num_blocks=B * S // bs + 2)
+    kw = dict(max_batch=B, max_seq=S, seed=5, device="cpu", proj_dtype=torch.float32)
+    flat = PaluDecoder(cfg, [(32, 16), (16, 32)], **kw)
+    paged = PaluDecoder(cfg, [(32, 16), (16, 32)], paged_attention_config=pc, **kw)
+    for L in flat.layers:
+        _cpu_ops(L["attn"])
+    for L in paged.layers:
+        _cpu_paged_ops(L["attn"])
+    pt = oracle.shuffled_page_table(B, S // bs, pc.max_num_blocks, torch.Generator().manual_seed(6))
+    tokens = torch.randint(0, cfg.vocab, (B, P), generator=torch.Generator().manual_seed(7))
+    want = flat.prefill_logits(tokens)
+    assert torch.equal(paged.prefill_logits(tokens, page_table=pt), want)
+    nxt = want.argmax(-1)
+    for step in range(2):
+        pos = torch.full((B,), P + step, dtype=torch.int32)
+        want = flat.decode_logits(nxt, pos)
+        assert torch.equal(paged.decode_logits(nxt, pos, page_table=pt), want), step
+        nxt = want.argmax(-1)

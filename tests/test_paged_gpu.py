@@ -170,3 +170,32 @@ def test_paged_layer_equals_contiguous_layer(cuda):
         xd = torch.randn(B, dim, generator=g).to(cuda)
         pos = torch.tensor([P + step, P - 1 + 2 * step, 7 * step], dtype=torch.int32, device=cuda)
         assert torch.equal(paged.forward_decode(xd, pos, page_table=pt), flat.forward_decode(xd, pos)), step
+
+
+def test_paged_decoder_step_and_graph_replay(cuda):
+    """The decoder over paged caches: a prefill and an eager greedy step give the contiguous decoder's
+    logits, and one step captured as a CUDA graph (page table in a captured buffer) replays the eager
+    step's tokens."""
+    from palu_b200.attention import PagedAttentionConfig
+    from palu_b200.model import DecoderConfig, PaluDecoder
+    cfg = DecoderConfig(dim=512, n_layers=2, n_heads=4, n_kv_heads=2, ffn_dim=768, vocab=300)
+    B, P, S, bs = 2, 16, 64, 16
+    pc = PagedAttentionConfig(block_size=bs, max_num_blocks=B * S // bs + 3)
+    kw = dict(max_batch=B, max_seq=S, seed=5, device="cuda", proj_dtype=torch.float32)
+    flat = PaluDecoder(cfg, [(32, 64), (48, 32)], **kw)
+    paged = PaluDecoder(cfg, [(32, 64), (48, 32)], paged_attention_config=pc, **kw)
+    pt = oracle.shuffled_page_table(B, S // bs, pc.max_num_blocks, torch.Generator().manual_seed(8)).to(cuda)
+    tokens = torch.randint(0, cfg.vocab, (B, P), generator=torch.Generator().manual_seed(9))
+    want = flat.prefill_logits(tokens)
+    assert torch.equal(paged.prefill_logits(tokens, page_table=pt), want)
+    nxt = want.argmax(-1)
+    pos = torch.full((B,), P, dtype=torch.int32, device=cuda)
+    assert torch.equal(paged.decode_logits(nxt, pos, page_table=pt), flat.decode_logits(nxt, pos))
+    graph = paged.capture_decode(B, page_table=pt)
+    pos1 = pos + 1
+    eager = paged.decode_step(nxt, pos1, page_table=pt)
+    graph.tokens.copy_(nxt)
+    graph.pos.copy_(pos1)
+    replayed = graph.replay().clone()
+    torch.cuda.synchronize()
+    assert torch.equal(eager, replayed)

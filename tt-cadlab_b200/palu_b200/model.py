@@ -21,7 +21,7 @@ from typing import List, Optional, Sequence, Tuple
 
 import torch
 
-from palu_b200.attention import LLAMA3_SCALING, PaluAttention
+from palu_b200.attention import LLAMA3_SCALING, PagedAttentionConfig, PaluAttention
 from palu_b200.convert import LowRank
 from palu_b200.shard import KVShard
 
@@ -63,11 +63,14 @@ class PaluDecoder:
     ``proj_dtype``: dtype of every weight matrix (bf16 for the full model; fp32 for exact comparisons).
     ``keep_source`` keeps each layer's checkpoint-layout weights (wq, wo, LowRank, full w1 / w3 / w2) in
     ``layers[i]["src"]``, for comparisons against a reference model built from the same weights.
+    ``paged_attention_config``: paged latent caches in every layer (``PagedAttentionConfig``); the prefill
+    and decode calls then take the batch's ``page_table`` [B, blocks per row] (tt_transformers' argument).
     """
 
     def __init__(self, cfg: DecoderConfig, ranks: Sequence[Tuple[int, int]], *, max_batch: int, max_seq: int,
                  seed: int = 0, device: str = "cuda", rank: int = 0, world: int = 1,
-                 proj_dtype: torch.dtype = torch.bfloat16, keep_source: bool = False):
+                 proj_dtype: torch.dtype = torch.bfloat16, keep_source: bool = False,
+                 paged_attention_config: Optional[PagedAttentionConfig] = None):
         if len(ranks) != cfg.n_layers:
             raise ValueError(f"{len(ranks)} rank pairs for {cfg.n_layers} layers")
         if cfg.ffn_dim % world or cfg.n_kv_heads % world:
@@ -95,7 +98,8 @@ class PaluDecoder:
             shard = KVShard(rank, world, cfg.n_kv_heads, cfg.n_heads, cfg.n_kv_heads) if world > 1 else None
             attn = PaluAttention(wq, wo, lr, cfg.n_heads, cfg.n_kv_heads, max_batch=max_batch,
                                  max_seq=max_seq, head_dim=hd, rope_theta=cfg.rope_theta,
-                                 rope_scaling=cfg.rope_scaling, shard=shard, device=device, proj_dtype=dt)
+                                 rope_scaling=cfg.rope_scaling, shard=shard, device=device, proj_dtype=dt,
+                                 paged_attention_config=paged_attention_config)
             w1f = randn(cfg.ffn_dim, D, scale=D ** -0.5)
             w3f = randn(cfg.ffn_dim, D, scale=D ** -0.5)
             w2f = randn(D, cfg.ffn_dim, scale=cfg.ffn_dim ** -0.5)
@@ -124,54 +128,59 @@ class PaluDecoder:
 
     # ---- decode ---------------------------------------------------------------------------------------
     @torch.no_grad()
-    def decode_logits(self, tokens: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+    def decode_logits(self, tokens: torch.Tensor, pos: torch.Tensor,
+                      page_table: Optional[torch.Tensor] = None) -> torch.Tensor:
         """One decode step for every batch row (generate.py:40-50): tokens [B] at positions pos [B] ->
         logits [B, vocab] fp32. Appends the step's latents to every layer's caches."""
         h = self.embed[tokens.to(self.device)].float()
         for L in self.layers:
-            h = h + L["attn"].forward_decode(rms_norm(h, L["attn_norm"], self.cfg.norm_eps), pos)
+            h = h + L["attn"].forward_decode(rms_norm(h, L["attn_norm"], self.cfg.norm_eps), pos, page_table)
             h = h + self._mlp(L, rms_norm(h, L["ffn_norm"], self.cfg.norm_eps))
         return self._logits(h)
 
     @torch.no_grad()
-    def decode_step(self, tokens: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+    def decode_step(self, tokens: torch.Tensor, pos: torch.Tensor,
+                    page_table: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Greedy next tokens [B] (generate.py:53-62)."""
-        return self.decode_logits(tokens, pos).argmax(-1)
+        return self.decode_logits(tokens, pos, page_table).argmax(-1)
 
     # ---- prefill --------------------------------------------------------------------------------------
     @torch.no_grad()
-    def prefill_logits(self, tokens: torch.Tensor) -> torch.Tensor:
+    def prefill_logits(self, tokens: torch.Tensor, page_table: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Prompt tokens [B, P] at positions 0..P-1 (cache rows 0..B-1): fills every layer's caches and
         returns the logits of the last prompt position [B, vocab] fp32 (generate.py:28-37)."""
         tokens = tokens.to(self.device)
         B, P = tokens.shape
         h = self.embed[tokens].float()                                   # [B, P, dim]
         for L in self.layers:
-            h = h + L["attn"].forward_prefill(rms_norm(h, L["attn_norm"], self.cfg.norm_eps))
+            h = h + L["attn"].forward_prefill(rms_norm(h, L["attn_norm"], self.cfg.norm_eps), page_table=page_table)
             h = h + self._mlp(L, rms_norm(h, L["ffn_norm"], self.cfg.norm_eps).reshape(B * P, -1)).view(B, P, -1)
         return self._logits(h[:, -1])
 
     # ---- CUDA graph of one decode step ------------------------------------------------------------------
-    def capture_decode(self, batch: int) -> "DecodeGraph":
-        """A CUDA graph of ``decode_step`` for ``batch`` rows: set ``graph.tokens`` / ``graph.pos`` and call
-        ``graph.replay()``; the next tokens land in ``graph.next``. The warm-up call (which builds the
-        library's packed tables and workspaces outside the capture) runs every row at position -1, which
-        the append and the decode op skip, so it leaves the caches as they were."""
-        return DecodeGraph(self, batch)
+    def capture_decode(self, batch: int, page_table: Optional[torch.Tensor] = None) -> "DecodeGraph":
+        """A CUDA graph of ``decode_step`` for ``batch`` rows: set ``graph.tokens`` / ``graph.pos`` (and, with
+        paged caches, ``graph.page_table``, captured from ``page_table``) and call ``graph.replay()``; the
+        next tokens land in ``graph.next``. The warm-up call (which builds the library's packed tables and
+        workspaces outside the capture) runs every row at position -1, which the append and the decode op
+        skip, so it leaves the caches as they were."""
+        return DecodeGraph(self, batch, page_table)
 
 
 class DecodeGraph:
     """One captured decode step (see ``PaluDecoder.capture_decode``)."""
 
-    def __init__(self, model: PaluDecoder, batch: int):
+    def __init__(self, model: PaluDecoder, batch: int, page_table: Optional[torch.Tensor] = None):
         dev = model.device
         self.tokens = torch.zeros(batch, dtype=torch.long, device=dev)
         self.pos = torch.full((batch,), -1, dtype=torch.int32, device=dev)
-        self.next = model.decode_step(self.tokens, self.pos)  # warm-up: position -1 writes nothing
+        # the table the graph reads (rewrite it in place between replays as blocks are allocated)
+        self.page_table = None if page_table is None else page_table.to(dev, torch.int32).contiguous().clone()
+        self.next = model.decode_step(self.tokens, self.pos, self.page_table)  # warm-up: position -1 writes nothing
         torch.cuda.synchronize(dev)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            self.next = model.decode_step(self.tokens, self.pos)
+            self.next = model.decode_step(self.tokens, self.pos, self.page_table)
 
     def replay(self) -> torch.Tensor:
         self.graph.replay()
