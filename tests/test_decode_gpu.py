@@ -266,3 +266,40 @@ def test_kernel_families_agree_and_report_ok_status(cuda):
     assert_close(outs[_lib.PALU_KERNEL_TC], ref, "tc vs oracle")
     assert_close(outs[_lib.PALU_KERNEL_MMA], ref, "mma vs oracle")
     assert_close(outs[_lib.PALU_KERNEL_TC], outs[_lib.PALU_KERNEL_MMA], "tc vs mma")
+
+
+@pytest.mark.parametrize("paged", [False, True], ids=["contiguous", "paged32"])
+def test_repeated_calls_are_bit_identical(cuda, kernel, paged):
+    """200 calls on the same inputs give the first call's output bit for bit. The shape (256 rows of 1024
+    positions: many row segments per CTA) is the one where a missing proxy fence before the RoPE table
+    slot's release showed up most often on B200 (over a third of the calls differed)."""
+    from palu_b200 import _lib, fused
+    B, S, r, bs = 256, 1024, 64, 32
+    g = torch.Generator(device=cuda).manual_seed(1234)
+    k = torch.randn(B, 8, S, r, generator=g, device=cuda).to(torch.bfloat16)
+    v = torch.randn(B, 8, S, r, generator=g, device=cuda).to(torch.bfloat16)
+    u = (torch.randn(8, r, 128, generator=g, device=cuda) / r ** 0.5).to(torch.bfloat16)
+    q = torch.randn(B, 32, 128, generator=g, device=cuda).to(torch.bfloat16)
+    pos = torch.full((B,), S - 1, dtype=torch.int32, device=cuda)
+    cos, sin = oracle.cos_sin_tables(128, S, THETA, LLAMA3)
+    cs = fused.pack_cs_table(fused.cs_table(cos, sin, S).to(cuda, torch.bfloat16))
+    pt = None
+    if paged:
+        per_row = S // bs
+        pt = torch.randperm(B * per_row, generator=g, device=cuda).view(B, per_row).to(torch.int32)
+        k = torch.empty(B * per_row, 8, bs, r, dtype=k.dtype, device=cuda).index_copy_(
+            0, pt.long().view(-1), k.view(B, 8, per_row, bs, r).transpose(1, 2).reshape(-1, 8, bs, r))
+        v = torch.empty(B * per_row, 8, bs, r, dtype=v.dtype, device=cuda).index_copy_(
+            0, pt.long().view(-1), v.view(B, 8, per_row, bs, r).transpose(1, 2).reshape(-1, 8, bs, r))
+    d = _lib.dims(B, 32, 8, 8, r, r, S)
+    ws = _lib.new_workspace(d, cuda)
+    out = torch.empty(B, 32, r, dtype=torch.float32, device=cuda)
+    fused.decode(q, k, v, u, cs, pos, out=out, workspace=ws, page_table=pt)
+    first = out.clone()
+    differ = 0
+    for _ in range(200):
+        fused.decode(q, k, v, u, cs, pos, out=out, workspace=ws, page_table=pt)
+        differ += int(not torch.equal(out, first))
+    torch.cuda.synchronize()
+    assert _lib.read_status(ws) == 0
+    assert differ == 0, f"{differ} of 200 calls differ from the first"

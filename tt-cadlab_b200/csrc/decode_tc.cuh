@@ -769,6 +769,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // Every lane has used its table values: the slot may refill. (An arrive issued while this warp's
         // tcgen05.ld is in flight waits for that load, measured at ~260 cycles on B200, hence after the math.)
+        // The chunk was read through the generic proxy and the refill writes it through the async proxy
+        // (TMA), so the reads are ordered before the release by fence.proxy.async. Without the fence the
+        // refill overwrote rows whose reads were still in flight (the first rows of the chunk, which the TMA
+        // writes first): on B200 a few percent of calls then differed in the last bits of one batch row.
+        fence_proxy_async();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(B_TE + sb));
         if (sub == 0 && i >= 1) {
