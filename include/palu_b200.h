@@ -21,6 +21,8 @@
  *                             scaled_dot_product_attention_decode on full K, palu_tt/attention.py:703-706,
  *                             tests/test_palu_sdpa_device.py:58-65, 238-241
  *   palu_pack_cs_table     <- the cs_tab upload of palu_tt/attention.py:70-72 (fused.py:62-73 layout)
+ *   palu_rope_q_append     <- nlp_create_qkv_heads_decode's split + rotary_embedding_llama on q + the two
+ *                             paged_update_cache calls, palu_tt/attention.py:601-625, in one kernel
  *   palu_decode_attn_paged / palu_append_latents_paged
  *                          <- the paged variant of palu_sdpa_decode and paged_update_cache with a page
  *                             table, which the reference plans but has not built (HANDOFF.md:54-55,
@@ -152,6 +154,24 @@ int palu_decode_attn_paged(const void* q, const void* k_cache, const void* v_cac
 int palu_append_latents_paged(const void* new_k, const void* new_v, const int32_t* cur_pos,
                               const palu_page_table* pages, void* k_cache, void* v_cache,
                               const palu_decode_dims* dims, palu_stream_t stream);
+
+/*
+ * One decode step's q rotation and latent append in one kernel (replaces the split of
+ * nlp_create_qkv_heads_decode, rotary_embedding_llama on q and the two paged_update_cache calls,
+ * palu_tt/attention.py:601-625).
+ *   qkv      [B][ld] (qkv_dtype PALU_BF16 or PALU_F32): per row the n_q_heads * 128 query values (Meta pair
+ *            order), then n_groups * r_k K latents, then n_groups * r_v V latents (the fused projection)
+ *   cos, sin [>= max_seq][128] f32: cos / sin of frequency j at columns 2j and 2j + 1
+ *   cur_pos  [B]: q is rotated at cur_pos clamped to [0, max_seq); the latents are appended at cur_pos
+ *            (rows outside [0, max_seq) append nothing)
+ *   q_out    [B][n_q_heads][128] bf16 (4-byte aligned), the decode op's q
+ *   k_cache, v_cache, pages: as palu_append_latents (pages NULL) or palu_append_latents_paged
+ * dims: batch, n_q_heads, n_groups, head_dim (128), r_k, r_v, max_seq. Each product of the rotation and
+ * their sum are rounded separately, so q is bit-identical to rotating in fp32 tensor ops and rounding to bf16.
+ */
+int palu_rope_q_append(const void* qkv, int64_t ld, int32_t qkv_dtype, const float* cos, const float* sin,
+                       const int32_t* cur_pos, void* q_out, void* k_cache, void* v_cache, const palu_page_table* pages,
+                       const palu_decode_dims* dims, palu_stream_t stream);
 
 /* Device bytes palu_decode_attn / palu_plain_gqa_decode need for their partial results (enough for either
  * kernel family, so palu_set_kernel may change between calls). */

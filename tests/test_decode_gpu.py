@@ -303,3 +303,42 @@ def test_repeated_calls_are_bit_identical(cuda, kernel, paged):
     torch.cuda.synchronize()
     assert _lib.read_status(ws) == 0
     assert differ == 0, f"{differ} of 200 calls differ from the first"
+
+
+@pytest.mark.parametrize("qkv_dtype", [torch.bfloat16, torch.float32], ids=["bf16", "f32"])
+@pytest.mark.parametrize("paged", [False, True], ids=["contiguous", "paged16"])
+def test_rope_q_append_matches_tensor_ops(cuda, qkv_dtype, paged):
+    """palu_rope_q_append (q rotation + latent append in one kernel) against the same step in fp32 torch ops
+    (the layer's rotation, bf16 rounding, then palu_append_latents): q and both caches bit for bit. Rows at
+    positions -1 (rotated at 0, nothing appended), 0, a block edge, max_seq - 1 and max_seq (rotated at
+    max_seq - 1, nothing appended)."""
+    from palu_b200 import fused
+    g = torch.Generator().manual_seed(77)
+    B, nh, G, r_k, r_v, S, bs = 6, 32, 8, 48, 96, 256, 16
+    qkv = torch.randn(B, nh * 128 + G * (r_k + r_v), generator=g).to(cuda, qkv_dtype)
+    pos = torch.tensor([-1, 0, 15, 16, S - 1, S], dtype=torch.int32, device=cuda)
+    cos, sin = oracle.cos_sin_tables(128, S, THETA, LLAMA3)
+    cos, sin = cos[:S].contiguous().to(cuda), sin[:S].contiguous().to(cuda)
+    if paged:
+        n_blocks = B * (S // bs) + 2
+        pt = oracle.shuffled_page_table(B, S // bs, n_blocks, g).to(cuda)
+        shape_k, shape_v, kw = (n_blocks, G, bs, r_k), (n_blocks, G, bs, r_v), {"page_table": pt}
+    else:
+        shape_k, shape_v, kw = (B, G, S, r_k), (B, G, S, r_v), {}
+    k0 = torch.randn(*shape_k, generator=g).to(cuda, torch.bfloat16)
+    v0 = torch.randn(*shape_v, generator=g).to(cuda, torch.bfloat16)
+    kf, vf, kt, vt = k0.clone(), v0.clone(), k0.clone(), v0.clone()
+    q = fused.rope_q_append(qkv, cos, sin, pos, kf, vf, nh, **kw)
+    # the same step in tensor ops
+    t = qkv[:, :nh * 128].float().view(B, nh, 128)
+    p = pos.clamp(0, S - 1).long()
+    c, s = cos[p].unsqueeze(-2), sin[p].unsqueeze(-2)
+    tr = torch.stack([-t[..., 1::2], t[..., 0::2]], dim=-1).flatten(-2)
+    want_q = (t * c + tr * s).to(torch.bfloat16)
+    nq, nk = nh * 128, G * r_k
+    fused.append_latents(qkv[:, nq:nq + nk].reshape(B, G, r_k).to(torch.bfloat16),
+                         qkv[:, nq + nk:].reshape(B, G, r_v).to(torch.bfloat16), pos, kt, vt, **kw)
+    torch.cuda.synchronize()
+    assert torch.equal(q, want_q)
+    assert torch.equal(kf, kt) and torch.equal(vf, vt)
+    assert not torch.equal(kf, k0)  # something was appended

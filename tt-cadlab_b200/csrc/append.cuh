@@ -79,3 +79,74 @@ __global__ void palu_pack_cs_kernel(const void* cs_tab, long ld, int in_f32, uin
 }
 
 }  // namespace palu
+
+namespace palu {
+
+// One decode step's q rotation and latent append in one pass over the step's fused projection output
+// (the reference's nlp_create_qkv_heads_decode split, rotary_embedding_llama on q and the two
+// paged_update_cache calls, attention.py:601-625).
+struct RopeAppendParams {
+  const void* qkv;        // [B][ld] bf16 or f32: n_q * 128 q values (Meta pair order), then n_groups * r_k
+                          // K latents, then n_groups * r_v V latents
+  long ld;
+  const float* cos;       // [>= max_seq][128] fp32: cos of frequency j at columns 2j and 2j + 1
+  const float* sin;       // the same layout
+  const int32_t* cur_pos; // [B]
+  __nv_bfloat16* q_out;   // [B][n_q][128]
+  __nv_bfloat16* k_cache; // as AppendParams (contiguous or paged)
+  __nv_bfloat16* v_cache;
+  int batch, n_q, n_groups, r_k, r_v, max_seq;
+  const int32_t* page_table;
+  int table_ld, blk_shift, n_blocks;
+};
+
+template <typename T>
+PALU_DEVINL float load_f32(const T* p, long i);
+template <>
+PALU_DEVINL float load_f32<float>(const float* p, long i) { return p[i]; }
+template <>
+PALU_DEVINL float load_f32<__nv_bfloat16>(const __nv_bfloat16* p, long i) { return __bfloat162float(p[i]); }
+
+// Items per batch row: n_q * 64 q pairs, then n_groups * (r_k + r_v) latent elements. The q rotation is
+// out(2j) = x(2j) cos(2j) + (-x(2j+1)) sin(2j), out(2j+1) = x(2j+1) cos(2j+1) + x(2j) sin(2j+1) with each
+// product and the sum rounded separately (no fused multiply-add), at cur_pos clamped to [0, max_seq), the
+// decode op's clamp. Latents are appended at cur_pos; rows outside [0, max_seq) append nothing.
+template <typename T>
+__global__ void palu_rope_q_append_kernel(const RopeAppendParams p) {
+  const T* qkv = static_cast<const T*>(p.qkv);
+  const int qp = p.n_q * 64, nk = p.n_groups * p.r_k, per = qp + nk + p.n_groups * p.r_v;
+  const long total = (long)p.batch * per;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int b = (int)(i / per), e = (int)(i - (long)b * per);
+    const long row = (long)b * p.ld;
+    const int pos = p.cur_pos[b];
+    if (e < qp) {
+      const int h = e >> 6, j = e & 63, d = h * 128 + 2 * j;
+      const int pr = pos < 0 ? 0 : (pos >= p.max_seq ? p.max_seq - 1 : pos);
+      const float x0 = load_f32(qkv, row + d), x1 = load_f32(qkv, row + d + 1);
+      const float* c = p.cos + (long)pr * 128 + 2 * j;
+      const float* s = p.sin + (long)pr * 128 + 2 * j;
+      const float o0 = __fadd_rn(__fmul_rn(x0, c[0]), __fmul_rn(-x1, s[0]));
+      const float o1 = __fadd_rn(__fmul_rn(x1, c[1]), __fmul_rn(x0, s[1]));
+      __nv_bfloat162 o;
+      o.x = __float2bfloat16_rn(o0);
+      o.y = __float2bfloat16_rn(o1);
+      *reinterpret_cast<__nv_bfloat162*>(p.q_out + ((long)b * p.n_q + h) * 128 + 2 * j) = o;
+      continue;
+    }
+    if (pos < 0 || pos >= p.max_seq) continue;
+    const int el = e - qp;
+    const bool is_k = el < nk;
+    const int r = is_k ? p.r_k : p.r_v, x = is_k ? el : el - nk, g = x / r, c = x - g * r;
+    long crow = ((long)b * p.n_groups + g) * p.max_seq + pos;
+    if (p.page_table) {
+      const int blk = p.page_table[(long)b * p.table_ld + (pos >> p.blk_shift)];
+      if ((unsigned)blk >= (unsigned)p.n_blocks) continue;  // an entry outside the caches drops the write
+      crow = (((long)blk * p.n_groups + g) << p.blk_shift) + (pos & ((1 << p.blk_shift) - 1));
+    }
+    const __nv_bfloat16 v = __float2bfloat16_rn(load_f32(qkv, row + p.n_q * 128 + el));
+    (is_k ? p.k_cache : p.v_cache)[crow * r + c] = v;
+  }
+}
+
+}  // namespace palu

@@ -581,6 +581,49 @@ int palu_append_latents_paged(const void* new_k, const void* new_v, const int32_
   return append(new_k, new_v, cur_pos, k_cache, v_cache, d, pages, stream);
 }
 
+int palu_rope_q_append(const void* qkv, int64_t ld, int32_t qkv_dtype, const float* cos, const float* sin,
+                       const int32_t* cur_pos, void* q_out, void* k_cache, void* v_cache, const palu_page_table* pages,
+                       const palu_decode_dims* d, palu_stream_t stream) {
+  g_err.clear();
+  if (!d) return fail(PALU_ERR_INVALID, "dims is NULL");
+  if (!qkv || !cos || !sin || !cur_pos || !q_out || !k_cache || !v_cache)
+    return fail(PALU_ERR_INVALID, "rope_q_append: every pointer must be set");
+  if (d->batch <= 0 || d->n_q_heads <= 0 || d->n_groups <= 0 || d->max_seq <= 0 || d->r_k <= 0 || d->r_v <= 0)
+    return fail(PALU_ERR_INVALID, "rope_q_append: batch, n_q_heads, n_groups, r_k, r_v and max_seq must be positive");
+  if (d->head_dim != 128) return fail(PALU_ERR_INVALID, "head_dim must be 128, got %d", d->head_dim);
+  if (qkv_dtype != PALU_BF16 && qkv_dtype != PALU_F32) return fail(PALU_ERR_INVALID, "qkv dtype must be bf16 or f32");
+  const long long width = (long long)d->n_q_heads * 128 + (long long)d->n_groups * (d->r_k + d->r_v);
+  if (ld < width)
+    return fail(PALU_ERR_INVALID, "qkv rows of %lld elements cannot hold the %lld q and latent values", (long long)ld,
+                width);
+  if (reinterpret_cast<uintptr_t>(q_out) % 4 != 0) return fail(PALU_ERR_INVALID, "q_out must be 4-byte aligned");
+  if (pages)
+    if (int st = validate_pages(pages, d)) return st;
+  palu::RopeAppendParams p;
+  p.qkv = qkv;
+  p.ld = (long)ld;
+  p.cos = cos;
+  p.sin = sin;
+  p.cur_pos = cur_pos;
+  p.q_out = static_cast<__nv_bfloat16*>(q_out);
+  p.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  p.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  p.batch = d->batch;
+  p.n_q = d->n_q_heads;
+  p.n_groups = d->n_groups;
+  p.r_k = d->r_k;
+  p.r_v = d->r_v;
+  p.max_seq = d->max_seq;
+  set_pages(p, pages);
+  const long total = (long)d->batch * (d->n_q_heads * 64 + d->n_groups * (d->r_k + d->r_v));
+  const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  if (qkv_dtype == PALU_F32)
+    palu::palu_rope_q_append_kernel<float><<<blocks, 256, 0, stream>>>(p);
+  else
+    palu::palu_rope_q_append_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(p);
+  return cuda_check("rope_q_append kernel launch");
+}
+
 int palu_pack_cs_table(const void* cs_tab, int64_t ld, int32_t in_dtype, void* cs_pairs, int32_t rows,
                        palu_stream_t stream) {
   g_err.clear();

@@ -156,6 +156,13 @@ class PaluAttention:
             y = layer_output_partial(attn, self.wo)
         return all_reduce_layer_output(y) if self.shard.world > 1 else y
 
+    def _fused_prep(self, qkv: torch.Tensor) -> bool:
+        """Whether the step's q rotation and latent append run as the library's one fused kernel: on CUDA,
+        with bf16 caches and the library's append (tests that substitute CPU models of the device ops take
+        the tensor-op path, which computes the same values)."""
+        return (qkv.is_cuda and self.append_op is fused.append_latents and self.k_cache.dtype == torch.bfloat16
+                and qkv.dtype in (torch.bfloat16, torch.float32))
+
     def _check_pages(self, page_table: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
         if (page_table is None) != (self.paged is None):
             raise RuntimeError("page_table is required with paged caches and refused without them")
@@ -178,22 +185,25 @@ class PaluAttention:
             raise RuntimeError(f"batch {B} exceeds the cache's {self.max_batch} rows")
         pos = current_pos.to(self.device, torch.int32).reshape(B)
         qkv = xb.to(self.proj_dtype) @ self.w_qkv.T
-        nq, nk = self.nh * self.head_dim, self.ng * self.r_k
-        q = qkv[:, :nq].float().view(B, self.nh, self.head_dim)
-        q = self._rotate(q, pos.clamp(min=0).long()).to(torch.bfloat16)
-        k_new = qkv[:, nq:nq + nk].reshape(B, self.ng, self.r_k).to(self.k_cache.dtype)
-        v_new = qkv[:, nq + nk:].reshape(B, self.ng, self.r_v).to(self.v_cache.dtype)
         pt = self._check_pages(page_table)
         if pt is None:
-            kc, vc = self.k_cache[:B], self.v_cache[:B]
-            self.append_op(k_new, v_new, pos, kc, vc)
-            attn = self.attend_op(q[None], kc, self.w_rot, self.cs_tab, vc, self.head_dim_v, pos, u_v=self.u_v,
-                                  scale=self.scale, out_dtype=torch.float32)[0]
+            kc, vc, paged = self.k_cache[:B], self.v_cache[:B], {}
         else:
             pt = pt[:B, :(self.max_seq + self.paged.block_size - 1) // self.paged.block_size]
-            self.append_op(k_new, v_new, pos, self.k_cache, self.v_cache, page_table=pt)
-            attn = self.attend_op(q[None], self.k_cache, self.w_rot, self.cs_tab, self.v_cache, self.head_dim_v, pos,
-                                  u_v=self.u_v, scale=self.scale, out_dtype=torch.float32, page_table_tensor=pt)[0]
+            kc, vc, paged = self.k_cache, self.v_cache, {"page_table": pt}
+        if self._fused_prep(qkv):
+            # q rotation + latent append in one kernel (attention.py:601-625), bit-identical to the path below
+            q = fused.rope_q_append(qkv, self.cos, self.sin, pos, kc, vc, self.nh, **paged)
+        else:
+            nq, nk = self.nh * self.head_dim, self.ng * self.r_k
+            q = qkv[:, :nq].float().view(B, self.nh, self.head_dim)
+            q = self._rotate(q, pos.clamp(min=0).long()).to(torch.bfloat16)
+            k_new = qkv[:, nq:nq + nk].reshape(B, self.ng, self.r_k).to(self.k_cache.dtype)
+            v_new = qkv[:, nq + nk:].reshape(B, self.ng, self.r_v).to(self.v_cache.dtype)
+            self.append_op(k_new, v_new, pos, kc, vc, **paged)
+        attn = self.attend_op(q[None], kc, self.w_rot, self.cs_tab, vc, self.head_dim_v, pos, u_v=self.u_v,
+                              scale=self.scale, out_dtype=torch.float32,
+                              **({"page_table_tensor": pt} if pt is not None else {}))[0]
         y = self._out(attn)
         return y.view(1, 1, B, self.dim) if shape4 else y
 

@@ -365,3 +365,35 @@ def _append_paged(new_k, new_v, cur_pos, k_cache, v_cache, page_table) -> None:
                                                      cur_pos.to(torch.int32).contiguous().data_ptr(), ctypes.byref(pg),
                                                      k_cache.data_ptr(), v_cache.data_ptr(), ctypes.byref(d),
                                                      _lib.stream_handle(k_cache.device)))
+
+
+def rope_q_append(qkv, cos, sin, cur_pos, k_cache, v_cache, n_q, page_table=None) -> torch.Tensor:
+    """One decode step's q rotation and latent append in one kernel (palu_rope_q_append; the reference's
+    nlp_create_qkv_heads_decode split, rotary_embedding_llama on q and paged_update_cache x2,
+    attention.py:601-625). qkv [B, n_q * 128 + n_groups * (r_k + r_v)] bf16 or fp32 (the fused
+    projection, rows contiguous); cos / sin [>= S, 128] fp32; cur_pos [B] int32; caches contiguous
+    [B, n_groups, S, r] or, with ``page_table``, paged [n_blocks, n_groups, block_size, r]. Returns the
+    rotated q [B, n_q, 128] bf16, bit-identical to rotating in fp32 torch ops and rounding to bf16."""
+    _lib.require_cuda(qkv, cos, sin, cur_pos, k_cache, v_cache, page_table)
+    if qkv.dtype not in (torch.bfloat16, torch.float32) or qkv.dim() != 2 or qkv.stride(1) != 1:
+        raise RuntimeError(f"qkv must be a row-major bf16 or fp32 [B, width] tensor, got {qkv.dtype} {tuple(qkv.shape)}")
+    if cos.dtype != torch.float32 or sin.dtype != torch.float32 or not cos.is_contiguous() or not sin.is_contiguous():
+        raise RuntimeError("cos / sin must be contiguous fp32 [S, 128] tables")
+    B = qkv.shape[0]
+    G, r_k, r_v = k_cache.shape[1], k_cache.shape[3], v_cache.shape[3]
+    if page_table is None:
+        S = k_cache.shape[2]
+        pg = None
+    else:
+        page_table = page_table.to(torch.int32).contiguous()
+        S = page_table.shape[1] * k_cache.shape[2]
+        pg = ctypes.byref(_lib.pages(page_table, k_cache.shape[2], k_cache.shape[0]))
+    if cos.shape[0] < S or sin.shape[0] < S:
+        raise RuntimeError(f"cos / sin tables of {cos.shape[0]} rows are shorter than the {S} cache positions")
+    q = torch.empty(B, n_q, HEAD_DIM, dtype=torch.bfloat16, device=qkv.device)
+    d = _lib.dims(B, n_q, G, G, r_k, r_v, S)
+    _lib.check(_lib.load().palu_rope_q_append(
+        qkv.data_ptr(), qkv.stride(0), _lib.PALU_F32 if qkv.dtype == torch.float32 else _lib.PALU_BF16,
+        cos.data_ptr(), sin.data_ptr(), cur_pos.to(torch.int32).contiguous().data_ptr(), q.data_ptr(),
+        k_cache.data_ptr(), v_cache.data_ptr(), pg, ctypes.byref(d), _lib.stream_handle(qkv.device)))
+    return q
