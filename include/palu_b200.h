@@ -23,6 +23,8 @@
  *   palu_pack_cs_table     <- the cs_tab upload of palu_tt/attention.py:70-72 (fused.py:62-73 layout)
  *   palu_rope_q_append     <- nlp_create_qkv_heads_decode's split + rotary_embedding_llama on q + the two
  *                             paged_update_cache calls, palu_tt/attention.py:601-625, in one kernel
+ *   palu_add_rms_norm, palu_swiglu
+ *                          <- the decoder's stock RMSNorm and SwiGLU (palu_tt/model.py:52-95, tt_transformers)
  *   palu_decode_attn_paged / palu_append_latents_paged
  *                          <- the paged variant of palu_sdpa_decode and paged_update_cache with a page
  *                             table, which the reference plans but has not built (HANDOFF.md:54-55,
@@ -172,6 +174,18 @@ int palu_append_latents_paged(const void* new_k, const void* new_v, const int32_
 int palu_rope_q_append(const void* qkv, int64_t ld, int32_t qkv_dtype, const float* cos, const float* sin,
                        const int32_t* cur_pos, void* q_out, void* k_cache, void* v_cache, const palu_page_table* pages,
                        const palu_decode_dims* dims, palu_stream_t stream);
+
+/*
+ * Decoder steps around the attention layer (the stock RMSNorm and SwiGLU MLP of the decoder the reference
+ * assembles, palu_tt/model.py:52-95), fused to cut a decode step's kernel count.
+ * palu_add_rms_norm: h [rows][dim] f32 in place += delta (f32, or NULL), then out [rows][dim] bf16 =
+ *   h * rsqrt(mean(h^2) + eps) * w (w [dim] f32). dim a multiple of 4; pointers 16-byte aligned.
+ * palu_swiglu: gu [rows][ld] bf16 = gate (columns 0..f-1) then up (f..2f-1); out [rows][f] bf16 =
+ *   bf16(bf16(silu(gate)) * up).
+ */
+int palu_add_rms_norm(float* h, const float* delta, const float* w, void* out, int32_t rows, int32_t dim, float eps,
+                      palu_stream_t stream);
+int palu_swiglu(const void* gu, int64_t ld, int32_t f, void* out, int32_t rows, palu_stream_t stream);
 
 /* Device bytes palu_decode_attn / palu_plain_gqa_decode need for their partial results (enough for either
  * kernel family, so palu_set_kernel may change between calls). */

@@ -172,3 +172,47 @@ def test_two_rank_tensor_parallel_decoder_equals_one_rank():
     for got, want in ((pre2, pre1), (dec2, dec1)):
         mx, mn = rel_errors(got, want)
         assert mx < 1e-4 and mn < 1e-4, (mx, mn)
+
+
+@pytest.mark.gpu
+def test_fused_norm_and_swiglu_kernels_match_tensor_ops(cuda):
+    """palu_add_rms_norm and palu_swiglu against the tensor ops they replace: the residual sum bit for bit,
+    the bf16 outputs within one bf16 rounding step (the fused kernels sum the squares in another order)."""
+    from palu_b200 import fused
+    g = torch.Generator().manual_seed(3)
+    N, D, f = 64, 4096, 1792
+    h = torch.randn(N, D, generator=g).to(cuda)
+    delta = torch.randn(N, D, generator=g).to(cuda)
+    w = (1 + 0.1 * torch.randn(D, generator=g)).to(cuda)
+    want_h = h + delta
+    want = torch.nn.functional.rms_norm(want_h, (D,), w, 1e-5).to(torch.bfloat16)
+    got = fused.add_rms_norm(h, delta, w, 1e-5)
+    assert torch.equal(h, want_h)
+    rel = ((got.float() - want.float()).abs() / want.float().abs().clamp_min(1e-3)).max().item()
+    assert rel <= 2 ** -7, rel
+    gu = torch.randn(N, 2 * f, generator=g).to(cuda, torch.bfloat16)
+    want = torch.nn.functional.silu(gu[:, :f]) * gu[:, f:]
+    got = fused.swiglu(gu, f)
+    rel = ((got.float() - want.float()).abs() / want.float().abs().clamp_min(1e-3)).max().item()
+    assert rel <= 2 ** -7, rel
+
+
+@pytest.mark.gpu
+def test_bf16_decoder_fused_elementwise_matches_tensor_ops(cuda):
+    """A bf16 decoder step through the fused norm / SwiGLU kernels against the same step in tensor ops:
+    logits within the layer bar (the two paths round the normalized activations separately)."""
+    cfg = DecoderConfig_small()
+    from palu_b200.model import PaluDecoder
+    m = PaluDecoder(cfg, [(32, 64), (48, 32)], max_batch=B, max_seq=40, seed=5, device="cuda")
+    tokens = torch.randint(0, cfg.vocab, (B, P), generator=torch.Generator().manual_seed(9))
+    nxt = m.prefill_logits(tokens).argmax(-1)
+    pos = torch.full((B,), P, dtype=torch.int32, device=cuda)
+    fast = m.decode_logits(nxt, pos)
+    m._fused_elementwise = lambda: False
+    slow = m.decode_logits(nxt, pos)
+    _check(fast, slow.cpu(), "fused vs tensor-op decoder step")
+
+
+def DecoderConfig_small():
+    from palu_b200.model import DecoderConfig
+    return DecoderConfig(dim=512, n_layers=2, n_heads=4, n_kv_heads=2, ffn_dim=768, vocab=300)

@@ -150,3 +150,67 @@ __global__ void palu_rope_q_append_kernel(const RopeAppendParams p) {
 }
 
 }  // namespace palu
+
+namespace palu {
+
+// Decoder elementwise steps around the attention layer (the stock RMSNorm and SwiGLU MLP that the
+// reference's model assembles, palu_tt/model.py:52-95), fused so that one decode step launches fewer kernels.
+
+// Residual add + RMSNorm, one CTA per row: h += delta (fp32, in place; delta may be null), then
+// out = bf16(h * rsqrt(mean(h^2) + eps) * w). dim is a multiple of 4.
+constexpr int kNormThreads = 512;
+__global__ void __launch_bounds__(kNormThreads) palu_add_rms_norm_kernel(float* h, const float* delta, const float* w,
+                                                                          __nv_bfloat16* out, int dim, float eps) {
+  __shared__ float s_part[kNormThreads / 32];
+  const long row = blockIdx.x;
+  float4* hr = reinterpret_cast<float4*>(h + row * dim);
+  const float4* dr = delta ? reinterpret_cast<const float4*>(delta + row * dim) : nullptr;
+  const int n4 = dim / 4;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < n4; i += kNormThreads) {
+    float4 x = hr[i];
+    if (dr) {
+      const float4 d = dr[i];
+      x.x += d.x;
+      x.y += d.y;
+      x.z += d.z;
+      x.w += d.w;
+      hr[i] = x;
+    }
+    ss += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < kNormThreads / 32 ? s_part[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (threadIdx.x == 0) s_part[0] = rsqrtf(v / dim + eps);
+  }
+  __syncthreads();
+  const float inv = s_part[0];
+  const float4* wr = reinterpret_cast<const float4*>(w);
+  __nv_bfloat162* orow = reinterpret_cast<__nv_bfloat162*>(out + row * dim);
+  for (int i = threadIdx.x; i < n4; i += kNormThreads) {
+    const float4 x = hr[i], g = wr[i];
+    orow[2 * i] = __floats2bfloat162_rn(x.x * inv * g.x, x.y * inv * g.y);
+    orow[2 * i + 1] = __floats2bfloat162_rn(x.z * inv * g.z, x.w * inv * g.w);
+  }
+}
+
+// SwiGLU on the gate/up GEMM output: gu [rows][ld] bf16 holds gate (columns 0..f-1) then up (f..2f-1);
+// out[r][i] = bf16(bf16(silu(gate)) * up), the rounding of a silu kernel followed by a multiply kernel.
+__global__ void palu_swiglu_kernel(const __nv_bfloat16* gu, long ld, int f, __nv_bfloat16* out, int rows) {
+  const long total = (long)rows * f;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / f;
+    const int c = (int)(i - r * f);
+    const float g = __bfloat162float(gu[r * ld + c]);
+    const float a = __bfloat162float(__float2bfloat16_rn(g / (1.0f + expf(-g))));
+    out[i] = __float2bfloat16_rn(a * __bfloat162float(gu[r * ld + f + c]));
+  }
+}
+
+}  // namespace palu

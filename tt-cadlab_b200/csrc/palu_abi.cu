@@ -624,6 +624,34 @@ int palu_rope_q_append(const void* qkv, int64_t ld, int32_t qkv_dtype, const flo
   return cuda_check("rope_q_append kernel launch");
 }
 
+int palu_add_rms_norm(float* h, const float* delta, const float* w, void* out, int32_t rows, int32_t dim, float eps,
+                      palu_stream_t stream) {
+  g_err.clear();
+  if (!h || !w || !out) return fail(PALU_ERR_INVALID, "add_rms_norm: h, w and out must be set");
+  if (rows <= 0 || dim <= 0 || dim % 4 != 0)
+    return fail(PALU_ERR_INVALID, "add_rms_norm: rows must be positive and dim a positive multiple of 4 (got %d, %d)",
+                rows, dim);
+  if ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(delta) | reinterpret_cast<uintptr_t>(w) |
+       reinterpret_cast<uintptr_t>(out)) % 16 != 0)
+    return fail(PALU_ERR_INVALID, "add_rms_norm: h, delta, w and out must be 16-byte aligned");
+  palu::palu_add_rms_norm_kernel<<<rows, palu::kNormThreads, 0, stream>>>(h, delta, w,
+                                                                          static_cast<__nv_bfloat16*>(out), dim, eps);
+  return cuda_check("add_rms_norm kernel launch");
+}
+
+int palu_swiglu(const void* gu, int64_t ld, int32_t f, void* out, int32_t rows, palu_stream_t stream) {
+  g_err.clear();
+  if (!gu || !out) return fail(PALU_ERR_INVALID, "swiglu: gu and out must be set");
+  if (rows <= 0 || f <= 0 || ld < 2LL * f)
+    return fail(PALU_ERR_INVALID, "swiglu: rows and f must be positive and rows of gu hold 2 f values (got %d, %d, %lld)",
+                rows, f, (long long)ld);
+  const long total = (long)rows * f;
+  const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  palu::palu_swiglu_kernel<<<blocks, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(gu), (long)ld, f,
+                                                       static_cast<__nv_bfloat16*>(out), rows);
+  return cuda_check("swiglu kernel launch");
+}
+
 int palu_pack_cs_table(const void* cs_tab, int64_t ld, int32_t in_dtype, void* cs_pairs, int32_t rows,
                        palu_stream_t stream) {
   g_err.clear();

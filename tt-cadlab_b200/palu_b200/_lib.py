@@ -19,7 +19,7 @@ PALU_BF16, PALU_F32 = 0, 1
 
 # Every symbol include/palu_b200.h declares (checked by the CPU test suite).
 EXPORTED = ("palu_decode_attn", "palu_decode_attn_static", "palu_decode_attn_paged", "palu_append_latents_paged",
-            "palu_rope_q_append",
+            "palu_rope_q_append", "palu_add_rms_norm", "palu_swiglu",
             "palu_workspace_bytes", "palu_choose_splits", "palu_append_latents",
             "palu_plain_gqa_decode", "palu_pack_cs_table", "palu_set_kernel", "palu_kernel_for", "palu_read_status",
             "palu_last_error", "palu_version")
@@ -61,6 +61,10 @@ def load() -> ctypes.CDLL:
     lib.palu_append_latents_paged.restype = ctypes.c_int
     lib.palu_rope_q_append.argtypes = [vp, i64, i32, vp, vp, vp, vp, vp, vp, pages_p, dims_p, vp]
     lib.palu_rope_q_append.restype = ctypes.c_int
+    lib.palu_add_rms_norm.argtypes = [vp, vp, vp, vp, i32, i32, f32, vp]
+    lib.palu_add_rms_norm.restype = ctypes.c_int
+    lib.palu_swiglu.argtypes = [vp, i64, i32, vp, i32, vp]
+    lib.palu_swiglu.restype = ctypes.c_int
     lib.palu_plain_gqa_decode.argtypes = [vp, vp, vp, vp, vp, i32, vp, sz, dims_p, f32, vp]
     lib.palu_plain_gqa_decode.restype = ctypes.c_int
     lib.palu_workspace_bytes.argtypes = [dims_p]

@@ -179,12 +179,14 @@ class PaluAttention:
         """x [B, dim] or [1, 1, B, dim]; current_pos [B] ints (each row's position; < 0 skips the row);
         page_table [B, blocks per row] with paged caches. Returns the layer output in x's layout, fp32."""
         shape4 = x.dim() == 4
-        xb = (x.reshape(-1, x.shape[-1]) if shape4 else x).to(self.device, torch.float32)
+        xb = (x.reshape(-1, x.shape[-1]) if shape4 else x).to(self.device)
         B = xb.shape[0]
         if B > self.max_batch:
             raise RuntimeError(f"batch {B} exceeds the cache's {self.max_batch} rows")
         pos = current_pos.to(self.device, torch.int32).reshape(B)
-        qkv = xb.to(self.proj_dtype) @ self.w_qkv.T
+        # x arrives in fp32, or already in the projection dtype (the decoder's fused norm writes bf16)
+        xp = xb if xb.dtype == self.proj_dtype else xb.float().to(self.proj_dtype)
+        qkv = xp @ self.w_qkv.T
         pt = self._check_pages(page_table)
         if pt is None:
             kc, vc, paged = self.k_cache[:B], self.v_cache[:B], {}
@@ -201,8 +203,10 @@ class PaluAttention:
             k_new = qkv[:, nq:nq + nk].reshape(B, self.ng, self.r_k).to(self.k_cache.dtype)
             v_new = qkv[:, nq + nk:].reshape(B, self.ng, self.r_v).to(self.v_cache.dtype)
             self.append_op(k_new, v_new, pos, kc, vc, **paged)
+        # bf16 projections take the op's output in bf16: the rounding _out's input cast would apply anyway
+        odt = torch.bfloat16 if self.proj_dtype == torch.bfloat16 else torch.float32
         attn = self.attend_op(q[None], kc, self.w_rot, self.cs_tab, vc, self.head_dim_v, pos, u_v=self.u_v,
-                              scale=self.scale, out_dtype=torch.float32,
+                              scale=self.scale, out_dtype=odt,
                               **({"page_table_tensor": pt} if pt is not None else {}))[0]
         y = self._out(attn)
         return y.view(1, 1, B, self.dim) if shape4 else y

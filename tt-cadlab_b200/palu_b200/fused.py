@@ -397,3 +397,30 @@ def rope_q_append(qkv, cos, sin, cur_pos, k_cache, v_cache, n_q, page_table=None
         cos.data_ptr(), sin.data_ptr(), cur_pos.to(torch.int32).contiguous().data_ptr(), q.data_ptr(),
         k_cache.data_ptr(), v_cache.data_ptr(), pg, ctypes.byref(d), _lib.stream_handle(qkv.device)))
     return q
+
+
+def add_rms_norm(h, delta, w, eps) -> torch.Tensor:
+    """Residual add + RMSNorm of the decoder (palu_add_rms_norm): h [N, D] fp32 (contiguous) += delta
+    (fp32 [N, D] or None) in place, then returns bf16(h * rsqrt(mean(h^2) + eps) * w), w [D] fp32."""
+    _lib.require_cuda(h, delta, w)
+    if h.dtype != torch.float32 or not h.is_contiguous() or h.dim() != 2:
+        raise RuntimeError("h must be a contiguous fp32 [N, D] tensor")
+    if delta is not None and (delta.dtype != torch.float32 or not delta.is_contiguous() or delta.shape != h.shape):
+        raise RuntimeError("delta must be a contiguous fp32 tensor shaped like h")
+    w = w.float().contiguous()
+    out = torch.empty(h.shape, dtype=torch.bfloat16, device=h.device)
+    _lib.check(_lib.load().palu_add_rms_norm(h.data_ptr(), _lib.ptr(delta), w.data_ptr(), out.data_ptr(), h.shape[0],
+                                             h.shape[1], float(eps), _lib.stream_handle(h.device)))
+    return out
+
+
+def swiglu(gu, f) -> torch.Tensor:
+    """SwiGLU on the fused gate/up GEMM output (palu_swiglu): gu [N, >= 2f] bf16, gate in columns 0..f-1 and
+    up in f..2f-1 -> bf16(bf16(silu(gate)) * up) [N, f]."""
+    _lib.require_cuda(gu)
+    if gu.dtype != torch.bfloat16 or gu.dim() != 2 or gu.stride(1) != 1:
+        raise RuntimeError("gu must be a row-major bf16 [N, 2f] tensor")
+    out = torch.empty(gu.shape[0], f, dtype=torch.bfloat16, device=gu.device)
+    _lib.check(_lib.load().palu_swiglu(gu.data_ptr(), gu.stride(0), int(f), out.data_ptr(), gu.shape[0],
+                                       _lib.stream_handle(gu.device)))
+    return out

@@ -21,6 +21,7 @@ from typing import List, Optional, Sequence, Tuple
 
 import torch
 
+from palu_b200 import fused
 from palu_b200.attention import LLAMA3_SCALING, PagedAttentionConfig, PaluAttention
 from palu_b200.convert import LowRank
 from palu_b200.shard import KVShard
@@ -103,9 +104,10 @@ class PaluDecoder:
             w1f = randn(cfg.ffn_dim, D, scale=D ** -0.5)
             w3f = randn(cfg.ffn_dim, D, scale=D ** -0.5)
             w2f = randn(D, cfg.ffn_dim, scale=cfg.ffn_dim ** -0.5)
+            # w1 and w3 rows of this rank as one matrix: the gate and up projections are one GEMM
+            w13 = torch.cat([w1f[f_lo:f_hi], w3f[f_lo:f_hi]])
             layer = dict(attn=attn, attn_norm=torch.ones(D, device=dev), ffn_norm=torch.ones(D, device=dev),
-                         w1=w1f[f_lo:f_hi].contiguous(), w3=w3f[f_lo:f_hi].contiguous(),
-                         w2=w2f[:, f_lo:f_hi].contiguous())
+                         w13=w13, w1=w13[:f_hi - f_lo], w3=w13[f_hi - f_lo:], w2=w2f[:, f_lo:f_hi].contiguous())
             if keep_source:
                 layer["src"] = dict(wq=wq, wo=wo, lowrank=lr, w1=w1f, w3=w3f, w2=w2f)
             self.layers.append(layer)
@@ -113,10 +115,20 @@ class PaluDecoder:
         self.lm_head = randn(cfg.vocab, D, scale=D ** -0.5)
 
     # ---- pieces -------------------------------------------------------------------------------------
+    def _fused_elementwise(self) -> bool:
+        """Decode steps on CUDA with bf16 weights run the residual adds, RMSNorms and SwiGLU as the library's
+        fused kernels (the tensor-op path below computes the same steps, for CPU runs and fp32 weights)."""
+        return self.device.type == "cuda" and self.dtype == torch.bfloat16
+
     def _mlp(self, L: dict, x: torch.Tensor) -> torch.Tensor:
         """SwiGLU on this rank's hidden slice, summed over ranks: x [N, dim] fp32 -> [N, dim] fp32."""
         h = x.to(self.dtype)
-        a = torch.nn.functional.silu(h @ L["w1"].t()) * (h @ L["w3"].t())
+        gu = h @ L["w13"].t()
+        f = L["w1"].shape[0]
+        if self._fused_elementwise():
+            a = fused.swiglu(gu, f)
+        else:
+            a = torch.nn.functional.silu(gu[:, :f]) * gu[:, f:]
         y = (a @ L["w2"].t()).float()
         if self.world > 1:
             torch.distributed.all_reduce(y)
@@ -133,6 +145,15 @@ class PaluDecoder:
         """One decode step for every batch row (generate.py:40-50): tokens [B] at positions pos [B] ->
         logits [B, vocab] fp32. Appends the step's latents to every layer's caches."""
         h = self.embed[tokens.to(self.device)].float()
+        if self._fused_elementwise():
+            # residual adds, RMSNorms and the bf16 casts as one library kernel each time (fp32 residual h)
+            eps = self.cfg.norm_eps
+            x = fused.add_rms_norm(h, None, self.layers[0]["attn_norm"], eps)
+            for i, L in enumerate(self.layers):
+                x = fused.add_rms_norm(h, L["attn"].forward_decode(x, pos, page_table), L["ffn_norm"], eps)
+                nxt = self.layers[i + 1]["attn_norm"] if i + 1 < len(self.layers) else self.norm
+                x = fused.add_rms_norm(h, self._mlp(L, x), nxt, eps)
+            return (x @ self.lm_head.t()).float()
         for L in self.layers:
             h = h + L["attn"].forward_decode(rms_norm(h, L["attn_norm"], self.cfg.norm_eps), pos, page_table)
             h = h + self._mlp(L, rms_norm(h, L["ffn_norm"], self.cfg.norm_eps))
