@@ -178,13 +178,14 @@ int palu_rope_q_append(const void* qkv, int64_t ld, int32_t qkv_dtype, const flo
 /*
  * Decoder steps around the attention layer (the stock RMSNorm and SwiGLU MLP of the decoder the reference
  * assembles, palu_tt/model.py:52-95), fused to cut a decode step's kernel count.
- * palu_add_rms_norm: h [rows][dim] f32 in place += delta (f32, or NULL), then out [rows][dim] bf16 =
- *   h * rsqrt(mean(h^2) + eps) * w (w [dim] f32). dim a multiple of 4; pointers 16-byte aligned.
+ * palu_add_rms_norm: h [rows][dim] f32 in place += delta ([rows][dim] of delta_dtype PALU_F32 or PALU_BF16,
+ *   or NULL), then out [rows][dim] bf16 = h * rsqrt(mean(h^2) + eps) * w (w [dim] f32). dim a multiple of 4;
+ *   pointers 16-byte aligned.
  * palu_swiglu: gu [rows][ld] bf16 = gate (columns 0..f-1) then up (f..2f-1); out [rows][f] bf16 =
  *   bf16(bf16(silu(gate)) * up).
  */
-int palu_add_rms_norm(float* h, const float* delta, const float* w, void* out, int32_t rows, int32_t dim, float eps,
-                      palu_stream_t stream);
+int palu_add_rms_norm(float* h, const void* delta, int32_t delta_dtype, const float* w, void* out, int32_t rows,
+                      int32_t dim, float eps, palu_stream_t stream);
 int palu_swiglu(const void* gu, int64_t ld, int32_t f, void* out, int32_t rows, palu_stream_t stream);
 
 /* Device bytes palu_decode_attn / palu_plain_gqa_decode need for their partial results (enough for either

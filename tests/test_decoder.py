@@ -190,6 +190,10 @@ def test_fused_norm_and_swiglu_kernels_match_tensor_ops(cuda):
     assert torch.equal(h, want_h)
     rel = ((got.float() - want.float()).abs() / want.float().abs().clamp_min(1e-3)).max().item()
     assert rel <= 2 ** -7, rel
+    d16 = delta.to(torch.bfloat16)  # a bf16 delta (a GEMM's output) is widened exactly while it is added
+    want_h = h + d16.float()
+    fused.add_rms_norm(h, d16, w, 1e-5)
+    assert torch.equal(h, want_h)
     gu = torch.randn(N, 2 * f, generator=g).to(cuda, torch.bfloat16)
     want = torch.nn.functional.silu(gu[:, :f]) * gu[:, f:]
     got = fused.swiglu(gu, f)

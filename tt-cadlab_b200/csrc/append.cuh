@@ -156,21 +156,29 @@ namespace palu {
 // Decoder elementwise steps around the attention layer (the stock RMSNorm and SwiGLU MLP that the
 // reference's model assembles, palu_tt/model.py:52-95), fused so that one decode step launches fewer kernels.
 
-// Residual add + RMSNorm, one CTA per row: h += delta (fp32, in place; delta may be null), then
+// Residual add + RMSNorm, one CTA per row: h += delta (fp32 or bf16, in place; delta may be null), then
 // out = bf16(h * rsqrt(mean(h^2) + eps) * w). dim is a multiple of 4.
 constexpr int kNormThreads = 512;
-__global__ void __launch_bounds__(kNormThreads) palu_add_rms_norm_kernel(float* h, const float* delta, const float* w,
+PALU_DEVINL float4 load4(const float* p, int i) { return reinterpret_cast<const float4*>(p)[i]; }
+PALU_DEVINL float4 load4(const __nv_bfloat16* p, int i) {
+  const uint2 u = reinterpret_cast<const uint2*>(p)[i];
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+template <typename TD>
+__global__ void __launch_bounds__(kNormThreads) palu_add_rms_norm_kernel(float* h, const TD* delta, const float* w,
                                                                           __nv_bfloat16* out, int dim, float eps) {
   __shared__ float s_part[kNormThreads / 32];
   const long row = blockIdx.x;
   float4* hr = reinterpret_cast<float4*>(h + row * dim);
-  const float4* dr = delta ? reinterpret_cast<const float4*>(delta + row * dim) : nullptr;
+  const TD* dr = delta ? delta + row * dim : nullptr;
   const int n4 = dim / 4;
   float ss = 0.f;
   for (int i = threadIdx.x; i < n4; i += kNormThreads) {
     float4 x = hr[i];
     if (dr) {
-      const float4 d = dr[i];
+      const float4 d = load4(dr, i);
       x.x += d.x;
       x.y += d.y;
       x.z += d.z;
@@ -202,15 +210,34 @@ __global__ void __launch_bounds__(kNormThreads) palu_add_rms_norm_kernel(float* 
 
 // SwiGLU on the gate/up GEMM output: gu [rows][ld] bf16 holds gate (columns 0..f-1) then up (f..2f-1);
 // out[r][i] = bf16(bf16(silu(gate)) * up), the rounding of a silu kernel followed by a multiply kernel.
+PALU_DEVINL __nv_bfloat16 swiglu1(__nv_bfloat16 gate, __nv_bfloat16 up) {
+  const float g = __bfloat162float(gate);
+  const float a = __bfloat162float(__float2bfloat16_rn(g / (1.0f + expf(-g))));
+  return __float2bfloat16_rn(a * __bfloat162float(up));
+}
 __global__ void palu_swiglu_kernel(const __nv_bfloat16* gu, long ld, int f, __nv_bfloat16* out, int rows) {
   const long total = (long)rows * f;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
     const long r = i / f;
     const int c = (int)(i - r * f);
-    const float g = __bfloat162float(gu[r * ld + c]);
-    const float a = __bfloat162float(__float2bfloat16_rn(g / (1.0f + expf(-g))));
-    out[i] = __float2bfloat16_rn(a * __bfloat162float(gu[r * ld + f + c]));
+    out[i] = swiglu1(gu[r * ld + c], gu[r * ld + f + c]);
   }
+}
+// The same with 8 columns per thread (16-byte loads and stores): row blockIdx.y, f and ld multiples of 8,
+// gu and out 16-byte aligned.
+__global__ void palu_swiglu8_kernel(const __nv_bfloat16* gu, long ld, int f, __nv_bfloat16* out) {
+  const int c8 = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c8 * 8 >= f) return;
+  const long r = blockIdx.y;
+  const uint4 gv = reinterpret_cast<const uint4*>(gu + r * ld)[c8];
+  const uint4 uv = reinterpret_cast<const uint4*>(gu + r * ld + f)[c8];
+  const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(&gv);
+  const __nv_bfloat16* u = reinterpret_cast<const __nv_bfloat16*>(&uv);
+  uint4 ov;
+  __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(&ov);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) o[k] = swiglu1(g[k], u[k]);
+  reinterpret_cast<uint4*>(out + r * f)[c8] = ov;
 }
 
 }  // namespace palu

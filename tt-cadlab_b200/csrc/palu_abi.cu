@@ -624,18 +624,24 @@ int palu_rope_q_append(const void* qkv, int64_t ld, int32_t qkv_dtype, const flo
   return cuda_check("rope_q_append kernel launch");
 }
 
-int palu_add_rms_norm(float* h, const float* delta, const float* w, void* out, int32_t rows, int32_t dim, float eps,
-                      palu_stream_t stream) {
+int palu_add_rms_norm(float* h, const void* delta, int32_t delta_dtype, const float* w, void* out, int32_t rows,
+                      int32_t dim, float eps, palu_stream_t stream) {
   g_err.clear();
   if (!h || !w || !out) return fail(PALU_ERR_INVALID, "add_rms_norm: h, w and out must be set");
+  if (delta_dtype != PALU_BF16 && delta_dtype != PALU_F32)
+    return fail(PALU_ERR_INVALID, "add_rms_norm: delta dtype must be bf16 or f32");
   if (rows <= 0 || dim <= 0 || dim % 4 != 0)
     return fail(PALU_ERR_INVALID, "add_rms_norm: rows must be positive and dim a positive multiple of 4 (got %d, %d)",
                 rows, dim);
   if ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(delta) | reinterpret_cast<uintptr_t>(w) |
        reinterpret_cast<uintptr_t>(out)) % 16 != 0)
     return fail(PALU_ERR_INVALID, "add_rms_norm: h, delta, w and out must be 16-byte aligned");
-  palu::palu_add_rms_norm_kernel<<<rows, palu::kNormThreads, 0, stream>>>(h, delta, w,
-                                                                          static_cast<__nv_bfloat16*>(out), dim, eps);
+  if (delta_dtype == PALU_BF16)
+    palu::palu_add_rms_norm_kernel<__nv_bfloat16><<<rows, palu::kNormThreads, 0, stream>>>(
+        h, static_cast<const __nv_bfloat16*>(delta), w, static_cast<__nv_bfloat16*>(out), dim, eps);
+  else
+    palu::palu_add_rms_norm_kernel<float><<<rows, palu::kNormThreads, 0, stream>>>(
+        h, static_cast<const float*>(delta), w, static_cast<__nv_bfloat16*>(out), dim, eps);
   return cuda_check("add_rms_norm kernel launch");
 }
 
@@ -645,6 +651,13 @@ int palu_swiglu(const void* gu, int64_t ld, int32_t f, void* out, int32_t rows, 
   if (rows <= 0 || f <= 0 || ld < 2LL * f)
     return fail(PALU_ERR_INVALID, "swiglu: rows and f must be positive and rows of gu hold 2 f values (got %d, %d, %lld)",
                 rows, f, (long long)ld);
+  if (f % 8 == 0 && ld % 8 == 0 && rows <= 65535 &&
+      (reinterpret_cast<uintptr_t>(gu) | reinterpret_cast<uintptr_t>(out)) % 16 == 0) {
+    const dim3 grid((f / 8 + 127) / 128, rows);
+    palu::palu_swiglu8_kernel<<<grid, 128, 0, stream>>>(static_cast<const __nv_bfloat16*>(gu), (long)ld, f,
+                                                        static_cast<__nv_bfloat16*>(out));
+    return cuda_check("swiglu kernel launch");
+  }
   const long total = (long)rows * f;
   const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
   palu::palu_swiglu_kernel<<<blocks, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(gu), (long)ld, f,

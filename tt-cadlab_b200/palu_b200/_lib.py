@@ -61,7 +61,7 @@ def load() -> ctypes.CDLL:
     lib.palu_append_latents_paged.restype = ctypes.c_int
     lib.palu_rope_q_append.argtypes = [vp, i64, i32, vp, vp, vp, vp, vp, vp, pages_p, dims_p, vp]
     lib.palu_rope_q_append.restype = ctypes.c_int
-    lib.palu_add_rms_norm.argtypes = [vp, vp, vp, vp, i32, i32, f32, vp]
+    lib.palu_add_rms_norm.argtypes = [vp, vp, i32, vp, vp, i32, i32, f32, vp]
     lib.palu_add_rms_norm.restype = ctypes.c_int
     lib.palu_swiglu.argtypes = [vp, i64, i32, vp, i32, vp]
     lib.palu_swiglu.restype = ctypes.c_int

@@ -148,10 +148,13 @@ class PaluAttention:
         tr = torch.stack([-t[..., 1::2], t[..., 0::2]], dim=-1).flatten(-2)  # (-x1, x0) per pair
         return t * c + tr * s
 
-    def _out(self, attn: torch.Tensor) -> torch.Tensor:
-        """[B, nh_local, w] attention output -> [B, dim] layer output (summed over ranks)."""
+    def _out(self, attn: torch.Tensor, fp32: bool = True) -> torch.Tensor:
+        """[B, nh_local, w] attention output -> [B, dim] layer output (summed over ranks), fp32, or in the
+        projection dtype when ``fp32`` is False on one rank."""
         if self.wo_compact is not None and attn.shape[-1] == self.r_v:
-            y = (attn.reshape(attn.shape[0], -1).to(self.wo_compact.dtype) @ self.wo_compact.t()).float()
+            y = attn.reshape(attn.shape[0], -1).to(self.wo_compact.dtype) @ self.wo_compact.t()
+            if fp32 or self.shard.world > 1:
+                y = y.float()
         else:
             y = layer_output_partial(attn, self.wo)
         return all_reduce_layer_output(y) if self.shard.world > 1 else y
@@ -175,9 +178,10 @@ class PaluAttention:
 
     @torch.no_grad()
     def forward_decode(self, x: torch.Tensor, current_pos: torch.Tensor,
-                       page_table: Optional[torch.Tensor] = None) -> torch.Tensor:
+                       page_table: Optional[torch.Tensor] = None, out_fp32: bool = True) -> torch.Tensor:
         """x [B, dim] or [1, 1, B, dim]; current_pos [B] ints (each row's position; < 0 skips the row);
-        page_table [B, blocks per row] with paged caches. Returns the layer output in x's layout, fp32."""
+        page_table [B, blocks per row] with paged caches. Returns the layer output in x's layout, fp32 (or,
+        with ``out_fp32`` False on one rank, the output GEMM's dtype, for a consumer that widens it itself)."""
         shape4 = x.dim() == 4
         xb = (x.reshape(-1, x.shape[-1]) if shape4 else x).to(self.device)
         B = xb.shape[0]
@@ -208,7 +212,7 @@ class PaluAttention:
         attn = self.attend_op(q[None], kc, self.w_rot, self.cs_tab, vc, self.head_dim_v, pos, u_v=self.u_v,
                               scale=self.scale, out_dtype=odt,
                               **({"page_table_tensor": pt} if pt is not None else {}))[0]
-        y = self._out(attn)
+        y = self._out(attn, out_fp32)
         return y.view(1, 1, B, self.dim) if shape4 else y
 
     @torch.no_grad()

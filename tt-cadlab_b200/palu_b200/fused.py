@@ -401,16 +401,18 @@ def rope_q_append(qkv, cos, sin, cur_pos, k_cache, v_cache, n_q, page_table=None
 
 def add_rms_norm(h, delta, w, eps) -> torch.Tensor:
     """Residual add + RMSNorm of the decoder (palu_add_rms_norm): h [N, D] fp32 (contiguous) += delta
-    (fp32 [N, D] or None) in place, then returns bf16(h * rsqrt(mean(h^2) + eps) * w), w [D] fp32."""
+    (fp32 or bf16 [N, D], or None) in place, then returns bf16(h * rsqrt(mean(h^2) + eps) * w), w [D] fp32."""
     _lib.require_cuda(h, delta, w)
     if h.dtype != torch.float32 or not h.is_contiguous() or h.dim() != 2:
         raise RuntimeError("h must be a contiguous fp32 [N, D] tensor")
-    if delta is not None and (delta.dtype != torch.float32 or not delta.is_contiguous() or delta.shape != h.shape):
-        raise RuntimeError("delta must be a contiguous fp32 tensor shaped like h")
+    if delta is not None and (delta.dtype not in (torch.float32, torch.bfloat16) or not delta.is_contiguous()
+                              or delta.shape != h.shape):
+        raise RuntimeError("delta must be a contiguous fp32 or bf16 tensor shaped like h")
+    ddt = _lib.PALU_BF16 if delta is not None and delta.dtype == torch.bfloat16 else _lib.PALU_F32
     w = w.float().contiguous()
     out = torch.empty(h.shape, dtype=torch.bfloat16, device=h.device)
-    _lib.check(_lib.load().palu_add_rms_norm(h.data_ptr(), _lib.ptr(delta), w.data_ptr(), out.data_ptr(), h.shape[0],
-                                             h.shape[1], float(eps), _lib.stream_handle(h.device)))
+    _lib.check(_lib.load().palu_add_rms_norm(h.data_ptr(), _lib.ptr(delta), ddt, w.data_ptr(), out.data_ptr(),
+                                             h.shape[0], h.shape[1], float(eps), _lib.stream_handle(h.device)))
     return out
 
 

@@ -120,8 +120,9 @@ class PaluDecoder:
         fused kernels (the tensor-op path below computes the same steps, for CPU runs and fp32 weights)."""
         return self.device.type == "cuda" and self.dtype == torch.bfloat16
 
-    def _mlp(self, L: dict, x: torch.Tensor) -> torch.Tensor:
-        """SwiGLU on this rank's hidden slice, summed over ranks: x [N, dim] fp32 -> [N, dim] fp32."""
+    def _mlp(self, L: dict, x: torch.Tensor, fp32: bool = True) -> torch.Tensor:
+        """SwiGLU on this rank's hidden slice, summed over ranks: x [N, dim] -> [N, dim] fp32 (in the weights'
+        dtype when ``fp32`` is False on one rank)."""
         h = x.to(self.dtype)
         gu = h @ L["w13"].t()
         f = L["w1"].shape[0]
@@ -129,7 +130,9 @@ class PaluDecoder:
             a = fused.swiglu(gu, f)
         else:
             a = torch.nn.functional.silu(gu[:, :f]) * gu[:, f:]
-        y = (a @ L["w2"].t()).float()
+        y = a @ L["w2"].t()
+        if fp32 or self.world > 1:
+            y = y.float()
         if self.world > 1:
             torch.distributed.all_reduce(y)
         return y
@@ -150,9 +153,11 @@ class PaluDecoder:
             eps = self.cfg.norm_eps
             x = fused.add_rms_norm(h, None, self.layers[0]["attn_norm"], eps)
             for i, L in enumerate(self.layers):
-                x = fused.add_rms_norm(h, L["attn"].forward_decode(x, pos, page_table), L["ffn_norm"], eps)
+                # on one rank the GEMM outputs stay bf16: the norm kernel widens them while adding
+                x = fused.add_rms_norm(h, L["attn"].forward_decode(x, pos, page_table, out_fp32=False),
+                                       L["ffn_norm"], eps)
                 nxt = self.layers[i + 1]["attn_norm"] if i + 1 < len(self.layers) else self.norm
-                x = fused.add_rms_norm(h, self._mlp(L, x), nxt, eps)
+                x = fused.add_rms_norm(h, self._mlp(L, x, fp32=False), nxt, eps)
             return (x @ self.lm_head.t()).float()
         for L in self.layers:
             h = h + L["attn"].forward_decode(rms_norm(h, L["attn_norm"], self.cfg.norm_eps), pos, page_table)
