@@ -141,3 +141,22 @@ def test_cpu_tensors_are_refused_loudly():
     q, k, w, cs, v, pos = _args()
     with pytest.raises(RuntimeError, match="CUDA tensors only"):
         fused.palu_sdpa_decode(q, k, w, cs, v, 64, pos)
+
+
+def test_decoder_step_entry_points_validate_before_any_cuda_call():
+    """palu_rope_q_append, palu_add_rms_norm and palu_swiglu reject bad shapes with PALU_ERR_INVALID and a
+    message naming the problem (the pointers are dummies: validation fails first)."""
+    lib = _lib.load()
+    z = ctypes.c_void_p(16)
+    d = _lib.dims(4, 32, 8, 8, 64, 64, 256)
+    width = 32 * 128 + 8 * (64 + 64)
+    st = lib.palu_rope_q_append(z, width - 1, _lib.PALU_BF16, z, z, z, z, z, z, None, ctypes.byref(d), None)
+    assert st == _lib.PALU_ERR_INVALID and "cannot hold" in lib.palu_last_error().decode()
+    st = lib.palu_rope_q_append(z, width, 7, z, z, z, z, z, z, None, ctypes.byref(d), None)
+    assert st == _lib.PALU_ERR_INVALID and "dtype" in lib.palu_last_error().decode()
+    st = lib.palu_add_rms_norm(z, None, _lib.PALU_F32, z, z, 4, 4098, 1e-5, None)
+    assert st == _lib.PALU_ERR_INVALID and "multiple of 4" in lib.palu_last_error().decode()
+    st = lib.palu_add_rms_norm(z, z, 9, z, z, 4, 4096, 1e-5, None)
+    assert st == _lib.PALU_ERR_INVALID and "dtype" in lib.palu_last_error().decode()
+    st = lib.palu_swiglu(z, 100, 64, z, 4, None)
+    assert st == _lib.PALU_ERR_INVALID and "2 f" in lib.palu_last_error().decode()
