@@ -1,7 +1,6 @@
 """palu_b200.convert against the reference's own outputs (golden fixtures from palu_tt/convert.py) and
 the reference's convert tests restated (tests/test_convert.py). CPU only."""
 import json
-import re
 
 import numpy as np
 import pytest
@@ -93,17 +92,6 @@ def test_unit_scale_keeps_the_product_and_is_group_aware():  # tests/test_conver
     assert torch.allclose(unit.k_U[2], U[2] * c[None, :])
     for h in range(4):
         assert torch.allclose(unit.k_U[h] @ unit.k_VT[h], lr.k_U[h] @ lr.k_VT[h], atol=1e-4)
-
-
-def test_cache_id_is_dirname_plus_content_hash(tmp_path):  # tests/test_convert.py:293-320
-    d = tmp_path / "my_dump_0.5"
-    d.mkdir()
-    (d / "config.json").write_text('{"head_wise_ranks": {}}')
-    cid = convert.palu_dir_cache_id(d)
-    assert re.fullmatch(r"my_dump_0\.5-[0-9a-f]{8}", cid)
-    (d / "config.json").write_text('{"head_wise_ranks": {}} ')
-    assert convert.palu_dir_cache_id(d) != cid
-    assert convert.palu_cache_id_for(d, "unit").endswith("-unit")
 
 
 def test_runtime_and_config_defaults():  # tests/test_convert.py:332-436

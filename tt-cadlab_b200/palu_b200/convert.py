@@ -15,10 +15,8 @@ to ``rank_multiple``, which changes nothing numerically.
 """
 from __future__ import annotations
 
-import hashlib
 import json
 import math
-import re
 from dataclasses import dataclass, field
 from pathlib import Path
 from typing import Dict, List, Optional
@@ -165,23 +163,6 @@ def load_palu_dir(palu_dir, n_layers: int, n_kv_heads: int, head_dim: int, rank_
     return out
 
 
-def palu_dir_cache_id(palu_dir) -> str:
-    """Directory name + 8 hex digits hashing config.json's bytes and each shard's name/size/mtime
-    (convert.py:202-216)."""
-    palu_dir = Path(palu_dir)
-    h = hashlib.sha256((palu_dir / "config.json").read_bytes())
-    for f in sorted(palu_dir.glob("*.safetensors")):
-        st = f.stat()
-        h.update(f"{f.name}:{st.st_size}:{st.st_mtime_ns}\n".encode())
-    name = re.sub(r"[^A-Za-z0-9._-]", "_", palu_dir.resolve().name)
-    return f"{name}-{h.hexdigest()[:8]}"
-
-
-def palu_cache_id_for(palu_dir, latent_scale: str) -> str:
-    base = palu_dir_cache_id(palu_dir)
-    return base if latent_scale == "balanced" else f"{base}-{latent_scale}"
-
-
 def palu_layer_tensors(hf_attn: Dict[str, torch.Tensor], lr: LowRank, n_heads: int, n_kv_heads: int,
                        head_dim: int) -> Dict[str, torch.Tensor]:
     """Per-layer tensors (convert.py:227-288):
@@ -227,48 +208,3 @@ def palu_layer_tensors(hf_attn: Dict[str, torch.Tensor], lr: LowRank, n_heads: i
             wo_fused[:, qh * head_dim:qh * head_dim + r_v] = wo[:, cols] @ u_v_eff[qh // rep]
     return {"wk_lat_pad": wk, "wv_lat_pad": wv, "u_k": u_k, "u_v": u_v, "wo_fused": wo_fused,
             "w_rot": w_rot_from_u_k(u_k)}
-
-
-def load_hf_tensors(hf_dir, predicate) -> Dict[str, torch.Tensor]:
-    """Load the tensors of an HF safetensors snapshot whose key satisfies ``predicate`` (fp32)."""
-    from safetensors import safe_open
-    hf_dir = Path(hf_dir)
-    index = hf_dir / "model.safetensors.index.json"
-    files = sorted(set(json.loads(index.read_text())["weight_map"].values())) if index.exists() else \
-        [p.name for p in sorted(hf_dir.glob("*.safetensors"))]
-    out = {}
-    for fn in files:
-        with safe_open(str(hf_dir / fn), framework="pt") as sf:
-            for k in sf.keys():
-                if predicate(k):
-                    out[k] = sf.get_tensor(k).float()
-    return out
-
-
-def hf_attn_weights(hf_dir, layer: int) -> Dict[str, torch.Tensor]:
-    p = f"model.layers.{layer}.self_attn."
-    t = load_hf_tensors(hf_dir, lambda k: k.startswith(p) and k.endswith("proj.weight"))
-    return {"q": t[p + "q_proj.weight"], "k": t[p + "k_proj.weight"], "v": t[p + "v_proj.weight"],
-            "o": t[p + "o_proj.weight"]}
-
-
-def add_palu_to_state_dict(state_dict: dict, hf_dir, palu_dir, n_layers: int, n_heads: int, n_kv_heads: int,
-                           head_dim: int, latent_scale: str = "balanced") -> PaluConfig:
-    """Add ``layers.{i}.attention.palu.*`` for every layer; ``palu_dir`` None = identity factorisation
-    (convert.py:297-312)."""
-    lrs = None if palu_dir is None else load_palu_dir(palu_dir, n_layers, n_kv_heads, head_dim,
-                                                      latent_scale=latent_scale)
-    rank_k, rank_v = [], []
-    for i in range(n_layers):
-        w = hf_attn_weights(hf_dir, i)
-        lr = identity_lowrank(w, n_kv_heads, head_dim) if lrs is None else lrs[i]
-        for name, t in palu_layer_tensors(w, lr, n_heads, n_kv_heads, head_dim).items():
-            state_dict[f"layers.{i}.attention.palu.{name}"] = t
-        rank_k.append(lr.r_k)
-        rank_v.append(lr.r_v)
-    cache_id = "identity" if palu_dir is None else palu_cache_id_for(palu_dir, latent_scale)
-    groups = {lr.group_size for lr in lrs.values()} if lrs else {1}
-    if len(groups) != 1:
-        raise ValueError(f"mixed group sizes across layers: {groups}")
-    return PaluConfig(rank_k=rank_k, rank_v=rank_v, cache_id=cache_id, group_size=groups.pop(),
-                      latent_scale=latent_scale)
