@@ -91,6 +91,27 @@ def test_layer_reference_shapes_and_cpu_refusal():
         fresh.forward_decode(d["x_d1"][:, 0], torch.full((2,), 0, dtype=torch.int32))
 
 
+def test_layer_reference_call_surface():
+    """The reference layer's call forms (attention.py:382, 585, 735-740): ``forward`` dispatches on
+    ``mode``, ``rot_mats`` is the third positional argument of both forward methods (accepted, unused),
+    ``page_table`` and ``kv_cache`` are keywords, and an external ``kv_cache`` is refused."""
+    from palu_b200.attention import Mode
+    a, d = _layer_from_golden("cpu")
+    b, _ = _layer_from_golden("cpu")
+    _cpu_ops(a)
+    _cpu_ops(b)
+    P, B = d["x_pre"].shape[1], d["x_pre"].shape[0]
+    assert torch.equal(a.forward(d["x_pre"], None, None, 0, Mode.PREFILL), b.forward_prefill(d["x_pre"], None))
+    pos = torch.full((B,), P, dtype=torch.int32)
+    x = d["x_d1"][:, 0]
+    want = b.forward_decode(x, pos, None, None, None)
+    assert torch.equal(a.forward(x, pos, "ignored rot_mats", mode="decode"), want)
+    with pytest.raises(RuntimeError, match="kv_cache"):
+        a.forward_decode(x, pos, kv_cache=[object()])
+    with pytest.raises(RuntimeError, match="chunked prefill"):
+        a.forward_prefill(d["x_pre"], None, 0, chunk_start_idx=32)
+
+
 @pytest.mark.gpu
 def test_layer_matches_reference_layer_on_gpu(cuda):
     layer, d = _layer_from_golden("cuda")

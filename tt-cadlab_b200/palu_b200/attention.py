@@ -25,6 +25,7 @@ so they meet the interleaved RoPE tables, ``u_k`` = U_kᵀ in Meta order, ``wo_f
 from __future__ import annotations
 
 from dataclasses import dataclass
+from enum import Enum
 from typing import Optional
 
 import torch
@@ -35,6 +36,13 @@ from palu_b200.shard import KVShard, all_reduce_layer_output, layer_output_parti
 
 LLAMA3_SCALING = {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
                   "original_max_position_embeddings": 8192}
+
+
+class Mode(str, Enum):
+    """Forward mode (tt_transformers' ``Mode``, which the reference's ``forward`` dispatches on,
+    attention.py:735-740). Plain strings "decode" / "prefill" are accepted too."""
+    DECODE = "decode"
+    PREFILL = "prefill"
 
 
 @dataclass
@@ -177,11 +185,30 @@ class PaluAttention:
         return page_table.to(self.device, torch.int32).contiguous()
 
     @torch.no_grad()
-    def forward_decode(self, x: torch.Tensor, current_pos: torch.Tensor,
-                       page_table: Optional[torch.Tensor] = None, out_fp32: bool = True) -> torch.Tensor:
-        """x [B, dim] or [1, 1, B, dim]; current_pos [B] ints (each row's position; < 0 skips the row);
-        page_table [B, blocks per row] with paged caches. Returns the layer output in x's layout, fp32 (or,
-        with ``out_fp32`` False on one rank, the output GEMM's dtype, for a consumer that widens it itself)."""
+    def forward(self, x: torch.Tensor, current_pos: Optional[torch.Tensor] = None, rot_mats=None, user_id: int = 0,
+                mode=Mode.DECODE, page_table: Optional[torch.Tensor] = None, chunk_page_table=None,
+                chunk_start_idx=None, kv_cache=None) -> torch.Tensor:
+        """The reference layer's entry point (attention.py:735-740): ``mode`` PREFILL runs
+        ``forward_prefill``, DECODE ``forward_decode``, with the same arguments."""
+        m = Mode(mode.value if isinstance(mode, Enum) else str(mode).lower())
+        if m is Mode.PREFILL:
+            return self.forward_prefill(x, rot_mats, user_id, page_table=page_table, chunk_page_table=chunk_page_table,
+                                        chunk_start_idx=chunk_start_idx, kv_cache=kv_cache)
+        return self.forward_decode(x, current_pos, rot_mats, page_table=page_table, kv_cache=kv_cache)
+
+    @torch.no_grad()
+    def forward_decode(self, x: torch.Tensor, current_pos: torch.Tensor, rot_mats=None,
+                       page_table: Optional[torch.Tensor] = None, kv_cache=None, *,
+                       out_fp32: bool = True) -> torch.Tensor:
+        """The reference's ``forward_decode(x, current_pos, rot_mats=None, page_table=None, kv_cache=None)``
+        (attention.py:585). x [B, dim] or [1, 1, B, dim]; current_pos [B] ints (each row's position; < 0
+        skips the row); ``rot_mats`` is accepted and not used: q is rotated at ``current_pos`` from the
+        layer's own tables inside the fused q-rotation kernel. page_table [B, blocks per row] with paged
+        caches; ``kv_cache`` must be None (the layer owns its latent caches, as the reference asserts).
+        Returns the layer output in x's layout, fp32 (or, with ``out_fp32`` False on one rank, the output
+        GEMM's dtype, for a consumer that widens it itself)."""
+        if kv_cache is not None:
+            raise RuntimeError("kv_cache must be None: the layer owns its latent caches (attention.py:586)")
         shape4 = x.dim() == 4
         xb = (x.reshape(-1, x.shape[-1]) if shape4 else x).to(self.device)
         B = xb.shape[0]
@@ -216,13 +243,19 @@ class PaluAttention:
         return y.view(1, 1, B, self.dim) if shape4 else y
 
     @torch.no_grad()
-    def forward_prefill(self, x: torch.Tensor, user_id: Optional[int] = None,
-                        page_table: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """Prompt of P tokens at positions 0..P-1: x [B, P, dim] (cache rows 0..B-1), or [1, 1, P, dim] for
-        cache row ``user_id`` (the reference's per-user prefill). Writes the prompt's latents into the
-        caches and returns its causal attention output (fp32, x's layout) computed with torch SDPA on K and
-        V rebuilt from the cached (bf16) latents. With paged caches, ``page_table`` is the whole batch's
+    def forward_prefill(self, x: torch.Tensor, rot_mats=None, user_id: int = 0,
+                        page_table: Optional[torch.Tensor] = None, chunk_page_table=None, chunk_start_idx=None,
+                        kv_cache=None) -> torch.Tensor:
+        """The reference's ``forward_prefill(x_11SH, rot_mats, user_id=0, page_table=None, ...)``
+        (attention.py:382). Prompt of P tokens at positions 0..P-1: x [B, P, dim] (cache rows 0..B-1), or
+        [1, 1, P, dim] for cache row ``user_id`` (the reference's per-user prefill). ``rot_mats`` is accepted
+        and not used (the layer rotates from its own tables); chunked prefill (``chunk_page_table``,
+        ``chunk_start_idx``) and an external ``kv_cache`` are not supported. Writes the prompt's latents into
+        the caches and returns its causal attention output (fp32, x's layout) computed with torch SDPA on K
+        and V rebuilt from the cached (bf16) latents. With paged caches, ``page_table`` is the whole batch's
         table [max_batch or B, blocks per row] and the rows' latents go through it (paged_fill_cache)."""
+        if chunk_page_table is not None or chunk_start_idx is not None or kv_cache is not None:
+            raise RuntimeError("chunked prefill and an external kv_cache are not supported")
         shape4 = x.dim() == 4
         xb = (x.reshape(1, x.shape[-2], x.shape[-1]) if shape4 else x).to(self.device, torch.float32)
         B, P, _ = xb.shape

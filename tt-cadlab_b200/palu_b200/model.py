@@ -154,13 +154,14 @@ class PaluDecoder:
             x = fused.add_rms_norm(h, None, self.layers[0]["attn_norm"], eps)
             for i, L in enumerate(self.layers):
                 # on one rank the GEMM outputs stay bf16: the norm kernel widens them while adding
-                x = fused.add_rms_norm(h, L["attn"].forward_decode(x, pos, page_table, out_fp32=False),
+                x = fused.add_rms_norm(h, L["attn"].forward_decode(x, pos, page_table=page_table, out_fp32=False),
                                        L["ffn_norm"], eps)
                 nxt = self.layers[i + 1]["attn_norm"] if i + 1 < len(self.layers) else self.norm
                 x = fused.add_rms_norm(h, self._mlp(L, x, fp32=False), nxt, eps)
             return (x @ self.lm_head.t()).float()
         for L in self.layers:
-            h = h + L["attn"].forward_decode(rms_norm(h, L["attn_norm"], self.cfg.norm_eps), pos, page_table)
+            h = h + L["attn"].forward_decode(rms_norm(h, L["attn_norm"], self.cfg.norm_eps), pos,
+                                                  page_table=page_table)
             h = h + self._mlp(L, rms_norm(h, L["ffn_norm"], self.cfg.norm_eps))
         return self._logits(h)
 
