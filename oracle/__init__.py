@@ -27,6 +27,8 @@ from oracle.palu_ref import (  # noqa: F401
     w_rot_from_u_k,
     PaluRefAttention,
     reverse_permute,
+    seeded_decode_inputs,
+    input_checksums,
 )
 from oracle.metrics import rel_errors, rowwise_rel_errors  # noqa: F401
 from oracle.paged import paged_append, paged_gather, paged_scatter, shuffled_page_table  # noqa: F401

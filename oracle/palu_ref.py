@@ -171,6 +171,32 @@ def reference_decode_streamed(q, k_lat, u_k, v_lat, cur_pos, cos, sin, scale: fl
     return out
 
 
+def seeded_decode_inputs(seed: int, B: int, n_kv: int, n_q: int, S: int, r_k: int, r_v: int, group_size: int = 1):
+    """Seeded CPU inputs in the reference device tests' recipe (test_palu_sdpa_device.py:45-55, 218-231):
+    bf16-rounded q ~ N(0,1) [1, B, n_q, 128], latents ~ N(0,1) [B, n_kv // group_size, S, r], U_k ~ N(0, 1/r_k)
+    [n_kv, r_k, 128] and, for grouped latents, U_v ~ N(0, 1/r_v) [n_kv, r_v, 128]; drawn in this order from one
+    generator, so that a long-context fixture can store its seed instead of hundreds of MB of latents.
+    Returns (q, k_lat, v_lat, u_k, u_v or None), fp32 holding bf16 values."""
+    g = torch.Generator().manual_seed(seed)
+    bf = lambda t: t.to(torch.bfloat16).float()
+    n_lat = n_kv // group_size
+    q = bf(torch.randn(1, B, n_q, 128, generator=g))
+    k_lat = bf(torch.randn(B, n_lat, S, r_k, generator=g))
+    v_lat = bf(torch.randn(B, n_lat, S, r_v, generator=g))
+    u_k = bf(torch.randn(n_kv, r_k, 128, generator=g) / r_k ** 0.5)
+    u_v = bf(torch.randn(n_kv, r_v, 128, generator=g) / r_v ** 0.5) if group_size > 1 else None
+    return q, k_lat, v_lat, u_k, u_v
+
+
+def input_checksums(*tensors) -> torch.Tensor:
+    """float64 sums of each tensor and of its squares (None -> 0, 0): a fingerprint that a regenerated
+    input set must reproduce before its stored output is trusted."""
+    out = []
+    for t in tensors:
+        out += [0.0, 0.0] if t is None else [t.double().sum().item(), t.double().square().sum().item()]
+    return torch.tensor(out, dtype=torch.float64)
+
+
 def expand_groups(lat: torch.Tensor, group_size: int) -> torch.Tensor:
     """[B, n_groups, S, r] -> [B, n_groups * gs, S, r] (test_palu_sdpa_device.py:234-235)."""
     return lat.repeat_interleave(group_size, dim=1)

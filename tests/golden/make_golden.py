@@ -71,6 +71,21 @@ def decode_case(fused, seed, B, nkv, nh, S, r_k, r_v, group_size=1, identity=Fal
     return d
 
 
+def long_case(fused, seed, B, nkv, nh, S, r_k, r_v, positions):
+    """A long-context decode (the sweep's mixed-path layer at 32k positions) through the reference's own
+    reference_decode. The inputs are NOT stored: they are regenerated from ``seed`` by
+    ``oracle.seeded_decode_inputs`` (tens of MB of latents), and their checksums are stored so that the
+    consumer can verify it regenerated the same tensors before comparing against ``out``."""
+    import oracle
+    q, k_lat, v_lat, u_k, _ = oracle.seeded_decode_inputs(seed, B, nkv, nh, S, r_k, r_v)
+    pos = torch.tensor(positions, dtype=torch.int32)
+    cos, sin = fused.cos_sin_tables(128, S, THETA, LLAMA3)
+    cos, sin = _bf(cos), _bf(sin)
+    out = fused.reference_decode(q, k_lat, u_k, v_lat, pos, cos, sin, 128 ** -0.5)
+    return dict(seed=np.int64(seed), dims=np.array([B, nkv, nh, S, r_k, r_v], dtype=np.int64), cur_pos=pos,
+                checksums=oracle.input_checksums(q, k_lat, v_lat, u_k), scale=np.float32(128 ** -0.5), out=out)
+
+
 def layer_case(reference, convert, seed):
     """PaluRefAttention (reference.py:14-55) on a small llama3-scaled layer: prefill 24 tokens, then
     two decode steps. head_dim 128 so the same fixture drives the CUDA decode path."""
@@ -150,6 +165,10 @@ def main(ref_root: str):
     }
     for name, d in cases.items():
         np.savez_compressed(HERE / f"{name}.npz", **_np(d))
+    # long context: 2 rows of the sweep's r_k 32 / r_v 128 layer over 32768 positions (inputs from the seed)
+    np.savez_compressed(HERE / "decode_long_rk32_rv128_s32768.npz",
+                        **_np(long_case(fused, 12, B=2, nkv=8, nh=32, S=32768, r_k=32, r_v=128,
+                                        positions=[32767, 20000])))
     np.savez_compressed(HERE / "layer_mlrd_llama3.npz", **_np(layer_case(reference, convert, 6)))
     np.savez_compressed(HERE / "convert_mlrd_ragged.npz",
                         **_np(convert_case(convert, 7, 1, [16, 8, 32, 24], [32, 32, 16, 8], rank_multiple=8)))
