@@ -88,7 +88,9 @@ typedef struct palu_decode_dims {
  *   out      [B][n_q_heads][r_v or 128], out_dtype PALU_BF16 or PALU_F32
  *   workspace / workspace_bytes: >= palu_workspace_bytes(dims) bytes of device memory; its first 4
  *            bytes are a status word that must be zero when the workspace is first used (zero the
- *            buffer once after allocating it); see palu_read_status
+ *            buffer once after allocating it); see palu_read_status. While that word is nonzero (a
+ *            bounded device wait expired in an earlier call and nobody has cleared it), every call that
+ *            uses the workspace writes NaN to `out`
  *   scale    softmax scale (the reference passes head_dim ** -0.5)
  * Query head h attends KV head h / (n_q_heads / n_kv_heads), which reads latent head
  * kv / (n_kv_heads / n_groups). Positions above cur_pos[b] are masked; cur_pos[b] >= max_seq is
@@ -113,8 +115,9 @@ int palu_decode_attn(const void* q, const void* k_lat, const void* v_lat, const 
  * one device (other streams, other host threads) race on that array; calls in one stream are ordered
  * and safe. The first call on each device sets the array up (its address, and a zeroed status word) with
  * synchronous CUDA calls, so make it before any stream capture.
- * A bounded device wait that expires is recorded in the array's status word, which this entry point
- * does not report; use palu_decode_attn + palu_read_status where that report is needed.
+ * A bounded device wait that expires is recorded in the array's status word, and the merge then writes
+ * NaN in place of the call's output; palu_read_status(NULL, &status, stream) reads (and clears) that
+ * word for the current device.
  */
 int palu_decode_attn_static(const void* q, const void* k_lat, const void* v_lat, const void* u_k, int64_t u_k_ld,
                             const void* u_v, const void* cs_pairs, const int32_t* cur_pos, void* out,
@@ -227,12 +230,22 @@ int palu_pack_cs_table(const void* cs_tab, int64_t ld, int32_t in_dtype, void* c
  */
 int palu_set_kernel(int32_t which);
 
+/*
+ * Test hook for the timeout path of the tcgen05 decode kernel (no reference counterpart; not needed in
+ * normal use). For subsequent decode calls in this process: wait_ns > 0 bounds every device-side wait at
+ * wait_ns nanoseconds instead of the default 1 s (0 restores the default); starve_v nonzero makes one V
+ * producer per CTA issue no loads, so that a wait runs out on purpose. Such a call records status 1 in its
+ * workspace (palu_read_status), its merge writes NaN, and the device stays usable for the next call.
+ */
+int palu_set_wait_limit(int64_t wait_ns, int32_t starve_v);
+
 /* The kernel family a palu_decode_attn call with these dims would run (PALU_KERNEL_MMA or _TC). */
 int32_t palu_kernel_for(const palu_decode_dims* dims);
 
 /*
  * Read (and clear) the status word a decode call left in `workspace`: 0 = ok, 1 = a bounded device
- * wait expired (the call's output is then invalid). Synchronises `stream`. No reference counterpart:
+ * wait expired (the call's output is then NaN). workspace NULL reads the static scratch of
+ * palu_decode_attn_static on the current device. Synchronises `stream`. No reference counterpart:
  * the Tensix op has no bounded waits (its known hangs were capped by the host, README.md:301-329).
  */
 int palu_read_status(void* workspace, int32_t* status, palu_stream_t stream);

@@ -22,45 +22,66 @@ pytestmark = pytest.mark.gpu
 THETA = 500000.0
 
 
-def _case(g, dev, B, nkv, nh, S, r_k, r_v):
+def _case(g, dev, B, nkv, n_lat, S, r_k, r_v, grouped):
     bf = torch.bfloat16
-    k_lat = torch.randn(B, nkv, S, r_k, generator=g).to(dev, bf)
-    v_lat = torch.randn(B, nkv, S, r_v, generator=g).to(dev, bf)
+    k_lat = torch.randn(B, n_lat, S, r_k, generator=g).to(dev, bf)
+    v_lat = torch.randn(B, n_lat, S, r_v, generator=g).to(dev, bf)
     u_k = (torch.randn(nkv, r_k, 128, generator=g) / r_k ** 0.5).to(dev, bf)
+    u_v = (torch.randn(nkv, r_v, 128, generator=g) / r_v ** 0.5).to(dev, bf) if grouped else None
     cos, sin = oracle.cos_sin_tables(128, S, THETA, None)
-    return k_lat, v_lat, u_k, cos[:S], sin[:S]
+    return k_lat, v_lat, u_k, u_v, cos[:S], sin[:S]
 
 
-def _call(lib, static, q, k_lat, v_lat, u_k, cs_pairs, pos, out, d, ws):
+def _call(lib, static, q, k_lat, v_lat, u_k, u_v, cs_pairs, pos, out, d, ws):
     from palu_b200 import _lib
     stream = _lib.stream_handle(q.device)
-    common = (q.data_ptr(), k_lat.data_ptr(), v_lat.data_ptr(), u_k.data_ptr(), 128, None, cs_pairs.data_ptr(),
-              pos.data_ptr(), out.data_ptr(), _lib.PALU_F32)
+    common = (q.data_ptr(), k_lat.data_ptr(), v_lat.data_ptr(), u_k.data_ptr(), 128, _lib.ptr(u_v),
+              cs_pairs.data_ptr(), pos.data_ptr(), out.data_ptr(), _lib.PALU_F32)
     if static:
         return lib.palu_decode_attn_static(*common, ctypes.byref(d), 128 ** -0.5, stream)
     return lib.palu_decode_attn(*common, ws.data_ptr(), ws.numel(), ctypes.byref(d), 128 ** -0.5, stream)
 
 
-def test_static_scratch_matches_workspace_entry_point_twice(cuda):
+@pytest.fixture(params=["tc", "mma"])
+def kernel_family(request, cuda):
+    """Both kernel families keep their partials in the static scratch; the choice is restored afterwards."""
+    from palu_b200 import _lib
+    _lib.set_kernel(_lib.PALU_KERNEL_TC if request.param == "tc" else _lib.PALU_KERNEL_MMA)
+    try:
+        yield request.param
+    finally:
+        _lib.set_kernel(_lib.PALU_KERNEL_AUTO)
+
+
+# (B, KV heads, latent heads, S, r_k, r_v): M-LRD with absorbed V, and grouped latents with V rebuilt per head
+CASES = [(8, 8, 8, 2048, 64, 64), (4, 8, 2, 1500, 128, 128)]
+
+
+@pytest.mark.parametrize("case", CASES, ids=["mlrd", "grouped_uv"])
+def test_static_scratch_matches_workspace_entry_point_twice(cuda, kernel_family, case):
     from palu_b200 import _lib, fused
     lib = _lib.load()
     g = torch.Generator().manual_seed(7)
-    B, nkv, nh, S, r_k, r_v = 8, 8, 32, 2048, 64, 64
-    k_lat, v_lat, u_k, cos, sin = _case(g, cuda, B, nkv, nh, S, r_k, r_v)
+    B, nkv, n_lat, S, r_k, r_v = case
+    nh = 4 * nkv
+    grouped = n_lat != nkv
+    k_lat, v_lat, u_k, u_v, cos, sin = _case(g, cuda, B, nkv, n_lat, S, r_k, r_v, grouped)
     cs_pairs = fused.pack_cs_table(fused.cs_table(cos, sin, S).to(cuda, torch.bfloat16))
-    d = _lib.dims(B, nh, nkv, nkv, r_k, r_v, S)
+    d = _lib.dims(B, nh, nkv, n_lat, r_k, r_v, S)
     ws = _lib.new_workspace(d, cuda)
+    width = 128 if grouped else r_v
     for call in range(2):
         q = torch.randn(B, nh, 128, generator=g).to(cuda, torch.bfloat16)
         pos = torch.randint(0, S, (B,), generator=g, dtype=torch.int32)
         pos[call] = S - 1
         pos = pos.to(cuda)
-        want = torch.full((B, nh, r_v), float("nan"), device=cuda)
-        got = torch.full((B, nh, r_v), float("nan"), device=cuda)
-        _lib.check(_call(lib, False, q, k_lat, v_lat, u_k, cs_pairs, pos, want, d, ws))
-        _lib.check(_call(lib, True, q, k_lat, v_lat, u_k, cs_pairs, pos, got, d, None))
+        want = torch.full((B, nh, width), float("nan"), device=cuda)
+        got = torch.full((B, nh, width), float("nan"), device=cuda)
+        _lib.check(_call(lib, False, q, k_lat, v_lat, u_k, u_v, cs_pairs, pos, want, d, ws))
+        _lib.check(_call(lib, True, q, k_lat, v_lat, u_k, u_v, cs_pairs, pos, got, d, None))
         torch.cuda.synchronize()
-        assert _lib.read_status(ws) == 0, "a bounded device wait expired"
+        assert _lib.read_status(ws) == 0, "a bounded device wait expired (workspace call)"
+        assert _lib.read_status(None) == 0, "a bounded device wait expired (static scratch)"
         assert torch.isfinite(got).all(), f"call {call}: output not fully written"
         mx, mn = rel_errors(got.cpu(), want.cpu())
         assert mx <= MAX_REL and mn <= MEAN_REL, f"call {call}: max {mx:.3e} mean {mn:.3e}"

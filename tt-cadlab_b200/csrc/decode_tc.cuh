@@ -8,9 +8,10 @@
 // CTA-local tiles t with t % 2 == g), so two tiles are in flight per CTA. Each group has its own warps,
 // rings, barriers and TMEM columns (24 warps in all, see role_of): a K+table TMA producer, a V producer, a
 // QK+PV issuer, a reconstruct issuer (a single thread issues at most one tcgen05.mma per ~64 cycles
-// whatever its shape, measured on B200, so the MMAs are split over two threads), 4 RoPE warps and 4 softmax
-// warps (a warp of either kind owns the 32 TMEM lanes of its SMSP quarter: 32 token rows of the tile, or
-// 32 latent dims of the PV output).
+// whatever its shape, measured on B200, so the MMAs are split over two threads; QK(j) and PV(j - 1) stay on
+// one thread, in that order: with PV on a third thread its MMAs interleave with QK's in the tensor pipe and
+// the op measured 20 % slower on B200), 4 RoPE warps and 4 softmax warps (a warp of either kind owns the 32
+// TMEM lanes of its SMSP quarter: 32 token rows of the tile, or 32 latent dims of the PV output).
 // At start the RoPE warps stage U_k (bf16) in shared memory with its head dims reordered as
 // [even dims | odd dims] per half of the frequencies, so that D_k holds each rotation pair (2f, 2f+1) 32
 // columns apart and the rotation of two adjacent frequencies is one packed half2 operation. The softmax
@@ -28,9 +29,9 @@
 // tile j + 1 and the QK MMAs of half h of tile j are issued, so the reconstruct latency overlaps the
 // rotation of the other half; RoPE(j + 1) overlaps softmax(j) and PV(j - 1). D_s, D_o and P are
 // double-buffered by j % 2, and every consumer releases what it read with its own barrier, so no barrier
-// runs two phases ahead of a waiter. Every wait is bounded
-// (1 s of globaltimer): on expiry the CTA records a status code, all roles stop, copies and MMAs in flight
-// are drained, and TMEM is freed.
+// runs two phases ahead of a waiter. Every wait is bounded (1 s of globaltimer by default): on expiry the CTA records a
+// status code, all roles stop (the multi-lane warps agree on it, so none is left divergent), copies and
+// MMAs in flight are drained, and TMEM is freed.
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -40,7 +41,12 @@
 namespace palu {
 namespace tc {
 
-constexpr int kThreads = 768;
+// Warps: 8 single-lane role warps (see role_of), then 8 RoPE warps and 8 softmax warps (4 per group). A
+// RoPE or softmax warp w owns TMEM lanes 32 (w % 4) .. + 31.
+constexpr int kRoleWarps = 8;
+constexpr int kRopeWarp0 = kRoleWarps;
+constexpr int kSoftWarp0 = kRoleWarps + 8;
+constexpr int kThreads = (kRoleWarps + 16) * 32;
 constexpr int kTile = 128;
 constexpr int kBox = 16384;             // one TMA box: 128 rows x 128 B
 constexpr int kTmemCols = 512;
@@ -67,6 +73,15 @@ struct TcParams {
   // [n_blocks][n_groups][bs][r] caches; the tensor maps then have boxes of bs rows.
   const int32_t* page_table;
   int table_ld, blk_shift, n_blocks;
+  // Bound on any single wait (ns), and a test switch: nonzero makes group 0's V producer issue no loads, so
+  // that a wait runs out on purpose (the test of the timeout path; never set in normal use).
+  unsigned long long wait_ns;
+  int starve_v;
+  // Nonzero when every CTA of the grid is resident at once (one wave): the merge, a programmatic dependent,
+  // may then be launched as soon as the CTAs start, so its CTAs take SMs as decode CTAs finish and wait there
+  // (griddepcontrol.wait) instead of being launched after the last one. With more CTAs than one wave the
+  // trigger stays implicit at exit, so no merge CTA can hold an SM a decode CTA is still waiting for.
+  int pdl_early;
 };
 
 // Work split: the tiles of one KV head over all batch rows, in row order (row b has ceil(L_b / 128)
@@ -138,23 +153,34 @@ struct GroupTiles {
   }
 };
 
+// Shared memory per CTA: the fixed buffers plus three rings, K (NS_K stages), V (NS_V stages) and the RoPE
+// table (T_SLOTS chunk slots per group). Stage i of the K and V rings holds tiles of group i % 2 only. The
+// first of these (NS_K, NS_V, T_SLOTS) choices that fits is used: two K stages per group, one V stage per
+// group and a whole tile of table chunks, when the latents are at most 64 wide.
+constexpr int kTabChunkBytes = 8192;  // table chunk: 128 rows x 16 pairs x 4 B (SWIZZLE_64B)
+constexpr int kSmemBudget = 227 * 1024;
+constexpr int layout_need(int fixed, int kb, int vb, int nk, int nv, int t) {
+  return fixed + nk * kb + nv * vb + 2 * t * kTabChunkBytes;
+}
+constexpr int layout_pick(int fixed, int kb, int vb) {
+  constexpr int c[4][3] = {{4, 2, 4}, {2, 2, 4}, {4, 2, 2}, {2, 2, 2}};
+  for (int i = 0; i < 4; ++i)
+    if (layout_need(fixed, kb, vb, c[i][0], c[i][1], c[i][2]) <= kSmemBudget) return c[i][0] * 100 + c[i][1] * 10 + c[i][2];
+  return 222;
+}
+
 template <int KBK, int KBV>
 struct Layout {
   static constexpr int K_BYTES = KBK * kBox;
   static constexpr int V_BYTES = KBV * kBox;
-  static constexpr int TCH_BYTES = 8192;              // table chunk: 128 rows x 16 pairs x 4 B (SWIZZLE_64B)
+  static constexpr int TCH_BYTES = kTabChunkBytes;
   static constexpr int U_BYTES = KBK * 2 * 64 * 128;  // 2 N-blocks x (<= 64 KBK rows) x 128 B
   static constexpr int Q_BYTES = 2 * 2048;            // one buffer: 2 K-blocks x 16 rows x 128 B (fp16)
   static constexpr int P_BYTES = 2 * 2048;            // one buffer: 2 K-blocks x 16 rows x 128 B (bf16)
   static constexpr int MISC_BYTES = 2048;
   static constexpr int FIXED = U_BYTES + 4 * Q_BYTES + 4 * P_BYTES + MISC_BYTES + 1024;
-  static constexpr int BUDGET = 227 * 1024;
-  // Rings, all group-private: stage i of a ring only holds tiles of group (i % 2) (K, V) or chunks of
-  // group (i / T_SLOTS) (table). V: one stage per group. Table: 4 chunk slots per group (a whole tile)
-  // when that fits, else 2. K: 2 stages per group when that fits, else 1.
-  static constexpr int NS_V = 2;
-  static constexpr int T_SLOTS = FIXED + 2 * K_BYTES + NS_V * V_BYTES + 8 * TCH_BYTES <= BUDGET ? 4 : 2;
-  static constexpr int NS_K = FIXED + 4 * K_BYTES + NS_V * V_BYTES + 2 * T_SLOTS * TCH_BYTES <= BUDGET ? 4 : 2;
+  static constexpr int PICK = layout_pick(FIXED, K_BYTES, V_BYTES);
+  static constexpr int NS_K = PICK / 100, NS_V = PICK / 10 % 10, T_SLOTS = PICK % 10;
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + NS_K * K_BYTES;
   static constexpr int OFF_TAB = OFF_V + NS_V * V_BYTES;
@@ -163,7 +189,8 @@ struct Layout {
   static constexpr int OFF_P = OFF_Q + 4 * Q_BYTES;  // Q: [group][segment parity], P: [group][tile parity]
   static constexpr int OFF_MISC = OFF_P + 4 * P_BYTES;
   static constexpr int TOTAL = OFF_MISC + MISC_BYTES + 1024;  // + slack to align the base to 1024
-  static_assert(TOTAL <= BUDGET, "shared memory budget");
+  static_assert(TOTAL <= kSmemBudget, "shared memory budget");
+  static_assert(NS_K % 2 == 0 && NS_V % 2 == 0, "K and V stages come in pairs, one per group");
 };
 
 // ---- PTX wrappers -----------------------------------------------------------------------------------
@@ -201,19 +228,27 @@ PALU_DEVINL unsigned long long globaltimer() {
   return t;
 }
 
-// Bounded wait for `parity` on `bar`. Returns false on timeout or when another role already gave up.
-PALU_DEVINL bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
-  if (mbar_try(bar, parity)) return true;
+// Bounded wait for `parity` on `bar` (at most `limit_ns`). Returns false on timeout or when another role
+// already gave up. The polling loop is one out-of-line function: inlined at each of the ~20 wait sites it
+// grew the kernel body past what the instruction cache serves well (no_instruction stalls), and the op
+// measured 2-4 % faster on B200 with one shared copy.
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                            unsigned long long limit_ns) {
   const unsigned long long t0 = globaltimer();
   for (;;) {
     if (mbar_try(bar, parity)) return true;
     if (*abort_flag) return mbar_try(bar, parity);
-    if (globaltimer() - t0 > kWaitNs) {
+    if (globaltimer() - t0 > limit_ns) {
       *abort_flag = 1;
       atomicExch(status, kStatusTimeout);
       return false;
     }
   }
+}
+PALU_DEVINL bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
+                           unsigned long long limit_ns) {
+  if (mbar_try(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, abort_flag, status, limit_ns);
 }
 
 // Bounded wait used on the abort path, to let copies already in flight land before the CTA exits.
@@ -247,9 +282,10 @@ PALU_DEVINL uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
          ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 // Instruction descriptor, kind::f16 with f32 accumulate, M = 128. fmt: 0 = f16, 1 = bf16 (A and B alike).
-__host__ __device__ constexpr uint32_t idesc_f16(int n, uint32_t fmt, bool a_mn_major, bool b_mn_major) {
+// M = 128 or 64 (an M = 64 accumulator holds its rows in lanes 0..15 of each 32-lane quarter).
+__host__ __device__ constexpr uint32_t idesc_f16(int n, uint32_t fmt, bool a_mn_major, bool b_mn_major, int m = 128) {
   return (1u << 4) | (fmt << 7) | (fmt << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
-         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
 PALU_DEVINL void mma_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
@@ -378,12 +414,10 @@ PALU_DEVINL void tmem_st4(uint32_t taddr, const uint32_t (&r)[4]) {
                : "memory");
 }
 
-// Warp roles (24 warps). Warps 0..7 are single-lane role warps, two per SMSP (warp w runs on SMSP w % 4):
+// Roles of the single-lane warps, two of each per group; warp w runs on SMSP w % 4:
 //   group 0: 0 = K+table producer, 1 = QK+PV issuer, 2 = reconstruct issuer, 3 = V producer
 //   group 1: 4 = QK+PV issuer, 5 = K+table producer, 6 = V producer, 7 = reconstruct issuer
-// Warps 8..15: RoPE warps (group (w - 8) / 4), warps 16..23: softmax warps (group (w - 16) / 4); warp w of
-// either kind owns TMEM lanes 32 (w % 4) .. + 31, i.e. token rows (tile) or latent dims (PV output).
-enum : int { kRoleKT = 0, kRoleQK = 1, kRoleRP = 2, kRoleV = 3 };
+enum : int { kRoleKT = 0, kRoleQK = 1, kRoleRC = 2, kRoleV = 3 };
 PALU_DEVINL int role_of(int warp) {
   switch (warp) {
     case 0:
@@ -391,12 +425,15 @@ PALU_DEVINL int role_of(int warp) {
     case 1:
     case 4: return kRoleQK;
     case 2:
-    case 7: return kRoleRP;
+    case 7: return kRoleRC;
     default: return kRoleV;
   }
 }
 
-template <int KBK, int KBV>
+// PAGED: the caches are paged (TcParams.page_table set). A template parameter rather than a runtime branch,
+// so that the contiguous-cache kernel carries none of the paged producers' code: with it the body fit the
+// instruction cache worse, and dropping it measured 2-4 % faster on B200.
+template <int KBK, int KBV, bool PAGED>
 __global__ void __launch_bounds__(kThreads, 1)
     palu_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                           const __grid_constant__ CUtensorMap tm_tab, const TcParams p) {
@@ -417,6 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto bar = [&](int i) { return smem_u32(bars + i); };
   // [g][x] pairs are double-buffered by the group-local tile index parity x.
   // V-full barriers are per (slot, use parity), so a parity wait is never more than one phase behind.
+  // Drain barriers: [g][QK+PV issuer, reconstruct issuer].
   constexpr int B_KF = 0, B_KE = B_KF + NS_K, B_VF = B_KE + NS_K, B_VE = B_VF + 2 * NS_V, B_TF = B_VE + NS_V,
                 B_TE = B_TF + NS_T, B_UF = B_TE + NS_T, B_REC = B_UF + 1, B_AF = B_REC + 4, B_AE = B_AF + 4,
                 B_SF = B_AE + 2, B_SR = B_SF + 4, B_PF = B_SR + 4, B_OF = B_PF + 4, B_OR = B_OF + 4,
@@ -425,6 +463,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
   int* s_range = reinterpret_cast<int*>(s_tmem + 4);      // n, b0, t0, cnt0 of this CTA's range
   float* s_max = reinterpret_cast<float*>(s_tmem + 8);    // [2 groups][2 bufs][4 warps][4 heads]
+  static_assert((B_COUNT + 8) * 8 + 64 * 4 <= Lay::MISC_BYTES, "misc area");
+
+  // Bounded waits. The RoPE and softmax warps use wait_all: every lane of the warp gets the same answer, so
+  // that when the CTA gives up no warp is left divergent before its next .sync.aligned instruction. A phase
+  // that has already completed is seen by the whole converged warp in one try_wait, so the vote is taken on
+  // the spinning path only.
+  auto wait = [&](uint32_t b, uint32_t ph) -> bool { return mbar_wait(b, ph, s_abort, p.status, p.wait_ns); };
+  auto wait_all = [&](uint32_t b, uint32_t ph) -> bool {
+    if (__all_sync(0xffffffffu, mbar_try(b, ph))) return true;
+    return __all_sync(0xffffffffu, mbar_wait_slow(b, ph, s_abort, p.status, p.wait_ns)) != 0;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS_K; ++s) {
@@ -495,20 +544,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       s_range[3] = cnt0;
     }
   }
-  if (warp >= 16) {
+  if (warp >= kSoftWarp0) {
     // Q buffers (4 x 4 KB) and P buffers (4 x 4 KB): rows past the query heads stay zero throughout.
-    for (int e = (warp - 16) * 32 + lane; e < (4 * Lay::Q_BYTES + 4 * Lay::P_BYTES) / 16; e += 256)
+    for (int e = (warp - kSoftWarp0) * 32 + lane; e < (4 * Lay::Q_BYTES + 4 * Lay::P_BYTES) / 16; e += 256)
       reinterpret_cast<uint4*>(smem + Lay::OFF_Q)[e] = make_uint4(0, 0, 0, 0);
     fence_proxy_async();
   }
   fence_before();
   __syncthreads();
   fence_after();
+  if (p.pdl_early) asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   const uint32_t tmem = *s_tmem;
   const int n = s_range[0];                                  // tiles of this CTA
   const RowSeg seg0{s_range[1], s_range[2], s_range[3], 0};  // its first segment
 
-  if (warp < 8) {
+  if (warp < kRoleWarps) {
     // ============================== single-lane role warps ==============================
     const int g = warp < 4 ? 0 : 1, role = role_of(warp);
     const int n_g = (n - g + 1) / 2;  // this group's tiles: CTA-local t = g + 2 j, j < n_g
@@ -516,6 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (role == kRoleKT || role == kRoleV) {
         // ---- TMA producers: K tile then its 4 table chunks (KT), or the V tile (V), per group tile.
         const bool kt = role == kRoleKT;
+        const bool starve = !kt && g == 0 && p.starve_v;  // test of the timeout path only
         tma_prefetch_map(kt ? &tm_k : &tm_v);
         if (kt) tma_prefetch_map(&tm_tab);
         int issued_kv = 0, issued_t = 0;
@@ -531,7 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // entry beyond the row's length is read; an entry outside [0, n_blocks) becomes a coordinate
           // past the tensor map, which the copy fills with zeros.
           int blk[kTile / 16];
-          if (p.page_table) {
+          if constexpr (PAGED) {
             const int32_t* pt = p.page_table + (size_t)it.s.b * p.table_ld;
             const int last = (it.len - 1) >> p.blk_shift, lb0 = row >> p.blk_shift;
 #pragma unroll
@@ -541,28 +592,31 @@ __global__ void __launch_bounds__(kThreads, 1)
                 blk[i] = (unsigned)e < (unsigned)p.n_blocks ? e * p.n_groups + lat_head : p.n_blocks * p.n_groups;
               }
           }
-          if (use >= 1 && !mbar_wait(empty, (use - 1) & 1, s_abort, p.status)) break;
-          const CUtensorMap* tm = kt ? &tm_k : &tm_v;
-          const uint32_t dst = sbase + (kt ? Lay::OFF_K + sb * Lay::K_BYTES : Lay::OFF_V + sb * Lay::V_BYTES);
-          const int nbox = kt ? KBK : KBV;
-          mbar_expect_tx(full, kt ? Lay::K_BYTES : Lay::V_BYTES);
-          if (!p.page_table) {
-            for (int c = 0; c < nbox; ++c) tma_load_3d(dst + c * kBox, tm, full, c * 64, row, item_lat);
-          } else {
-            // one box of bs rows per block; bs * 128 B is a whole number of 1 KB swizzle atoms, so the
-            // rows land exactly where one 128-row box would put them
-            const int nsub = kTile >> p.blk_shift, sub_bytes = 128 << p.blk_shift;
+          if (use >= 1 && !wait(empty, (use - 1) & 1)) break;
+          if (!starve) {
+            const CUtensorMap* tm = kt ? &tm_k : &tm_v;
+            const uint32_t dst = sbase + (kt ? Lay::OFF_K + sb * Lay::K_BYTES : Lay::OFF_V + sb * Lay::V_BYTES);
+            const int nbox = kt ? KBK : KBV;
+            mbar_expect_tx(full, kt ? Lay::K_BYTES : Lay::V_BYTES);
+            if constexpr (!PAGED) {
+              for (int c = 0; c < nbox; ++c) tma_load_3d(dst + c * kBox, tm, full, c * 64, row, item_lat);
+            } else {
+              // one box of bs rows per block; bs * 128 B is a whole number of 1 KB swizzle atoms, so the
+              // rows land exactly where one 128-row box would put them
+              const int nsub = kTile >> p.blk_shift, sub_bytes = 128 << p.blk_shift;
 #pragma unroll
-            for (int i = 0; i < kTile / 16; ++i)
-              if (i < nsub)
-                for (int c = 0; c < nbox; ++c) tma_load_3d(dst + c * kBox + i * sub_bytes, tm, full, c * 64, 0, blk[i]);
+              for (int i = 0; i < kTile / 16; ++i)
+                if (i < nsub)
+                  for (int c = 0; c < nbox; ++c)
+                    tma_load_3d(dst + c * kBox + i * sub_bytes, tm, full, c * 64, 0, blk[i]);
+            }
+            issued_kv = j + 1;
           }
-          issued_kv = j + 1;
           if (kt) {
             bool ok = true;
             for (int c = 0; c < 4; ++c) {
               const int nc = 4 * j + c, ts = g * T_SLOTS + nc % T_SLOTS, tuse = nc / T_SLOTS;
-              if (tuse >= 1 && !mbar_wait(bar(B_TE + ts), (tuse - 1) & 1, s_abort, p.status)) {
+              if (tuse >= 1 && !wait(bar(B_TE + ts), (tuse - 1) & 1)) {
                 ok = false;
                 break;
               }
@@ -590,9 +644,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           // ---- QK(j): D_s[j & 1] = K_rot (TMEM, fp16) x Q^T in two halves, half h once RoPE(j) wrote A half h
           // (and, first, once softmax(j - 2) read D_s[j & 1]); then PV(j - 1) once softmax(j - 1) wrote P.
           // (PV first measured slower on B200: waiting for P(j - 1) then delays QK(j) and the RoPE chain.)
+          // The commit after QK(j) also covers PV(j - 2), issued before it by this thread: once softmax(j) sees
+          // D_s[j & 1], P[j & 1] is free to rewrite.
           // Q: the group's buffer of the tile's row, staged by the softmax warps per group segment.
           constexpr uint32_t ID_QK = idesc_f16(16, 0, false, false);
-          constexpr uint32_t ID_PV = idesc_f16(16, 1, true, false);  // bf16 V^T (MN-major) x bf16 P
+          // bf16 V^T (MN-major) x bf16 P. A V latent at most 64 wide is one M = 64 block: with M = 128 the
+          // MMA read every V row twice (measured 1.6 % faster at the bench workload with M = 64).
+          constexpr uint32_t ID_PV = idesc_f16(16, 1, true, false, KBV == 1 ? 64 : 128);
           const uint32_t v_lbo = p.rv > 64 ? kBox : 0;  // V: second 64-dim M-block (or a duplicate of the first)
           GroupTiles it, pit;  // QK(j) and PV(j - 1) tiles
           it.init(p, seg0, g, n);
@@ -600,14 +658,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j <= n_g; ++j) {
             if (j < n_g) {
               const int qb = it.sigma & 1;
-              if (it.first() && !mbar_wait(bar(B_QF + 2 * g + qb), (it.sigma >> 1) & 1, s_abort, p.status)) break;
-              if (j >= 2 && !mbar_wait(bar(B_SR + 2 * g + (j & 1)), ((j >> 1) - 1) & 1, s_abort, p.status)) break;
+              if (it.first() && !wait(bar(B_QF + 2 * g + qb), (it.sigma >> 1) & 1)) break;
+              if (j >= 2 && !wait(bar(B_SR + 2 * g + (j & 1)), ((j >> 1) - 1) & 1)) break;
               const uint32_t sQ = sbase + Lay::OFF_Q + (2 * g + qb) * Lay::Q_BYTES;
               it.next(p);
               bool ok = true;
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
-                if (!mbar_wait(bar(B_AF + 2 * g + h), j & 1, s_abort, p.status)) {
+                if (!wait(bar(B_AF + 2 * g + h), j & 1)) {
                   ok = false;
                   break;
                 }
@@ -625,9 +683,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (j >= 1) {  // PV(j - 1)
               const int jp = j - 1, tp = g + 2 * jp, sv = tp % NS_V;
-              if (!mbar_wait(bar(B_PF + 2 * g + (jp & 1)), (jp >> 1) & 1, s_abort, p.status)) break;
-              if (jp >= 2 && !mbar_wait(bar(B_OR + 2 * g + (jp & 1)), ((jp >> 1) - 1) & 1, s_abort, p.status)) break;
-              if (!mbar_wait(bar(B_VF + 2 * sv + ((tp / NS_V) & 1)), (tp / NS_V >> 1) & 1, s_abort, p.status)) break;
+              if (!wait(bar(B_PF + 2 * g + (jp & 1)), (jp >> 1) & 1)) break;
+              if (jp >= 2 && !wait(bar(B_OR + 2 * g + (jp & 1)), ((jp >> 1) - 1) & 1)) break;
+              if (!wait(bar(B_VF + 2 * sv + ((tp / NS_V) & 1)), (tp / NS_V >> 1) & 1)) break;
               // A row's last tile may be partial. V rows past cur_pos may hold anything (NaN included) and
               // 0 * NaN is not 0, so for such a tile the MMA takes only the 16-token K-steps that hold valid
               // rows, and the invalid rows inside the last of them are zeroed here first: by this thread, whose
@@ -669,7 +727,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t u_lbo = p.rk * 128;  // U: stride between the two 64-column N-blocks
           auto recon = [&](int j, int h) -> bool {
             const int t = g + 2 * j, s = t % NS_K;
-            if (h == 0 && !mbar_wait(bar(B_KF + s), (t / NS_K) & 1, s_abort, p.status)) return false;
+            if (h == 0 && !wait(bar(B_KF + s), (t / NS_K) & 1)) return false;
             fence_after();
             const uint32_t sK = sbase + Lay::OFF_K + s * Lay::K_BYTES;
             for (int kk = 0; kk < p.rk / 16; ++kk)
@@ -679,10 +737,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_commit(bar(B_REC + 2 * g + h));
             return true;
           };
-          bool ok = mbar_wait(bar(B_UF), 0, s_abort, p.status) && recon(0, 0) && recon(0, 1);
+          bool ok = wait(bar(B_UF), 0) && recon(0, 0) && recon(0, 1);
           for (int j = 0; ok && j + 1 < n_g; ++j)
-            for (int h = 0; ok && h < 2; ++h)
-              ok = mbar_wait(bar(B_AF + 2 * g + h), j & 1, s_abort, p.status) && recon(j + 1, h);
+            for (int h = 0; ok && h < 2; ++h) ok = wait(bar(B_AF + 2 * g + h), j & 1) && recon(j + 1, h);
         }
         // Drain: every MMA this thread issued has completed once this barrier flips.
         mma_commit(bar(drain));
@@ -690,9 +747,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp < 16) {
+  } else if (warp < kSoftWarp0) {
     // ============================== RoPE warps ==============================
-    const int g = (warp - 8) >> 2, quarter = warp & 3, row = quarter * 32 + lane;
+    const int g = (warp - kRopeWarp0) >> 2, quarter = warp & 3, row = quarter * 32 + lane;
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + g * kGrpCols;
     {
       // U_k -> shared memory as the MN-major SWIZZLE_128B B operand of the reconstruction, one 64-column
@@ -700,7 +757,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // (columns 0..31), then their odd dims (columns 32..63).
       // Item: (latent row r, source dims 16 a .. 16 a + 15 = frequencies 8 a .. 8 a + 7) -> 16-byte chunks
       // a % 4 (even dims) and 4 + a % 4 (odd dims) of row r of N-block a / 4.
-      for (int e = (warp - 8) * 32 + lane; e < p.rk * 8; e += 256) {
+      for (int e = (warp - kRopeWarp0) * 32 + lane; e < p.rk * 8; e += 256) {
         const int r = e >> 3, a = e & 7;
         const uint4* src = reinterpret_cast<const uint4*>(p.u_k + ((size_t)kvh * p.rk + r) * p.ld_u + 16 * a);
         const uint4 x0 = src[0], x1 = src[1];
@@ -727,7 +784,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int ch = 0; ch < 4; ++ch) {
         const int h = ch >> 1, sub = ch & 1;
         if (sub == 0) {
-          if (!mbar_wait(bar(B_REC + 2 * g + h), i & 1, s_abort, p.status)) {
+          if (!wait_all(bar(B_REC + 2 * g + h), i & 1)) {
             ok = false;
             break;
           }
@@ -738,7 +795,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t ke[16], ko[16];
         tmem_ld16(trow + kColDk + 64 * h + 16 * sub, ke);
         tmem_ld16(trow + kColDk + 64 * h + 32 + 16 * sub, ko);
-        if (!mbar_wait(bar(B_TF + sb), (n / T_SLOTS) & 1, s_abort, p.status)) {
+        if (!wait_all(bar(B_TF + sb), (n / T_SLOTS) & 1)) {
           tmem_wait_ld_regs(ke, ko);
           ok = false;
           break;
@@ -780,8 +837,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           // A half h still feeds half h of QK(i - 1) until those MMAs complete: their commit is AE (h = 0)
           // or the scores barrier (h = 1).
           const int jq = i - 1;
-          const bool freed = h == 0 ? mbar_wait(bar(B_AE + g), jq & 1, s_abort, p.status)
-                                    : mbar_wait(bar(B_SF + 2 * g + (jq & 1)), (jq >> 1) & 1, s_abort, p.status);
+          const bool freed = h == 0 ? wait_all(bar(B_AE + g), jq & 1)
+                                    : wait_all(bar(B_SF + 2 * g + (jq & 1)), (jq >> 1) & 1);
           if (!freed) {
             ok = false;
             break;
@@ -803,7 +860,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ============================== softmax warps ==============================
-    const int g = (warp - 16) >> 2, quarter = warp & 3, row = quarter * 32 + lane;
+    const int g = (warp - kSoftWarp0) >> 2, quarter = warp & 3, row = quarter * 32 + lane;
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + g * kGrpCols;
     // Q^T of a batch row into the group's Q buffer `buf`: fp16, K-major SWIZZLE_128B, 16 rows (this KV
     // head's query heads; the rest stay zero) x 128 dims in [even | odd] order: K-block 0 = even dims,
@@ -867,7 +924,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // ---- softmax(j) -------------------------------------------------------------------------------
           if (x < cnt) {
             const int j = j0 + x;
-            if (!mbar_wait(bar(B_SF + 2 * g + (j & 1)), (j >> 1) & 1, s_abort, p.status)) {
+            if (!wait_all(bar(B_SF + 2 * g + (j & 1)), (j >> 1) & 1)) {
               ok = false;
               break;
             }
@@ -893,7 +950,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int h = 0; h < 4; ++h) smx[quarter * 4 + h] = mx[h];
               mbar_arrive(bar(B_MX + 2 * g + (j & 1)));
             }
-            if (!mbar_wait(bar(B_MX + 2 * g + (j & 1)), (j >> 1) & 1, s_abort, p.status)) {
+            if (!wait_all(bar(B_MX + 2 * g + (j & 1)), (j >> 1) & 1)) {
               ok = false;
               break;
             }
@@ -923,7 +980,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // ---- accumulate(j - 1) --------------------------------------------------------------------------
           if (x >= 1) {
             const int ja = j0 + x - 1;
-            if (!mbar_wait(bar(B_OF + 2 * g + (ja & 1)), (ja >> 1) & 1, s_abort, p.status)) {
+            if (!wait_all(bar(B_OF + 2 * g + (ja & 1)), (ja >> 1) & 1)) {
               ok = false;
               break;
             }
@@ -959,7 +1016,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (h < p.rep) {
           if (lane == 0) wml[h * 5 + 1 + quarter] = v;
           if (quarter == 0 && lane == 0) wml[h * 5] = m_run[h];
-          if (row < p.rv) wo[h * p.rv + row] = o_acc[h];
+          // D_o rows (latent dims): lane 32 q + l holds row 32 q + l (M = 128), or row 16 q + l for l < 16 (M = 64)
+          const int orow = KBV == 1 ? 16 * quarter + lane : row;
+          if ((KBV != 1 || lane < 16) && orow < p.rv) wo[h * p.rv + orow] = o_acc[h];
         }
       }
     }

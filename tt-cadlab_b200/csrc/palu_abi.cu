@@ -4,6 +4,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -35,16 +36,18 @@ int cuda_check(const char* where) {
   return PALU_OK;
 }
 
+// SM count of the current device, cached per device. Several host threads may race on the first lookup;
+// each stores the same value, and the atomics make those stores and the loads well defined.
 int device_sms() {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (cache[dev] == 0) {
-    int n = 0;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    cache[dev] = n;
+    cache[dev].store(n, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return n;
 }
 
 int rep_of(const palu_decode_dims* d) { return d->n_q_heads / d->n_kv_heads; }
@@ -114,6 +117,9 @@ size_t ws_bytes(const palu_decode_dims* d, int splits) {
 // ---- tcgen05 path: availability, split planning, tensor maps ---------------------------------------
 
 int g_kernel_choice = PALU_KERNEL_AUTO;
+// Timeout-path test hook (palu_set_wait_limit): the bound on every device wait, and the V-starve switch.
+std::atomic<unsigned long long> g_wait_ns{palu::tc::kWaitNs};
+std::atomic<int> g_starve_v{0};
 
 bool tc_supported(const palu_decode_dims* d, bool recon) {
   return recon && d->r_k <= 128 && d->r_v <= 128 && rep_of(d) <= 4;
@@ -154,17 +160,17 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// The driver's cuTensorMapEncodeTiled, looked up once. A function-local static is initialised exactly once
+// even when several host threads make their first call at the same time.
 EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
+  static const EncodeTiledFn fn = []() -> EncodeTiledFn {
     void* ptr = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  }
+      return reinterpret_cast<EncodeTiledFn>(ptr);
+    return nullptr;
+  }();
   return fn;
 }
 
@@ -191,11 +197,11 @@ void set_pages(Params& p, const palu_page_table* pg) {
   while (pg && (1 << p.blk_shift) < pg->block_size) ++p.blk_shift;
 }
 
-template <int KBK, int KBV>
+template <int KBK, int KBV, bool PAGED>
 int launch_tc(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mt, const palu::tc::TcParams& p,
               cudaStream_t stream) {
   using Lay = palu::tc::Layout<KBK, KBV>;
-  auto kern = palu::tc::palu_decode_tc_kernel<KBK, KBV>;
+  auto kern = palu::tc::palu_decode_tc_kernel<KBK, KBV, PAGED>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::TOTAL) != cudaSuccess)
     return cuda_check("cudaFuncSetAttribute(decode tc)");
   kern<<<dim3(p.ctas, p.n_kv, 1), palu::tc::kThreads, Lay::TOTAL, stream>>>(mk, mv, mt, p);
@@ -250,11 +256,20 @@ int run_tc(const void* q, const void* k, const void* v, const void* u_k, int64_t
   p.rep = rep_of(d);
   p.scale_log2 = scale * palu::kLog2e;
   set_pages(p, pg);
+  p.wait_ns = g_wait_ns.load(std::memory_order_relaxed);
+  p.starve_v = g_starve_v.load(std::memory_order_relaxed);
+  p.pdl_early = (long)splits * d->n_kv_heads <= device_sms();
   const int kbk = d->r_k > 64 ? 2 : 1, kbv = d->r_v > 64 ? 2 : 1;
-  if (kbk == 1 && kbv == 1) return launch_tc<1, 1>(mk, mv, mt, p, stream);
-  if (kbk == 1 && kbv == 2) return launch_tc<1, 2>(mk, mv, mt, p, stream);
-  if (kbk == 2 && kbv == 1) return launch_tc<2, 1>(mk, mv, mt, p, stream);
-  return launch_tc<2, 2>(mk, mv, mt, p, stream);
+  if (pg) {
+    if (kbk == 1 && kbv == 1) return launch_tc<1, 1, true>(mk, mv, mt, p, stream);
+    if (kbk == 1 && kbv == 2) return launch_tc<1, 2, true>(mk, mv, mt, p, stream);
+    if (kbk == 2 && kbv == 1) return launch_tc<2, 1, true>(mk, mv, mt, p, stream);
+    return launch_tc<2, 2, true>(mk, mv, mt, p, stream);
+  }
+  if (kbk == 1 && kbv == 1) return launch_tc<1, 1, false>(mk, mv, mt, p, stream);
+  if (kbk == 1 && kbv == 2) return launch_tc<1, 2, false>(mk, mv, mt, p, stream);
+  if (kbk == 2 && kbv == 1) return launch_tc<2, 1, false>(mk, mv, mt, p, stream);
+  return launch_tc<2, 2, false>(mk, mv, mt, p, stream);
 }
 
 template <int RV16, bool RECON, int NS>
@@ -345,6 +360,7 @@ int run_decode(bool recon, const void* q, const void* k, const void* v, const vo
     st = run_tc(q, k, v, u_k, u_k_ld, cs_pairs, cur_pos, workspace, ws_o, ws_ml, d, splits, scale, pg, stream);
     if (st) return st;
     palu::CombineTcParams c;
+    c.status = static_cast<const int*>(workspace);
     c.ws_o = ws_o;
     c.ws_ml = ws_ml;
     c.cur_pos = cur_pos;
@@ -377,6 +393,7 @@ int run_decode(bool recon, const void* q, const void* k, const void* v, const vo
   if (st) return st;
 
   palu::CombineParams c;
+  c.status = static_cast<const int*>(workspace);
   c.ws_o = ws_o;
   c.ws_ml = ws_ml;
   c.u_v = static_cast<const __nv_bfloat16*>(u_v);
@@ -502,6 +519,14 @@ int palu_set_kernel(int32_t which) {
   return PALU_OK;
 }
 
+int palu_set_wait_limit(int64_t wait_ns, int32_t starve_v) {
+  g_err.clear();
+  if (wait_ns < 0) return fail(PALU_ERR_INVALID, "wait_ns must be >= 0");
+  g_wait_ns.store(wait_ns == 0 ? palu::tc::kWaitNs : (unsigned long long)wait_ns, std::memory_order_relaxed);
+  g_starve_v.store(starve_v != 0, std::memory_order_relaxed);
+  return PALU_OK;
+}
+
 int32_t palu_kernel_for(const palu_decode_dims* dims) {
   if (!dims) return -1;
   return use_tc(dims, true) ? PALU_KERNEL_TC : PALU_KERNEL_MMA;
@@ -509,7 +534,10 @@ int32_t palu_kernel_for(const palu_decode_dims* dims) {
 
 int palu_read_status(void* workspace, int32_t* status, palu_stream_t stream) {
   g_err.clear();
-  if (!workspace || !status) return fail(PALU_ERR_INVALID, "workspace and status must be set");
+  if (!status) return fail(PALU_ERR_INVALID, "status must be set");
+  if (!workspace) {  // the static scratch of palu_decode_attn_static on the current device
+    if (int st = static_scratch(&workspace)) return st;
+  }
   if (cudaMemcpyAsync(status, workspace, sizeof(int32_t), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
       cudaStreamSynchronize(stream) != cudaSuccess)
     return cuda_check("reading the status word");
@@ -533,7 +561,9 @@ int palu_decode_attn_static(const void* q, const void* k_lat, const void* v_lat,
   g_err.clear();
   int st = validate(dims, true, u_v != nullptr);
   if (st) return st;
-  const size_t need = use_tc(dims, true) ? ws_tc_bytes(dims, choose_splits_tc(dims)) : ws_bytes(dims, choose_splits(dims));
+  // The same bound for every kernel family, so whether a shape is accepted does not depend on
+  // palu_set_kernel: what palu_workspace_bytes() reports must fit.
+  const size_t need = palu_workspace_bytes(dims);
   if (need > kStaticScratchBytes)
     return fail(PALU_ERR_WORKSPACE, "palu_decode_attn_static: these shapes need %zu bytes of scratch, more than the "
                 "%zu-byte static scratch; use palu_decode_attn with a caller workspace", need, kStaticScratchBytes);

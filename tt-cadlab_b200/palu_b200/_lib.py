@@ -22,6 +22,7 @@ EXPORTED = ("palu_decode_attn", "palu_decode_attn_static", "palu_decode_attn_pag
             "palu_rope_q_append", "palu_add_rms_norm", "palu_swiglu",
             "palu_workspace_bytes", "palu_choose_splits", "palu_append_latents",
             "palu_plain_gqa_decode", "palu_pack_cs_table", "palu_set_kernel", "palu_kernel_for", "palu_read_status",
+            "palu_set_wait_limit",
             "palu_last_error", "palu_version")
 PALU_KERNEL_AUTO, PALU_KERNEL_MMA, PALU_KERNEL_TC = 0, 1, 2
 
@@ -77,6 +78,8 @@ def load() -> ctypes.CDLL:
     lib.palu_pack_cs_table.restype = ctypes.c_int
     lib.palu_set_kernel.argtypes = [i32]
     lib.palu_set_kernel.restype = ctypes.c_int
+    lib.palu_set_wait_limit.argtypes = [i64, i32]
+    lib.palu_set_wait_limit.restype = ctypes.c_int
     lib.palu_kernel_for.argtypes = [dims_p]
     lib.palu_kernel_for.restype = i32
     lib.palu_read_status.argtypes = [vp, ctypes.POINTER(i32), vp]
@@ -142,14 +145,24 @@ def set_kernel(which: int) -> None:
     check(load().palu_set_kernel(int(which)))
 
 
+def set_wait_limit(wait_ns: int = 0, starve_v: bool = False) -> None:
+    """Test hook of the timeout path (palu_set_wait_limit): bound device waits at ``wait_ns`` (0 = the
+    default 1 s) and, with ``starve_v``, make a V producer skip its loads so that a wait runs out."""
+    check(load().palu_set_wait_limit(int(wait_ns), int(bool(starve_v))))
+
+
 def kernel_for(d: DecodeDims) -> int:
     return int(load().palu_kernel_for(ctypes.byref(d)))
 
 
-def read_status(workspace: torch.Tensor) -> int:
-    """The status word a decode call left in ``workspace`` (0 = ok); reading clears it."""
+def read_status(workspace) -> int:
+    """The status word a decode call left in ``workspace`` (0 = ok); reading clears it. ``None`` reads the
+    static scratch of palu_decode_attn_static on the current device."""
     st = ctypes.c_int32(0)
-    check(load().palu_read_status(workspace.data_ptr(), ctypes.byref(st), stream_handle(workspace.device)))
+    if workspace is None:
+        check(load().palu_read_status(None, ctypes.byref(st), stream_handle(torch.device("cuda"))))
+    else:
+        check(load().palu_read_status(workspace.data_ptr(), ctypes.byref(st), stream_handle(workspace.device)))
     return int(st.value)
 
 
