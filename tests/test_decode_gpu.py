@@ -342,3 +342,19 @@ def test_rope_q_append_matches_tensor_ops(cuda, qkv_dtype, paged):
     assert torch.equal(q, want_q)
     assert torch.equal(kf, kt) and torch.equal(vf, vt)
     assert not torch.equal(kf, k0)  # something was appended
+
+
+def test_packed_table_cache_never_returns_a_dead_tables_values(cuda):
+    """The packed RoPE table is cached per live table tensor: a new table of the same shape (which the
+    allocator may place at a freed table's address) is packed afresh, never served the old values."""
+    from palu_b200 import fused
+    S = 1024
+    outs = []
+    for scaling in (LLAMA3, None, LLAMA3):
+        cos, sin = oracle.cos_sin_tables(128, S, THETA, scaling)
+        cs = fused.cs_table(cos[:S], sin[:S], S).to(cuda, torch.bfloat16)
+        outs.append(fused.pack_cs_table(cs).clone())
+        del cs
+    torch.cuda.synchronize()
+    assert not torch.equal(outs[0], outs[1]), "a no-scaling table was served the llama3 table's packing"
+    assert torch.equal(outs[0], outs[2])

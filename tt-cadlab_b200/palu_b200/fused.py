@@ -19,6 +19,8 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
+import weakref
 from typing import Optional
 
 import torch
@@ -109,30 +111,33 @@ def rot_step_table(cos: torch.Tensor, sin: torch.Tensor, chunk: int) -> torch.Te
 # Device-side table packing (cached per cs_tab tensor)
 # ----------------------------------------------------------------------------------------------
 
+# id(cs_tab) -> (weak reference to cs_tab, its version counter, packed table). Keyed by the table tensor
+# object, not its address: a freed table's memory can be reused by a new table of the same shape, and an
+# address-keyed entry would then hand back the old table's values.
 _PACK_CACHE: dict = {}
 
 
 def pack_cs_table(cs_tab: torch.Tensor) -> torch.Tensor:
     """[.., S, 256] [cos | sin] (bf16 or fp32, CUDA) -> [S, 64] int32 rows of packed fp16 (per row 4 blocks
-    of 16 frequencies: 16 cosines, then the same frequencies' sines),
-    computed by the library's pack kernel and cached while the table tensor is unchanged."""
+    of 16 frequencies: 16 cosines, then the same frequencies' sines), computed by the library's pack kernel
+    and cached while the same table tensor is alive and unchanged (in-place writes bump its version)."""
     _lib.require_cuda(cs_tab)
+    hit = _PACK_CACHE.get(id(cs_tab))
+    if hit is not None and hit[0]() is cs_tab and hit[1] == cs_tab._version:
+        return hit[2]
     t = cs_tab.reshape(-1, cs_tab.shape[-1])
     if t.stride(-1) != 1:
         t = t.contiguous()
-    key = (t.data_ptr(), tuple(t.shape), t.dtype, cs_tab._version, t.device.index)
-    hit = _PACK_CACHE.get(key)
-    if hit is not None:
-        return hit
     if t.dtype not in (torch.bfloat16, torch.float32):
         t = t.float()
     out = torch.empty(t.shape[0], 64, dtype=torch.int32, device=t.device)
     dt = _lib.PALU_F32 if t.dtype == torch.float32 else _lib.PALU_BF16
     _lib.check(_lib.load().palu_pack_cs_table(t.data_ptr(), t.stride(0), dt, out.data_ptr(), t.shape[0],
                                               _lib.stream_handle(t.device)))
-    if len(_PACK_CACHE) > 256:  # one entry per distinct table (a model holds one per layer)
-        _PACK_CACHE.clear()
-    _PACK_CACHE[key] = out
+    if len(_PACK_CACHE) > 256:  # one entry per live table (a model holds one per layer): drop the dead ones
+        for k in [k for k, v in _PACK_CACHE.items() if v[0]() is None]:
+            del _PACK_CACHE[k]
+    _PACK_CACHE[id(cs_tab)] = (weakref.ref(cs_tab), cs_tab._version, out)
     return out
 
 
@@ -161,10 +166,11 @@ def _grid_cores(program_config) -> Optional[int]:
 _WS_CACHE: dict = {}
 
 
-def _workspace_for(d, device) -> torch.Tensor:
+def _workspace_for(d, device, need=None) -> torch.Tensor:
     """A zeroed workspace, cached per (device, size) so that repeated calls reuse it; calls that overlap on
     different streams must pass their own ``workspace``."""
-    need = _lib.workspace_bytes(d)
+    if need is None:
+        need = _lib.workspace_bytes(d)
     key = (device.index if device.index is not None else torch.cuda.current_device(), need)
     ws = _WS_CACHE.get(key)
     if ws is None:
@@ -183,8 +189,20 @@ def workspace_status() -> int:
     return st
 
 
+def _check_status(workspace, what: str) -> None:
+    """Wait for the call and raise if one of its bounded device waits expired (its output is then NaN)."""
+    st = _lib.read_status(workspace)
+    if st != 0:
+        raise RuntimeError(f"{what}: a bounded device wait expired (status {st}); the output is invalid")
+
+
+def _check_by_default() -> bool:
+    return os.environ.get("PALU_CHECK_STATUS", "") not in ("", "0")
+
+
 def decode(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, *, u_k_ld=HEAD_DIM, u_v=None, scale=None,
-           out=None, out_dtype=torch.bfloat16, splits=0, workspace=None, page_table=None) -> torch.Tensor:
+           out=None, out_dtype=torch.bfloat16, splits=0, workspace=None, page_table=None,
+           check_status=None, _checked=False) -> torch.Tensor:
     """Low-level entry (no reference-surface validation): the arrays are already in the library's layout.
 
     q [B, nh, 128] bf16; k_latent [B, n_groups, S, r_k]; v_latent [B, n_groups, S, r_v]; u_k rows of
@@ -192,8 +210,11 @@ def decode(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, *, u_k_ld=HEAD_DIM, u_
     cur_pos [B] int32; u_v [n_kv, r_v, 128] or None. Returns [B, nh, r_v or 128].
     Paged caches: ``page_table`` [B, blocks per row] int32 and k_latent [n_blocks, n_groups, block_size,
     r_k], v_latent [n_blocks, n_groups, block_size, r_v]; a row then holds blocks per row x block_size
-    positions (palu_decode_attn_paged)."""
-    _lib.require_cuda(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, u_v, page_table)
+    positions (palu_decode_attn_paged).
+    ``check_status`` (default: the PALU_CHECK_STATUS environment variable) waits for the call and raises
+    RuntimeError if a bounded device wait expired, as the reference op raises on a failed run."""
+    if not _checked:
+        _lib.require_cuda(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, u_v, page_table)
     B, nh = q.shape[0], q.shape[1]
     n_groups, S, r_k = k_latent.shape[1], k_latent.shape[2], k_latent.shape[3]
     r_v = v_latent.shape[3]
@@ -204,8 +225,9 @@ def decode(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, *, u_k_ld=HEAD_DIM, u_
     width = HEAD_DIM if u_v is not None else r_v
     if out is None:
         out = torch.empty(B, nh, width, dtype=out_dtype, device=q.device)
-    if workspace is None or workspace.numel() < _lib.workspace_bytes(d):
-        workspace = _workspace_for(d, q.device)
+    need = _lib.workspace_bytes(d)
+    if workspace is None or workspace.numel() < need:
+        workspace = _workspace_for(d, q.device, need)
     odt = _lib.PALU_F32 if out.dtype == torch.float32 else _lib.PALU_BF16
     sc = HEAD_DIM ** -0.5 if scale is None else float(scale)
     if page_table is None:
@@ -219,13 +241,15 @@ def decode(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, *, u_k_ld=HEAD_DIM, u_
             q.data_ptr(), k_latent.data_ptr(), v_latent.data_ptr(), u_k.data_ptr(), int(u_k_ld), _lib.ptr(u_v),
             cs_pairs.data_ptr(), cur_pos.data_ptr(), ctypes.byref(pg), out.data_ptr(), odt, workspace.data_ptr(),
             workspace.numel(), ctypes.byref(d), sc, _lib.stream_handle(q.device)))
+    if check_status if check_status is not None else _check_by_default():
+        _check_status(workspace, "palu_sdpa_decode")
     return out
 
 
 def palu_sdpa_decode(q, k_latent, w_rot, cs_tab, v_latent, head_dim_v, cur_pos_tensor, *, rot_step=None,
                      trans_mat=None, u_v=None, scale=None, heads_per_core=None, rot_mode="dst", table_mcast=True,
                      program_config=None, compute_kernel_config=None, memory_config=None,
-                     out_dtype=torch.bfloat16, splits=0, page_table_tensor=None) -> torch.Tensor:
+                     out_dtype=torch.bfloat16, splits=0, page_table_tensor=None, check_status=None) -> torch.Tensor:
     """B200 implementation of ``ttnn.transformer.palu_sdpa_decode`` (same positional / keyword surface).
 
     q [1, B, nh, 128] (rotated), k_latent [B, n_groups, S, r_k], w_rot [1, n_kv, r_k, 256],
@@ -236,7 +260,8 @@ def palu_sdpa_decode(q, k_latent, w_rot, cs_tab, v_latent, head_dim_v, cur_pos_t
     ``page_table_tensor`` [B, blocks per row] int32 (the stock paged decode op's keyword; the paged
     variant the reference plans, HANDOFF.md:126-127): the caches are then paged, k_latent
     [n_blocks, n_groups, block_size, r_k] and v_latent [n_blocks, n_groups, block_size, r_v], and
-    S = blocks per row x block_size."""
+    S = blocks per row x block_size. ``check_status`` True (or PALU_CHECK_STATUS=1 in the environment)
+    waits for the call and raises RuntimeError when a bounded device wait expired."""
     if rot_mode not in ROT_MODES:
         raise RuntimeError(f"rot_mode must be one of {ROT_MODES}, got {rot_mode!r}")
     if (rot_step is None) != (trans_mat is None):
@@ -307,7 +332,8 @@ def palu_sdpa_decode(q, k_latent, w_rot, cs_tab, v_latent, head_dim_v, cur_pos_t
     pt = None if page_table_tensor is None else page_table_tensor.to(torch.int32).contiguous()
     out = decode(_bf16(q[0]), k_latent.contiguous(), v_latent.contiguous(), wb, pack_cs_table(cs_tab), pos,
                  u_k_ld=wb.shape[-1], u_v=_bf16(u_v.reshape(n_kv, r_v, HEAD_DIM)) if u_v is not None else None,
-                 scale=scale, out_dtype=out_dtype, splits=splits, page_table=pt)
+                 scale=scale, out_dtype=out_dtype, splits=splits, page_table=pt, check_status=check_status,
+                 _checked=True)
     return out.unsqueeze(0)
 
 
