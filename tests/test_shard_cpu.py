@@ -76,12 +76,14 @@ def _rank_main(rank, world, port, grouped, out_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("grouped", [False, True], ids=["mlrd", "glrd"])
-def test_two_rank_sharded_layer_equals_unsharded(grouped):
+@pytest.mark.parametrize("grouped,world", [(False, 2), (True, 2), (True, 4)], ids=["mlrd", "glrd", "glrd_split4"])
+def test_sharded_layer_equals_unsharded(grouped, world):
+    """2 ranks: heads and whole latent groups split; 4 ranks with 2 groups: each group's heads split over
+    two ranks, each holding the whole group latent."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, grouped, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, grouped, q)) for r in range(world)]
     for p in procs:
         p.start()
     got = q.get(timeout=90)
@@ -99,5 +101,13 @@ def test_shard_ranges_cover_every_head_once():
         shards = [KVShard(r, world, 8, 32, 8) for r in range(world)]
         assert sorted(h for s in shards for h in s.kv) == list(range(8))
         assert sorted(h for s in shards for h in s.q) == list(range(32))
+    # 2 G-LRD groups over 4 or 8 ranks: each group's heads split, its latent replicated on those ranks
+    for world in (4, 8):
+        shards = [KVShard(r, world, 8, 32, 2) for r in range(world)]
+        assert sorted(h for s in shards for h in s.kv) == list(range(8))
+        for s in shards:
+            assert list(s.groups) == [s.kv.start // 4] and s.kv.stop - 1 < 4 * (s.kv.start // 4 + 1)
+            assert s.latent_replicas == world // 2
+    assert KVShard(0, 2, 8, 32, 2).latent_replicas == 1
     with pytest.raises(ValueError, match="do not shard"):
-        KVShard(0, 4, 8, 32, 2)  # 2 G-LRD groups over 4 ranks
+        KVShard(0, 3, 6, 24, 2)  # neither 2 groups nor 3 ranks divides the other

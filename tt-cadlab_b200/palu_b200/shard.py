@@ -20,8 +20,14 @@ HEAD_DIM = 128
 
 @dataclass(frozen=True)
 class KVShard:
-    """The heads rank ``rank`` of ``world`` owns. Latent groups shard whole: a G-LRD layer with
-    ``n_groups`` groups runs on ``world`` ranks only if ``n_groups % world == 0``."""
+    """The heads rank ``rank`` of ``world`` owns: ``n_kv / world`` consecutive KV heads, their query heads
+    and the latent groups those heads read.
+
+    Latent groups shard whole when ``n_groups % world == 0``. With more ranks than groups (a G-LRD layer of
+    2 groups on 4 or 8 GPUs), a group's KV heads are split over ``world / n_groups`` ranks and each of them
+    holds the whole group latent: its latent projection and cache are replicated, so the latent bytes each
+    GPU reads stop shrinking past ``world == n_groups`` (the cap of head sharding for grouped latents; a
+    sequence split with an exchange of partial softmax states would lift it)."""
     rank: int
     world: int
     n_kv: int
@@ -33,8 +39,11 @@ class KVShard:
             raise ValueError(f"rank {self.rank} outside world {self.world}")
         if self.n_q % self.n_kv or self.n_kv % self.n_groups:
             raise ValueError(f"heads do not nest: n_q {self.n_q}, n_kv {self.n_kv}, n_groups {self.n_groups}")
-        if self.n_groups % self.world:
-            raise ValueError(f"{self.n_groups} latent groups do not shard over {self.world} ranks")
+        if self.n_kv % self.world:
+            raise ValueError(f"{self.n_kv} KV heads do not shard over {self.world} ranks")
+        if self.n_groups % self.world and self.world % self.n_groups:
+            raise ValueError(f"{self.n_groups} latent groups do not shard over {self.world} ranks (neither "
+                             "divides the other)")
 
     @property
     def kv(self) -> range:
@@ -48,8 +57,15 @@ class KVShard:
 
     @property
     def groups(self) -> range:
-        per = self.n_groups // self.world
-        return range(self.rank * per, (self.rank + 1) * per)
+        """The latent groups this rank's KV heads read (whole groups, or the one group its heads belong to
+        when a group is split over ranks)."""
+        gs = self.n_kv // self.n_groups
+        return range(self.kv.start // gs, (self.kv.stop - 1) // gs + 1)
+
+    @property
+    def latent_replicas(self) -> int:
+        """How many ranks hold a copy of each latent group: 1 when groups shard whole."""
+        return max(1, self.world // self.n_groups)
 
 
 def shard_layer_inputs(shard: KVShard, q, k_lat, v_lat, u_k, wo_fused, u_v=None) -> dict:
