@@ -220,9 +220,15 @@ class PaluRefAttention:
     K = lat_k @ U_kᵀ and V = lat_v @ U_vᵀ rebuilt over the whole cache, HF rotate-half RoPE,
     GQA, causal mask ``tril(start_pos)``, softmax, ``@ woᵀ``.
 
-    ``lowrank`` is any object with ``k_VT [nkv, r_k, dim]``, ``k_U [nkv, hd, r_k]``, ``v_VT``, ``v_U``."""
+    ``lowrank`` is any object with ``k_VT [nkv, r_k, dim]``, ``k_U [nkv, hd, r_k]``, ``v_VT``, ``v_U``.
 
-    def __init__(self, hf_cfg: dict, w: dict, lowrank):
+    ``device_rounding`` (off by default, which is the reference as written) applies the roundings of the
+    values the device path stores, so that a comparison measures the kernels rather than those roundings:
+    the latent caches in bf16 (the caches are bf16, attention.py:159-169) and, for a one-token decode step,
+    q rounded to bf16 after RoPE (the op's q input) and K rotated with the bf16 [cos | sin] table the op
+    reads (attention.py:52-78)."""
+
+    def __init__(self, hf_cfg: dict, w: dict, lowrank, device_rounding: bool = False):
         from transformers import LlamaConfig
         from transformers.models.llama.modeling_llama import LlamaRotaryEmbedding
         self.cfg = LlamaConfig(**{k: v for k, v in hf_cfg.items() if k != "architectures"})
@@ -234,6 +240,7 @@ class PaluRefAttention:
         self.rotary = LlamaRotaryEmbedding(config=self.cfg)
         self.cache_k_lat = None
         self.cache_v_lat = None
+        self.device_rounding = device_rounding
 
     @torch.no_grad()
     def forward(self, x: torch.Tensor, start_pos: int) -> torch.Tensor:
@@ -242,6 +249,9 @@ class PaluRefAttention:
         q = (x @ self.wq.T).view(B, S, self.nh, self.hd).transpose(1, 2)
         k_lat = torch.einsum("bsd,hrd->bhsr", x, self.lr.k_VT.float())
         v_lat = torch.einsum("bsd,hrd->bhsr", x, self.lr.v_VT.float())
+        rnd = lambda t: t.to(torch.bfloat16).float() if self.device_rounding else t
+        k_lat, v_lat = rnd(k_lat), rnd(v_lat)
+        decode = self.device_rounding and S == 1
         if self.cache_k_lat is None or start_pos == 0:
             self.cache_k_lat, self.cache_v_lat = k_lat, v_lat
         else:
@@ -255,7 +265,11 @@ class PaluRefAttention:
         pos_k = torch.arange(0, T)[None].expand(B, -1)
         cos_q, sin_q = self.rotary(x, pos_q)
         cos_k, sin_k = self.rotary(x, pos_k)
+        if decode:
+            cos_k, sin_k = rnd(cos_k), rnd(sin_k)
         q, _ = apply_rotary_pos_emb(q, q, cos_q, sin_q)
+        if decode:
+            q = rnd(q)
         _, K = apply_rotary_pos_emb(K, K, cos_k, sin_k)
         rep = self.nh // self.nkv
         K = K.repeat_interleave(rep, dim=1)

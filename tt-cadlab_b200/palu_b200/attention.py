@@ -247,8 +247,9 @@ class PaluAttention:
                         page_table: Optional[torch.Tensor] = None, chunk_page_table=None, chunk_start_idx=None,
                         kv_cache=None) -> torch.Tensor:
         """The reference's ``forward_prefill(x_11SH, rot_mats, user_id=0, page_table=None, ...)``
-        (attention.py:382). Prompt of P tokens at positions 0..P-1: x [B, P, dim] (cache rows 0..B-1), or
-        [1, 1, P, dim] for cache row ``user_id`` (the reference's per-user prefill). ``rot_mats`` is accepted
+        (attention.py:382). Prompt of P tokens at positions 0..P-1: x [B, P, dim] (cache rows user_id ..
+        user_id + B - 1, so a long batch can be prefilled a few rows at a time), or [1, 1, P, dim] for cache
+        row ``user_id`` (the reference's per-user prefill). ``rot_mats`` is accepted
         and not used (the layer rotates from its own tables); chunked prefill (``chunk_page_table``,
         ``chunk_start_idx``) and an external ``kv_cache`` are not supported. Writes the prompt's latents into
         the caches and returns its causal attention output (fp32, x's layout) computed with torch SDPA on K
@@ -259,7 +260,7 @@ class PaluAttention:
         shape4 = x.dim() == 4
         xb = (x.reshape(1, x.shape[-2], x.shape[-1]) if shape4 else x).to(self.device, torch.float32)
         B, P, _ = xb.shape
-        rows = slice(user_id, user_id + 1) if shape4 else slice(0, B)
+        rows = slice(user_id, user_id + B)
         if P > self.max_seq or rows.stop > self.max_batch:
             raise RuntimeError(f"prompt of {P} tokens / cache rows {rows} exceed the cache")
         xp = xb.to(self.proj_dtype)

@@ -42,13 +42,31 @@ class DecoderConfig:
     head_dim: int = 128
 
 
-def mixed_ranks(n_layers: int, seed: int, choices: Sequence[int] = (32, 48, 64, 96, 128)) -> List[Tuple[int, int]]:
-    """Per-layer (r_k, r_v), drawn from ``choices`` with ``seed``: the mixed-rank decoder config. The
-    reference pads a layer's per-head ranks to the layer maximum (convert.py:148-199), so one rank pair
-    per layer describes it."""
+RANK_CHOICES = (32, 48, 64, 96, 128)
+
+
+def mixed_ranks(n_layers: int, seed: int, choices: Sequence[int] = RANK_CHOICES) -> List[Tuple[int, int]]:
+    """Per-layer (r_k, r_v), drawn from ``choices`` with ``seed``: every KV head of a layer gets the same
+    ranks (a lighter variant of the mixed-rank config, for tests)."""
     g = torch.Generator().manual_seed(seed)
     pick = lambda: int(choices[int(torch.randint(len(choices), (1,), generator=g))])
     return [(pick(), pick()) for _ in range(n_layers)]
+
+
+def mixed_head_ranks(n_layers: int, n_kv_heads: int, seed: int,
+                     choices: Sequence[int] = RANK_CHOICES) -> List[Tuple[List[int], List[int]]]:
+    """The mixed-rank decoder config as BASELINE states it: ranks drawn from ``choices`` per layer AND per
+    KV head, K and V separately -> per layer (K ranks per head, V ranks per head)."""
+    g = torch.Generator().manual_seed(seed)
+    pick = lambda: [int(choices[int(i)]) for i in torch.randint(len(choices), (n_kv_heads,), generator=g)]
+    return [(pick(), pick()) for _ in range(n_layers)]
+
+
+def padded_rank(head_ranks: Sequence[int], multiple: int = 32) -> int:
+    """A layer's cache width: the largest per-head rank rounded up to ``multiple`` (load_palu_dir's padding,
+    convert.py:148-199; the padded rows and columns of the factors are zero)."""
+    r = max(head_ranks)
+    return -(-r // multiple) * multiple
 
 
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
@@ -59,7 +77,9 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 class PaluDecoder:
     """Decoder of ``cfg.n_layers`` layers with Palu attention, random weights from ``seed``.
 
-    ``ranks``: per-layer (r_k, r_v) (``mixed_ranks``); ``world`` / ``rank``: tensor-parallel ranks (the
+    ``ranks``: per layer either (r_k, r_v) for every KV head (``mixed_ranks``) or per-head rank lists
+    (K ranks, V ranks) (``mixed_head_ranks``), zero-padded per layer to ``padded_rank`` as the reference's
+    loader pads them; ``world`` / ``rank``: tensor-parallel ranks (the
     default process group, when world > 1). Caches hold ``max_batch`` rows of ``max_seq`` positions.
     ``proj_dtype``: dtype of every weight matrix (bf16 for the full model; fp32 for exact comparisons).
     ``keep_source`` keeps each layer's checkpoint-layout weights (wq, wo, LowRank, full w1 / w3 / w2) in
@@ -89,13 +109,27 @@ class PaluDecoder:
         self.embed = randn(cfg.vocab, D, scale=1.0)
         self.layers = []
         f_lo, f_hi = rank * cfg.ffn_dim // world, (rank + 1) * cfg.ffn_dim // world
-        for (r_k, r_v) in ranks:
+        for (rk_spec, rv_spec) in ranks:
             wq = randn(cfg.n_heads * hd, D, scale=D ** -0.5)          # q_proj weight [n_heads * hd, dim]
             wo = randn(D, cfg.n_heads * hd, scale=(cfg.n_heads * hd) ** -0.5)  # o_proj weight [dim, n_heads * hd]
-            lr = LowRank(k_VT=randn(cfg.n_kv_heads, r_k, D, scale=D ** -0.5).float(),
-                         k_U=randn(cfg.n_kv_heads, hd, r_k, scale=r_k ** -0.5).float(),
-                         v_VT=randn(cfg.n_kv_heads, r_v, D, scale=D ** -0.5).float(),
-                         v_U=randn(cfg.n_kv_heads, hd, r_v, scale=r_v ** -0.5).float())
+            heads_k = [int(rk_spec)] * cfg.n_kv_heads if isinstance(rk_spec, int) else [int(r) for r in rk_spec]
+            heads_v = [int(rv_spec)] * cfg.n_kv_heads if isinstance(rv_spec, int) else [int(r) for r in rv_spec]
+            r_k = rk_spec if isinstance(rk_spec, int) else padded_rank(heads_k)
+            r_v = rv_spec if isinstance(rv_spec, int) else padded_rank(heads_v)
+
+            def factors(head_ranks, r_pad):
+                # per head: VT rows and U columns beyond the head's rank are zero (the loader's padding)
+                VT = randn(cfg.n_kv_heads, r_pad, D, scale=D ** -0.5).float()
+                U = randn(cfg.n_kv_heads, hd, r_pad, scale=1.0).float()
+                for h, r in enumerate(head_ranks):
+                    VT[h, r:] = 0
+                    U[h, :, r:] = 0
+                    U[h, :, :r] *= r ** -0.5
+                return VT, U
+
+            k_VT, k_U = factors(heads_k, r_k)
+            v_VT, v_U = factors(heads_v, r_v)
+            lr = LowRank(k_VT=k_VT, k_U=k_U, v_VT=v_VT, v_U=v_U)
             shard = KVShard(rank, world, cfg.n_kv_heads, cfg.n_heads, cfg.n_kv_heads) if world > 1 else None
             attn = PaluAttention(wq, wo, lr, cfg.n_heads, cfg.n_kv_heads, max_batch=max_batch,
                                  max_seq=max_seq, head_dim=hd, rope_theta=cfg.rope_theta,
@@ -173,14 +207,16 @@ class PaluDecoder:
 
     # ---- prefill --------------------------------------------------------------------------------------
     @torch.no_grad()
-    def prefill_logits(self, tokens: torch.Tensor, page_table: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """Prompt tokens [B, P] at positions 0..P-1 (cache rows 0..B-1): fills every layer's caches and
-        returns the logits of the last prompt position [B, vocab] fp32 (generate.py:28-37)."""
+    def prefill_logits(self, tokens: torch.Tensor, page_table: Optional[torch.Tensor] = None,
+                       row0: int = 0) -> torch.Tensor:
+        """Prompt tokens [B, P] at positions 0..P-1 (cache rows row0 .. row0 + B - 1): fills every layer's
+        caches and returns the logits of the last prompt position [B, vocab] fp32 (generate.py:28-37)."""
         tokens = tokens.to(self.device)
         B, P = tokens.shape
         h = self.embed[tokens].float()                                   # [B, P, dim]
         for L in self.layers:
-            h = h + L["attn"].forward_prefill(rms_norm(h, L["attn_norm"], self.cfg.norm_eps), page_table=page_table)
+            h = h + L["attn"].forward_prefill(rms_norm(h, L["attn_norm"], self.cfg.norm_eps), None, row0,
+                                              page_table=page_table)
             h = h + self._mlp(L, rms_norm(h, L["ffn_norm"], self.cfg.norm_eps).reshape(B * P, -1)).view(B, P, -1)
         return self._logits(h[:, -1])
 
