@@ -108,10 +108,11 @@ def test_mlrd_matches_oracle(cuda, kernel, r_k, r_v, B, S):
     assert_close(out32, ref, "fp32 out")
 
 
-@pytest.mark.parametrize("r_k,r_v,n_groups", [(256, 256, 2), (160, 224, 8), (64, 256, 8)])
-def test_wide_latents_match_oracle(cuda, r_k, r_v, n_groups):
+@pytest.mark.parametrize("r_k,r_v,n_groups", [(256, 256, 2), (160, 224, 8), (64, 256, 8), (256, 48, 8)])
+def test_wide_latents_match_oracle(cuda, kernel, r_k, r_v, n_groups):
     """Latents wider than 128 (BASELINE's G-LRD config: 2 groups of 4 KV heads, rank 256, V rebuilt per
-    head), at a reduced batch and context. They run on the mma.sync kernel with one pipeline stage."""
+    head), at a reduced batch and context: on the tcgen05 kernel with one pipeline per CTA (four 64-wide
+    boxes per K and V tile, V^T as two M = 128 blocks), and on the mma.sync kernel with one stage."""
     g = torch.Generator().manual_seed(r_k + r_v + n_groups)
     B, S = 3, 1500
     q, k_lat, u_k, v_lat, u_v, pos, cos, sin = _inputs(g, B, 8, 32, S, r_k, r_v, n_groups=n_groups,
@@ -122,6 +123,23 @@ def test_wide_latents_match_oracle(cuda, r_k, r_v, n_groups):
     out = _run_fused(cuda, q, k_lat, u_k, v_lat, pos, cos, sin, 128 ** -0.5, u_v=u_v, out_dtype=torch.float32)
     assert out.shape == ref.shape
     assert_close(out, ref, f"r_k={r_k} r_v={r_v} groups={n_groups}")
+
+
+@pytest.mark.parametrize("splits", [1, 5, 64])
+def test_wide_latents_split_counts(cuda, splits):
+    """The one-pipeline tcgen05 kernel (rank-256 grouped latents) under several CTA counts per KV head:
+    ranges that cut rows, ranges of a single tile, and rows whose tiles all sit in one CTA."""
+    from palu_b200 import _lib
+    d = _lib.dims(2, 32, 8, 2, 256, 256, 2000)
+    assert _lib.kernel_for(d) == _lib.PALU_KERNEL_TC
+    g = torch.Generator().manual_seed(31)
+    q, k_lat, u_k, v_lat, u_v, pos, cos, sin = _inputs(g, 2, 8, 32, 2000, 256, 256, n_groups=2, uv=True)
+    pos[0] = 1999
+    ref = oracle.reference_decode(q, oracle.expand_groups(k_lat, 4), u_k, oracle.expand_groups(v_lat, 4), pos,
+                                  cos, sin, 128 ** -0.5, u_v=u_v)
+    out = _run_fused(cuda, q, k_lat, u_k, v_lat, pos, cos, sin, 128 ** -0.5, u_v=u_v, out_dtype=torch.float32,
+                     splits=splits)
+    assert_close(out, ref, f"wide, splits={splits}")
 
 
 def test_full_context_rows_are_checked_per_row(cuda, kernel):

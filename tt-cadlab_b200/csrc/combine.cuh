@@ -106,6 +106,7 @@ struct CombineTcParams {
   void* out;                 // [B][n_q][r_out]
   int out_f32;
   int batch, n_q, n_kv, rep, ctas, r_lat, r_out, max_seq;
+  int npipe;                 // pipelines per decode CTA (1 or 2): records g < npipe of each pair are written
 };
 constexpr int kMaxTcRecords = 2 * kMaxSplits;
 
@@ -133,12 +134,12 @@ __global__ void __launch_bounds__(kCombineThreads) palu_combine_tc_kernel(const 
       if (nb > 0 && T > 0) {
         const int cf = (int)(((sb + 1) * p.ctas - 1) / T), cl = (int)(((sb + nb) * p.ctas - 1) / T);
         if (cf == cl) {
-          for (int g = 0; g < 2; ++g) s_rec[cnt++] = (int)tc_rec_direct(b, kvh, p.n_kv, g);
+          for (int g = 0; g < p.npipe; ++g) s_rec[cnt++] = (int)tc_rec_direct(b, kvh, p.n_kv, g);
         } else {
-          for (int g = 0; g < 2; ++g) s_rec[cnt++] = (int)tc_rec_edge(p.batch, p.n_kv, p.ctas, kvh, cf, 1, g);
+          for (int g = 0; g < p.npipe; ++g) s_rec[cnt++] = (int)tc_rec_edge(p.batch, p.n_kv, p.ctas, kvh, cf, 1, g);
           for (int c = cf + 1; c <= cl && cnt + 2 <= kMaxTcRecords; ++c) {
             if ((long long)c * T / p.ctas == (long long)(c + 1) * T / p.ctas) continue;  // empty range: no records
-            for (int g = 0; g < 2; ++g) s_rec[cnt++] = (int)tc_rec_edge(p.batch, p.n_kv, p.ctas, kvh, c, 0, g);
+            for (int g = 0; g < p.npipe; ++g) s_rec[cnt++] = (int)tc_rec_edge(p.batch, p.n_kv, p.ctas, kvh, c, 0, g);
           }
         }
       }

@@ -32,6 +32,10 @@
 // runs two phases ahead of a waiter. Every wait is bounded (1 s of globaltimer by default): on expiry the CTA records a
 // status code, all roles stop (the multi-lane warps agree on it, so none is left divergent), copies and
 // MMAs in flight are drained, and TMEM is freed.
+// Latents wider than 128 (up to 256: the grouped G-LRD caches) run the same roles with ONE pipeline per CTA
+// (NP = 1; group 1's warps only help stage U_k): U_k alone is then 64 KB and a K or V tile 64 KB, so a single
+// K and V stage per CTA is what fits in shared memory; V^T is then two M = 128 blocks (latent dims 0..127 and
+// 128..255) whose PV results sit in TMEM columns 256..319, the columns group 1 would have used.
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -54,7 +58,9 @@ constexpr int kGrpCols = 256;           // TMEM columns reserved per softmax gro
 constexpr int kColDk = 0;               // 128 columns: f32 K tile, two halves of [even | odd] dims (reconstruct output)
 constexpr int kColA = 128;              // 64 columns: fp16 K_rot, the A operand of QK (packed 2 per column)
 constexpr int kColDs = 192;             // 2 x 16 columns: scores, double-buffered
-constexpr int kColDo = 224;             // 2 x 16 columns: PV result, double-buffered
+constexpr int kColDo = 224;             // 2 x 16 columns: PV result, double-buffered (two pipelines)
+constexpr int kColDoWide = 256;         // one pipeline: 2 buffers x 2 M-blocks x 16 columns at 256..319
+constexpr int kColDk2 = 320;            // one pipeline: the second D_k buffer (128 columns)
 constexpr unsigned long long kWaitNs = 1000000000ull;  // bound on any single wait
 
 enum : int { kStatusOk = 0, kStatusTimeout = 1 };
@@ -111,14 +117,18 @@ PALU_DEVINL RowSeg seg_next(const TcParams& p, int n, const RowSeg& s) {
   r.cnt = min(nb, n - r.kb);
   return r;
 }
-// Group g takes the CTA-local tiles k with k % 2 == g: its first tile in segment s and their count.
-PALU_DEVINL int seg_group_first(const RowSeg& s, int g) { return s.kb + ((g - s.kb) & 1); }
+// With np pipelines (groups) per CTA (1 or 2), group g takes the CTA-local tiles k with k % np == g: its first
+// tile in segment s and their count.
+template <int NP>
+PALU_DEVINL int seg_group_first(const RowSeg& s, int g) { return s.kb + ((g - s.kb) & (NP - 1)); }
+template <int NP>
 PALU_DEVINL int seg_group_count(const RowSeg& s, int g) {
-  const int kf = seg_group_first(s, g);
-  return kf < s.kb + s.cnt ? (s.kb + s.cnt - kf + 1) / 2 : 0;
+  const int kf = seg_group_first<NP>(s, g);
+  return kf < s.kb + s.cnt ? (s.kb + s.cnt - kf + NP - 1) / NP : 0;
 }
 // Group g's tiles in order, with their row, tile within the row and group-segment index (segments in which
 // the group has tiles, counted from 0).
+template <int NP>
 struct GroupTiles {
   RowSeg s;
   int g, n, x, cnt, kf, sigma, len;  // len: positions the current row attends
@@ -130,16 +140,16 @@ struct GroupTiles {
     settle(p);
   }
   PALU_DEVINL void settle(const TcParams& p) {
-    while (s.cnt > 0 && (cnt = seg_group_count(s, g)) == 0) s = seg_next(p, n, s);
+    while (s.cnt > 0 && (cnt = seg_group_count<NP>(s, g)) == 0) s = seg_next(p, n, s);
     if (s.cnt > 0) {
-      kf = seg_group_first(s, g);
+      kf = seg_group_first<NP>(s, g);
       x = 0;
       ++sigma;
       len = row_len(p, s.b);
     }
   }
   PALU_DEVINL bool valid() const { return s.cnt > 0; }
-  PALU_DEVINL int tile() const { return s.ta + (kf - s.kb) + 2 * x; }
+  PALU_DEVINL int tile() const { return s.ta + (kf - s.kb) + NP * x; }
   PALU_DEVINL bool first() const { return x == 0; }
   PALU_DEVINL void next(const TcParams& p) {
     if (++x >= cnt) {
@@ -154,43 +164,55 @@ struct GroupTiles {
 };
 
 // Shared memory per CTA: the fixed buffers plus three rings, K (NS_K stages), V (NS_V stages) and the RoPE
-// table (T_SLOTS chunk slots per group). Stage i of the K and V rings holds tiles of group i % 2 only. The
-// first of these (NS_K, NS_V, T_SLOTS) choices that fits is used: two K stages per group, one V stage per
-// group and a whole tile of table chunks, when the latents are at most 64 wide.
+// table (T_SLOTS chunk slots per group). With two pipelines, stage i of the K and V rings holds tiles of
+// group i % 2 only. The first (NS_K, NS_V, T_SLOTS) choice that fits is used: with two pipelines, two K
+// stages per group, one V stage per group and a whole tile of table chunks when the latents are at most 64
+// wide. With one pipeline (latents up to 256 wide) a K stage is one 64-wide box (the reconstruction streams
+// a tile box by box), and the choice is three K boxes, one V tile and a whole tile of table chunks.
 constexpr int kTabChunkBytes = 8192;  // table chunk: 128 rows x 16 pairs x 4 B (SWIZZLE_64B)
 constexpr int kSmemBudget = 227 * 1024;
-constexpr int layout_need(int fixed, int kb, int vb, int nk, int nv, int t) {
-  return fixed + nk * kb + nv * vb + 2 * t * kTabChunkBytes;
+constexpr int layout_need(int fixed, int kb, int vb, int nk, int nv, int t, int np) {
+  return fixed + nk * kb + nv * vb + np * t * kTabChunkBytes;
 }
-constexpr int layout_pick(int fixed, int kb, int vb) {
-  constexpr int c[4][3] = {{4, 2, 4}, {2, 2, 4}, {4, 2, 2}, {2, 2, 2}};
-  for (int i = 0; i < 4; ++i)
-    if (layout_need(fixed, kb, vb, c[i][0], c[i][1], c[i][2]) <= kSmemBudget) return c[i][0] * 100 + c[i][1] * 10 + c[i][2];
-  return 222;
+constexpr int layout_pick(int fixed, int kb, int vb, int np) {
+  constexpr int c2[4][3] = {{4, 2, 4}, {2, 2, 4}, {4, 2, 2}, {2, 2, 2}};
+  constexpr int c1[5][3] = {{4, 1, 4}, {3, 1, 4}, {2, 1, 4}, {2, 1, 2}, {1, 1, 2}};
+  if (np == 2) {
+    for (int i = 0; i < 4; ++i)
+      if (layout_need(fixed, kb, vb, c2[i][0], c2[i][1], c2[i][2], 2) <= kSmemBudget)
+        return c2[i][0] * 100 + c2[i][1] * 10 + c2[i][2];
+    return 222;
+  }
+  for (int i = 0; i < 5; ++i)
+    if (layout_need(fixed, kb, vb, c1[i][0], c1[i][1], c1[i][2], 1) <= kSmemBudget)
+      return c1[i][0] * 100 + c1[i][1] * 10 + c1[i][2];
+  return 112;
 }
 
-template <int KBK, int KBV>
+// NP pipelines per CTA: 2 (latents at most 128 wide), or 1 (up to 256 wide: U_k alone is then 64 KB and a
+// K or V tile 64 KB, so one pipeline, a ring of K boxes and a single V stage is what fits).
+template <int KBK, int KBV, int NP>
 struct Layout {
-  static constexpr int K_BYTES = KBK * kBox;
+  static constexpr int K_BYTES = NP == 1 ? kBox : KBK * kBox;  // one pipeline: a K ring stage is one box
   static constexpr int V_BYTES = KBV * kBox;
   static constexpr int TCH_BYTES = kTabChunkBytes;
   static constexpr int U_BYTES = KBK * 2 * 64 * 128;  // 2 N-blocks x (<= 64 KBK rows) x 128 B
   static constexpr int Q_BYTES = 2 * 2048;            // one buffer: 2 K-blocks x 16 rows x 128 B (fp16)
   static constexpr int P_BYTES = 2 * 2048;            // one buffer: 2 K-blocks x 16 rows x 128 B (bf16)
   static constexpr int MISC_BYTES = 2048;
-  static constexpr int FIXED = U_BYTES + 4 * Q_BYTES + 4 * P_BYTES + MISC_BYTES + 1024;
-  static constexpr int PICK = layout_pick(FIXED, K_BYTES, V_BYTES);
+  static constexpr int FIXED = U_BYTES + 2 * NP * Q_BYTES + 2 * NP * P_BYTES + MISC_BYTES + 1024;
+  static constexpr int PICK = layout_pick(FIXED, K_BYTES, V_BYTES, NP);
   static constexpr int NS_K = PICK / 100, NS_V = PICK / 10 % 10, T_SLOTS = PICK % 10;
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + NS_K * K_BYTES;
   static constexpr int OFF_TAB = OFF_V + NS_V * V_BYTES;
-  static constexpr int OFF_U = OFF_TAB + 2 * T_SLOTS * TCH_BYTES;
+  static constexpr int OFF_U = OFF_TAB + NP * T_SLOTS * TCH_BYTES;
   static constexpr int OFF_Q = OFF_U + U_BYTES;
-  static constexpr int OFF_P = OFF_Q + 4 * Q_BYTES;  // Q: [group][segment parity], P: [group][tile parity]
-  static constexpr int OFF_MISC = OFF_P + 4 * P_BYTES;
+  static constexpr int OFF_P = OFF_Q + 2 * NP * Q_BYTES;  // Q: [group][segment parity], P: [group][tile parity]
+  static constexpr int OFF_MISC = OFF_P + 2 * NP * P_BYTES;
   static constexpr int TOTAL = OFF_MISC + MISC_BYTES + 1024;  // + slack to align the base to 1024
   static_assert(TOTAL <= kSmemBudget, "shared memory budget");
-  static_assert(NS_K % 2 == 0 && NS_V % 2 == 0, "K and V stages come in pairs, one per group");
+  static_assert(NS_K % NP == 0 && NS_V % NP == 0, "every group owns the same number of K and V stages");
 };
 
 // ---- PTX wrappers -----------------------------------------------------------------------------------
@@ -433,13 +455,19 @@ PALU_DEVINL int role_of(int warp) {
 // PAGED: the caches are paged (TcParams.page_table set). A template parameter rather than a runtime branch,
 // so that the contiguous-cache kernel carries none of the paged producers' code: with it the body fit the
 // instruction cache worse, and dropping it measured 2-4 % faster on B200.
-template <int KBK, int KBV, bool PAGED>
+template <int KBK, int KBV, bool PAGED, int NP>
 __global__ void __launch_bounds__(kThreads, 1)
     palu_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                           const __grid_constant__ CUtensorMap tm_tab, const TcParams p) {
-  using Lay = Layout<KBK, KBV>;
+  using Lay = Layout<KBK, KBV, NP>;
   constexpr int NS_K = Lay::NS_K, NS_V = Lay::NS_V, T_SLOTS = Lay::T_SLOTS;
-  constexpr int NS_T = 2 * T_SLOTS;  // table chunk slots, [group][slot]
+  constexpr int NS_T = NP * T_SLOTS;  // table chunk slots, [group][slot]
+  // V^T as PV's A operand: one M = 64 block (V at most 64 wide), one M = 128 block (at most 128), or two M = 128
+  // blocks (at most 256; a block's rows past the latent width are the TMA's zero fill).
+  constexpr int NMB = KBV <= 2 ? 1 : 2;
+  const int nmb = NMB == 1 || p.rv <= 128 ? 1 : 2;  // M-blocks that hold latent dims
+  // PV result columns of buffer b, M-block mb (relative to the group's TMEM base)
+  auto do_col = [](int b, int mb) -> uint32_t { return NP == 1 ? kColDoWide + mb * 32 + b * 16 : kColDo + b * 16; };
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -454,11 +482,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto bar = [&](int i) { return smem_u32(bars + i); };
   // [g][x] pairs are double-buffered by the group-local tile index parity x.
   // V-full barriers are per (slot, use parity), so a parity wait is never more than one phase behind.
-  // Drain barriers: [g][QK+PV issuer, reconstruct issuer].
+  // Drain barriers: [g][QK+PV issuer, reconstruct issuer]. One pipeline: REC[x] marks D_k[x] reconstructed
+  // (tiles j with j % 2 == x) and DKF[x] marks it read by RoPE.
   constexpr int B_KF = 0, B_KE = B_KF + NS_K, B_VF = B_KE + NS_K, B_VE = B_VF + 2 * NS_V, B_TF = B_VE + NS_V,
                 B_TE = B_TF + NS_T, B_UF = B_TE + NS_T, B_REC = B_UF + 1, B_AF = B_REC + 4, B_AE = B_AF + 4,
                 B_SF = B_AE + 2, B_SR = B_SF + 4, B_PF = B_SR + 4, B_OF = B_PF + 4, B_OR = B_OF + 4,
-                B_MX = B_OR + 4, B_QF = B_MX + 4, B_DRAIN = B_QF + 4, B_COUNT = B_DRAIN + 4;
+                B_MX = B_OR + 4, B_QF = B_MX + 4, B_DRAIN = B_QF + 4, B_DKF = B_DRAIN + 4, B_COUNT = B_DKF + 2;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + B_COUNT);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
   int* s_range = reinterpret_cast<int*>(s_tmem + 4);      // n, b0, t0, cnt0 of this CTA's range
@@ -507,6 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     for (int x = 0; x < 4; ++x) mbar_init(bar(B_DRAIN + x), 1);
+    for (int x = 0; x < 2; ++x) mbar_init(bar(B_DKF + x), 8);  // one pipeline: the 8 RoPE warps read D_k[x]
     *s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
@@ -546,7 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp >= kSoftWarp0) {
     // Q buffers (4 x 4 KB) and P buffers (4 x 4 KB): rows past the query heads stay zero throughout.
-    for (int e = (warp - kSoftWarp0) * 32 + lane; e < (4 * Lay::Q_BYTES + 4 * Lay::P_BYTES) / 16; e += 256)
+    for (int e = (warp - kSoftWarp0) * 32 + lane; e < (2 * NP * Lay::Q_BYTES + 2 * NP * Lay::P_BYTES) / 16; e += 256)
       reinterpret_cast<uint4*>(smem + Lay::OFF_Q)[e] = make_uint4(0, 0, 0, 0);
     fence_proxy_async();
   }
@@ -561,7 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp < kRoleWarps) {
     // ============================== single-lane role warps ==============================
     const int g = warp < 4 ? 0 : 1, role = role_of(warp);
-    const int n_g = (n - g + 1) / 2;  // this group's tiles: CTA-local t = g + 2 j, j < n_g
+    const int n_g = g < NP ? (n - g + NP - 1) / NP : 0;  // this group's tiles: CTA-local t = g + NP j, j < n_g
     if (lane == 0 && n_g > 0) {
       if (role == kRoleKT || role == kRoleV) {
         // ---- TMA producers: K tile then its 4 table chunks (KT), or the V tile (V), per group tile.
@@ -570,10 +600,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_prefetch_map(kt ? &tm_k : &tm_v);
         if (kt) tma_prefetch_map(&tm_tab);
         int issued_kv = 0, issued_t = 0;
-        GroupTiles it;
+        // One pipeline: K streams through a ring of single boxes (kbn: boxes issued so far).
+        const bool box_ring = NP == 1 && kt;
+        const int nbk = (p.rk + 63) >> 6;
+        int kbn = 0;
+        GroupTiles<NP> it;
         it.init(p, seg0, g, n);
         for (int j = 0; j < n_g && it.valid(); ++j, it.next(p)) {
-          const int t = g + 2 * j, row = it.tile() * kTile, item_lat = it.s.b * p.n_groups + lat_head;
+          const int t = g + NP * j, row = it.tile() * kTile, item_lat = it.s.b * p.n_groups + lat_head;
           const int sb = kt ? t % NS_K : t % NS_V, use = kt ? t / NS_K : t / NS_V;
           const uint32_t full = kt ? bar(B_KF + sb) : bar(B_VF + 2 * sb + (use & 1));
           const uint32_t empty = bar((kt ? B_KE : B_VE) + sb);
@@ -592,12 +626,36 @@ __global__ void __launch_bounds__(kThreads, 1)
                 blk[i] = (unsigned)e < (unsigned)p.n_blocks ? e * p.n_groups + lat_head : p.n_blocks * p.n_groups;
               }
           }
-          if (use >= 1 && !wait(empty, (use - 1) & 1)) break;
-          if (!starve) {
+          if (box_ring) {
+            bool ok = true;
+            for (int c = 0; c < nbk; ++c, ++kbn) {
+              const int s = kbn % NS_K, u = kbn / NS_K;
+              if (u >= 1 && !wait(bar(B_KE + s), (u - 1) & 1)) {
+                ok = false;
+                break;
+              }
+              const uint32_t kf = bar(B_KF + s), dst = sbase + Lay::OFF_K + s * Lay::K_BYTES;
+              mbar_expect_tx(kf, kBox);
+              if constexpr (!PAGED) {
+                tma_load_3d(dst, &tm_k, kf, c * 64, row, item_lat);
+              } else {
+                const int nsub = kTile >> p.blk_shift, sub_bytes = 128 << p.blk_shift;
+#pragma unroll
+                for (int i = 0; i < kTile / 16; ++i)
+                  if (i < nsub) tma_load_3d(dst + i * sub_bytes, &tm_k, kf, c * 64, 0, blk[i]);
+              }
+              issued_kv = kbn + 1;
+            }
+            if (!ok) break;
+          } else if (use >= 1 && !wait(empty, (use - 1) & 1)) {
+            break;
+          } else if (!starve) {
             const CUtensorMap* tm = kt ? &tm_k : &tm_v;
             const uint32_t dst = sbase + (kt ? Lay::OFF_K + sb * Lay::K_BYTES : Lay::OFF_V + sb * Lay::V_BYTES);
-            const int nbox = kt ? KBK : KBV;
-            mbar_expect_tx(full, kt ? Lay::K_BYTES : Lay::V_BYTES);
+            // boxes that hold latent dims (the wide layout reserves four; a tile of a narrower latent skips
+            // the boxes wholly past it, which its MMAs never read)
+            const int nbox = kt ? min(KBK, (p.rk + 63) >> 6) : min(KBV, (p.rv + 63) >> 6);
+            mbar_expect_tx(full, nbox * kBox);
             if constexpr (!PAGED) {
               for (int c = 0; c < nbox; ++c) tma_load_3d(dst + c * kBox, tm, full, c * 64, row, item_lat);
             } else {
@@ -628,11 +686,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (*s_abort) {  // let every copy already issued land before the CTA can exit
-          const int ring = kt ? NS_K / 2 : NS_V / 2;
-          for (int j = max(0, issued_kv - ring); j < issued_kv; ++j) {
-            const int t = g + 2 * j;
-            if (kt) mbar_drain(bar(B_KF + t % NS_K), (t / NS_K) & 1);
-            else mbar_drain(bar(B_VF + 2 * (t % NS_V) + ((t / NS_V) & 1)), (t / NS_V >> 1) & 1);
+          const int ring = kt ? NS_K / NP : NS_V / NP;
+          if (box_ring) {
+            for (int u = max(0, issued_kv - NS_K); u < issued_kv; ++u)
+              mbar_drain(bar(B_KF + u % NS_K), (u / NS_K) & 1);
+          } else {
+            for (int j = max(0, issued_kv - ring); j < issued_kv; ++j) {
+              const int t = g + NP * j;
+              if (kt) mbar_drain(bar(B_KF + t % NS_K), (t / NS_K) & 1);
+              else mbar_drain(bar(B_VF + 2 * (t % NS_V) + ((t / NS_V) & 1)), (t / NS_V >> 1) & 1);
+            }
           }
           for (int nc = max(0, issued_t - T_SLOTS); nc < issued_t; ++nc)
             mbar_drain(bar(B_TF + g * T_SLOTS + nc % T_SLOTS), (nc / T_SLOTS) & 1);
@@ -651,8 +714,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           // bf16 V^T (MN-major) x bf16 P. A V latent at most 64 wide is one M = 64 block: with M = 128 the
           // MMA read every V row twice (measured 1.6 % faster at the bench workload with M = 64).
           constexpr uint32_t ID_PV = idesc_f16(16, 1, true, false, KBV == 1 ? 64 : 128);
-          const uint32_t v_lbo = p.rv > 64 ? kBox : 0;  // V: second 64-dim M-block (or a duplicate of the first)
-          GroupTiles it, pit;  // QK(j) and PV(j - 1) tiles
+          static_assert(KBV != 1 || NMB == 1, "an M = 64 PV block holds the whole V latent");
+          const uint32_t v_lbo = p.rv > 64 ? kBox : 0;  // V: stride between the 64-dim halves of an M = 128 block
+          GroupTiles<NP> it, pit;  // QK(j) and PV(j - 1) tiles
           it.init(p, seg0, g, n);
           pit.init(p, seg0, g, n);
           for (int j = 0; j <= n_g; ++j) {
@@ -682,7 +746,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (!ok) break;
             }
             if (j >= 1) {  // PV(j - 1)
-              const int jp = j - 1, tp = g + 2 * jp, sv = tp % NS_V;
+              const int jp = j - 1, tp = g + NP * jp, sv = tp % NS_V;
               if (!wait(bar(B_PF + 2 * g + (jp & 1)), (jp >> 1) & 1)) break;
               if (jp >= 2 && !wait(bar(B_OR + 2 * g + (jp & 1)), ((jp >> 1) - 1) & 1)) break;
               if (!wait(bar(B_VF + 2 * sv + ((tp / NS_V) & 1)), (tp / NS_V >> 1) & 1)) break;
@@ -698,9 +762,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (nv >= kTile) {
                 fence_after();
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                  mma_ss(tg + kColDo + (jp & 1) * 16, sdesc(sV + kk * 2048, v_lbo, 1024),
-                         sdesc(sP + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), ID_PV, kk > 0);
+                for (int mb = 0; mb < NMB; ++mb)
+                  if (mb < nmb)
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk)
+                      mma_ss(tg + do_col(jp & 1, mb), sdesc(sV + mb * 2 * kBox + kk * 2048, v_lbo, 1024),
+                           sdesc(sP + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), ID_PV, kk > 0);
               } else {
                 const int ksteps = (nv + 15) >> 4;
                 for (int rr = nv; rr < ksteps * 16; ++rr)
@@ -711,9 +778,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                           make_uint4(0, 0, 0, 0);
                 fence_proxy_async();
                 fence_after();
-                for (int kk = 0; kk < ksteps; ++kk)
-                  mma_ss(tg + kColDo + (jp & 1) * 16, sdesc(sV + kk * 2048, v_lbo, 1024),
-                         sdesc(sP + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), ID_PV, kk > 0);
+                for (int mb = 0; mb < nmb; ++mb)
+                  for (int kk = 0; kk < ksteps; ++kk)
+                    mma_ss(tg + do_col(jp & 1, mb), sdesc(sV + mb * 2 * kBox + kk * 2048, v_lbo, 1024),
+                           sdesc(sP + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), ID_PV, kk > 0);
               }
               mma_commit(bar(B_OF + 2 * g + (jp & 1)));
               mma_commit(bar(B_VE + sv));
@@ -726,7 +794,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sU = sbase + Lay::OFF_U;
           const uint32_t u_lbo = p.rk * 128;  // U: stride between the two 64-column N-blocks
           auto recon = [&](int j, int h) -> bool {
-            const int t = g + 2 * j, s = t % NS_K;
+            const int t = g + NP * j, s = t % NS_K;
             if (h == 0 && !wait(bar(B_KF + s), (t / NS_K) & 1)) return false;
             fence_after();
             const uint32_t sK = sbase + Lay::OFF_K + s * Lay::K_BYTES;
@@ -737,9 +805,36 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_commit(bar(B_REC + 2 * g + h));
             return true;
           };
-          bool ok = wait(bar(B_UF), 0) && recon(0, 0) && recon(0, 1);
-          for (int j = 0; ok && j + 1 < n_g; ++j)
-            for (int h = 0; ok && h < 2; ++h) ok = wait(bar(B_AF + 2 * g + h), j & 1) && recon(j + 1, h);
+          if constexpr (NP == 2) {
+            bool ok = wait(bar(B_UF), 0) && recon(0, 0) && recon(0, 1);
+            for (int j = 0; ok && j + 1 < n_g; ++j)
+              for (int h = 0; ok && h < 2; ++h) ok = wait(bar(B_AF + 2 * g + h), j & 1) && recon(j + 1, h);
+          } else {
+            // One pipeline: D_k is double-buffered by tile parity (columns kColDk / kColDk2), so reconstruct(j)
+            // runs a whole tile ahead of RoPE(j - 1): it waits only for RoPE(j - 2) to have read its buffer.
+            // It is one N = 128 pass streamed box by box through the K ring (4 K-steps per 64-wide box), each
+            // box released as soon as its MMAs complete.
+            constexpr uint32_t ID_REC2 = idesc_f16(128, 1, false, true);  // N = 128: both frequency halves
+            const int nbk = (p.rk + 63) >> 6, nks = p.rk >> 4;
+            int kbn = 0;
+            bool ok = wait(bar(B_UF), 0);
+            for (int j = 0; ok && j < n_g; ++j) {
+              if (j >= 2 && !(ok = wait(bar(B_DKF + (j & 1)), ((j >> 1) - 1) & 1))) break;
+              fence_after();
+              const uint32_t dk = tg + ((j & 1) ? kColDk2 : kColDk);
+              for (int c = 0; c < nbk; ++c, ++kbn) {
+                const int s = kbn % NS_K;
+                if (!(ok = wait(bar(B_KF + s), (kbn / NS_K) & 1))) break;
+                fence_after();
+                const uint32_t sK = sbase + Lay::OFF_K + s * Lay::K_BYTES;
+                for (int kk = 4 * c; kk < min(4 * c + 4, nks); ++kk)
+                  mma_ss(dk, sdesc(sK + (kk & 3) * 32, 16, 1024), sdesc(sU + kk * 2048, u_lbo, 1024), ID_REC2,
+                         kk > 0);
+                mma_commit(bar(B_KE + s));
+              }
+              if (ok) mma_commit(bar(B_REC + (j & 1)));
+            }
+          }
         }
         // Drain: every MMA this thread issued has completed once this barrier flips.
         mma_commit(bar(drain));
@@ -749,7 +844,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp < kSoftWarp0) {
     // ============================== RoPE warps ==============================
-    const int g = (warp - kRopeWarp0) >> 2, quarter = warp & 3, row = quarter * 32 + lane;
+    // Two pipelines: warps 4 g .. 4 g + 3 rotate pipeline g's tiles, all four chunks each. One pipeline: all
+    // 8 warps rotate every tile, warps 4 hh .. 4 hh + 3 its frequency half hh (chunks 2 hh, 2 hh + 1), so
+    // the two halves of a tile run side by side.
+    const int g = NP == 2 ? (warp - kRopeWarp0) >> 2 : 0, quarter = warp & 3, row = quarter * 32 + lane;
+    const int ch0 = NP == 2 ? 0 : ((warp - kRopeWarp0) >> 2) * 2, nch = NP == 2 ? 4 : 2;
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + g * kGrpCols;
     {
       // U_k -> shared memory as the MN-major SWIZZLE_128B B operand of the reconstruction, one 64-column
@@ -773,18 +872,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(B_UF));
     }
-    const int n_g = (n - g + 1) / 2;
+    const int n_g = NP == 2 ? (n - g + 1) / 2 : n;
     for (int i = 0; i < n_g; ++i) {
       // ---- RoPE(i), by halves: D_k columns 64 h .. 64 h + 31 hold the even dims of frequencies 32 h + c,
       // columns 64 h + 32 + c their odd dims; chunk ch = 2 h + sub rotates frequencies 16 ch .. 16 ch + 15.
       // K_rot -> fp16 A columns. Finishing half h releases D_k half h (reconstruction of tile i + 1) and
       // hands A half h to QK(i).
+      // One pipeline: D_k[i % 2] holds the whole tile once REC[i % 2] flips; reading it is signalled on DKF.
       bool ok = true;
+      const uint32_t dk = trow + (NP == 1 && (i & 1) ? kColDk2 : kColDk);
 #pragma unroll 1
-      for (int ch = 0; ch < 4; ++ch) {
-        const int h = ch >> 1, sub = ch & 1;
+      for (int c = 0; c < nch; ++c) {
+        const int ch = ch0 + c, h = ch >> 1, sub = ch & 1;
         if (sub == 0) {
-          if (!wait_all(bar(B_REC + 2 * g + h), i & 1)) {
+          if (!(NP == 2 ? wait_all(bar(B_REC + 2 * g + h), i & 1) : wait_all(bar(B_REC + (i & 1)), (i >> 1) & 1))) {
             ok = false;
             break;
           }
@@ -793,8 +894,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int n = i * 4 + ch, sb = g * T_SLOTS + n % T_SLOTS;
         // The chunk's D_k columns load while this warp waits for and reads its table chunk.
         uint32_t ke[16], ko[16];
-        tmem_ld16(trow + kColDk + 64 * h + 16 * sub, ke);
-        tmem_ld16(trow + kColDk + 64 * h + 32 + 16 * sub, ko);
+        tmem_ld16(dk + 64 * h + 16 * sub, ke);
+        tmem_ld16(dk + 64 * h + 32 + 16 * sub, ko);
         if (!wait_all(bar(B_TF + sb), (n / T_SLOTS) & 1)) {
           tmem_wait_ld_regs(ke, ko);
           ok = false;
@@ -813,6 +914,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           cs[4 * c4 + 3] = w.w;
         }
         tmem_wait_ld_regs(ke, ko);
+        if (NP == 1 && sub == 1) {  // this warp's last read of D_k[i % 2]
+          fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(B_DKF + (i & 1)));
+        }
         uint32_t ae[8], ao[8];
 #pragma unroll
         for (int x = 0; x < 8; ++x) {
@@ -892,25 +998,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     // Q for the group's first two segments now; at the start of segment sigma >= 1, the one after it
     // (buffer (sigma + 1) & 1 last fed QK of segment sigma - 1, all of whose scores are read by then).
-    GroupTiles qa;
+    GroupTiles<NP> qa;
     qa.init(p, seg0, g, n);
-    if (qa.valid()) {
+    if (g < NP && qa.valid()) {
       stage_q(qa.s.b, 0);
       qa.next_segment(p);
       if (qa.valid()) stage_q(qa.s.b, 1);
     }
-    float m_run[4], l_run[4], o_acc[4], alpha0[4], alpha1[4];  // alphaN: softmax scale of tiles j with j%2 == N
+    // alphaN: softmax scale of tiles j with j%2 == N; o_acc[mb][h]: latent dim 128 mb + row of head h
+    float m_run[4], l_run[4], o_acc[NMB][4], alpha0[4], alpha1[4];
     int j0 = 0, sigma = 0;
     bool ok = true;
-    for (RowSeg sg = seg0; sg.cnt > 0; sg = seg_next(p, n, sg)) {
+    for (RowSeg sg = seg0; g < NP && sg.cnt > 0; sg = seg_next(p, n, sg)) {
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         m_run[h] = -INFINITY;
         l_run[h] = 0.f;
-        o_acc[h] = 0.f;
+#pragma unroll
+        for (int mb = 0; mb < NMB; ++mb) o_acc[mb][h] = 0.f;
         alpha0[h] = alpha1[h] = 1.f;
       }
-      const int cnt = seg_group_count(sg, g), kf = seg_group_first(sg, g);
+      const int cnt = seg_group_count<NP>(sg, g), kf = seg_group_first<NP>(sg, g);
       if (cnt > 0) {
         if (sigma >= 1) {
           qa.next_segment(p);
@@ -935,7 +1043,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(B_SR + 2 * g + (j & 1)));  // D_s[j & 1] may be overwritten
-            const int tile_start = (sg.ta + (kf - sg.kb) + 2 * x) * kTile;
+            const int tile_start = (sg.ta + (kf - sg.kb) + NP * x) * kTile;
             const bool valid = tile_start + row < L;
             float xs[4], mx[4];
 #pragma unroll
@@ -985,12 +1093,17 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             fence_after();
-            uint32_t ov[8];
-            tmem_ld8(trow + kColDo + (ja & 1) * 16, ov);
-            tmem_wait_ld_regs(ov);
 #pragma unroll
-            for (int h = 0; h < 4; ++h)
-              o_acc[h] = o_acc[h] * ((ja & 1) ? alpha1[h] : alpha0[h]) + __uint_as_float(ov[h]) + __uint_as_float(ov[4 + h]);
+            for (int mb = 0; mb < NMB; ++mb) {
+              if (mb >= nmb) break;
+              uint32_t ov[8];
+              tmem_ld8(trow + do_col(ja & 1, mb), ov);
+              tmem_wait_ld_regs(ov);
+#pragma unroll
+              for (int h = 0; h < 4; ++h)
+                o_acc[mb][h] = o_acc[mb][h] * ((ja & 1) ? alpha1[h] : alpha0[h]) + __uint_as_float(ov[h]) +
+                               __uint_as_float(ov[4 + h]);
+            }
             fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(B_OR + 2 * g + (ja & 1)));
@@ -1016,9 +1129,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (h < p.rep) {
           if (lane == 0) wml[h * 5 + 1 + quarter] = v;
           if (quarter == 0 && lane == 0) wml[h * 5] = m_run[h];
-          // D_o rows (latent dims): lane 32 q + l holds row 32 q + l (M = 128), or row 16 q + l for l < 16 (M = 64)
-          const int orow = KBV == 1 ? 16 * quarter + lane : row;
-          if ((KBV != 1 || lane < 16) && orow < p.rv) wo[h * p.rv + orow] = o_acc[h];
+          // D_o rows (latent dims): lane 32 q + l holds row 32 q + l (M = 128), or row 16 q + l for l < 16 (M = 64);
+          // M-block mb holds latent dims 128 mb + row.
+#pragma unroll
+          for (int mb = 0; mb < NMB; ++mb) {
+            const int orow = KBV == 1 ? 16 * quarter + lane : 128 * mb + row;
+            if ((KBV != 1 || lane < 16) && orow < p.rv) wo[h * p.rv + orow] = o_acc[mb][h];
+          }
         }
       }
     }

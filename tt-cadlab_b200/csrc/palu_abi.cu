@@ -121,9 +121,11 @@ int g_kernel_choice = PALU_KERNEL_AUTO;
 std::atomic<unsigned long long> g_wait_ns{palu::tc::kWaitNs};
 std::atomic<int> g_starve_v{0};
 
+// Latents up to 128 wide run two pipelines per CTA; up to 256 wide, one (tc_pipes).
 bool tc_supported(const palu_decode_dims* d, bool recon) {
-  return recon && d->r_k <= 128 && d->r_v <= 128 && rep_of(d) <= 4;
+  return recon && d->r_k <= 256 && d->r_v <= 256 && rep_of(d) <= 4;
 }
+int tc_pipes(const palu_decode_dims* d) { return d->r_k > 128 || d->r_v > 128 ? 1 : 2; }
 
 bool use_tc(const palu_decode_dims* d, bool recon) {
   if (g_kernel_choice == PALU_KERNEL_MMA) return false;
@@ -197,11 +199,11 @@ void set_pages(Params& p, const palu_page_table* pg) {
   while (pg && (1 << p.blk_shift) < pg->block_size) ++p.blk_shift;
 }
 
-template <int KBK, int KBV, bool PAGED>
+template <int KBK, int KBV, bool PAGED, int NP = 2>
 int launch_tc(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mt, const palu::tc::TcParams& p,
               cudaStream_t stream) {
-  using Lay = palu::tc::Layout<KBK, KBV>;
-  auto kern = palu::tc::palu_decode_tc_kernel<KBK, KBV, PAGED>;
+  using Lay = palu::tc::Layout<KBK, KBV, NP>;
+  auto kern = palu::tc::palu_decode_tc_kernel<KBK, KBV, PAGED, NP>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::TOTAL) != cudaSuccess)
     return cuda_check("cudaFuncSetAttribute(decode tc)");
   kern<<<dim3(p.ctas, p.n_kv, 1), palu::tc::kThreads, Lay::TOTAL, stream>>>(mk, mv, mt, p);
@@ -259,6 +261,8 @@ int run_tc(const void* q, const void* k, const void* v, const void* u_k, int64_t
   p.wait_ns = g_wait_ns.load(std::memory_order_relaxed);
   p.starve_v = g_starve_v.load(std::memory_order_relaxed);
   p.pdl_early = (long)splits * d->n_kv_heads <= device_sms();
+  if (tc_pipes(d) == 1)  // latents wider than 128: one pipeline, four 64-wide boxes per K and V tile
+    return pg ? launch_tc<4, 4, true, 1>(mk, mv, mt, p, stream) : launch_tc<4, 4, false, 1>(mk, mv, mt, p, stream);
   const int kbk = d->r_k > 64 ? 2 : 1, kbv = d->r_v > 64 ? 2 : 1;
   if (pg) {
     if (kbk == 1 && kbv == 1) return launch_tc<1, 1, true>(mk, mv, mt, p, stream);
@@ -375,6 +379,7 @@ int run_decode(bool recon, const void* q, const void* k, const void* v, const vo
     c.r_lat = d->r_v;
     c.r_out = u_v ? 128 : d->r_v;
     c.max_seq = d->max_seq;
+    c.npipe = tc_pipes(d);
     // Programmatic dependent launch: the merge's prologue overlaps the decode kernel's tail.
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(d->n_q_heads, d->batch);

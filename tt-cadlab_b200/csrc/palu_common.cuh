@@ -74,7 +74,8 @@ PALU_DEVINL float2 unpack_bf16(uint32_t v) {
 }
 
 // Partial records of the tcgen05 decode (decode_tc.cuh: one CTA per (tile range, KV head), two groups
-// per CTA): a batch row wholly inside one CTA has a direct pair (one record per group); a CTA's first
+// per CTA, or one for latents wider than 128, whose second record of each pair stays unused): a batch row
+// wholly inside one CTA has a direct pair (one record per group); a CTA's first
 // segment, when its row began in an earlier CTA (side 0), and its last segment, when its row continues in
 // a later one (side 1), have the CTA's edge pairs. Each record: O [rep][r_v] and (m, l x 4) [rep][5].
 __host__ __device__ inline size_t tc_rec_direct(int b, int kvh, int n_kv, int g) {
