@@ -32,6 +32,11 @@
  *                             page-table convention is the stock paged flash-decode op's the plan names
  *                             as its template: caches [n_blocks][heads][block_size][width], a table
  *                             [B][blocks per row] of physical block indices.
+ *   palu_decode_attn_f8 / palu_append_latents_f8 / palu_quantize_latents_f8
+ *                          <- palu_sdpa_decode and paged_update_cache over block-float latent caches
+ *                             (bfp8_b by default, bfp4_b per side: palu_tt/attention.py:159-169;
+ *                             tests/test_palu_sdpa_device.py:558-575), in the B200 form: e4m3 codes with
+ *                             one power-of-two scale per (position, latent head).
  */
 #ifndef PALU_B200_H
 #define PALU_B200_H
@@ -141,6 +146,33 @@ typedef struct palu_page_table {
   int32_t block_size;
   int32_t n_blocks;
 } palu_page_table;
+
+/*
+ * fp8 latent caches. k_codes [B][n_groups][max_seq][r_k] and v_codes [B][n_groups][max_seq][r_v] hold
+ * e4m3 codes (one byte each), k_exp and v_exp [B][n_groups][max_seq] int8 the exponent k of each row's
+ * scale: the cached value is code * 2^k. palu_quantize_latents_f8 and palu_append_latents_f8 write them:
+ * k is the smallest integer with max|row| <= 448 * 2^k, kept in [-120, 7] (0 for an all-zero row); the
+ * codes are the row times 2^-k rounded to nearest even with saturation, codes below the smallest normal
+ * e4m3 value stored as a signed zero.
+ *
+ * palu_decode_attn_f8: palu_decode_attn over such caches (every other argument, the workspace and the
+ * output as palu_decode_attn; same palu_workspace_bytes(dims)). The result equals palu_decode_attn's on
+ * the dequantized caches (the kernel rebuilds each row's bf16 values exactly). Envelope: r_k, r_v <= 128,
+ * contiguous caches, the tcgen05 kernel (PALU_ERR_INVALID under palu_set_kernel(PALU_KERNEL_MMA)).
+ */
+int palu_decode_attn_f8(const void* q, const void* k_codes, const void* v_codes, const int8_t* k_exp,
+                        const int8_t* v_exp, const void* u_k, int64_t u_k_ld, const void* u_v, const void* cs_pairs,
+                        const int32_t* cur_pos, void* out, int32_t out_dtype, void* workspace, size_t workspace_bytes,
+                        const palu_decode_dims* dims, float scale, palu_stream_t stream);
+
+/* rows x r bf16 values (r a multiple of 16 in [16, 256]) -> rows x r e4m3 codes and rows exponents. */
+int palu_quantize_latents_f8(const void* latents, int64_t rows, int32_t r, void* codes, int8_t* exps,
+                             palu_stream_t stream);
+
+/* palu_append_latents into fp8 caches: new_k [B][n_groups][r_k], new_v [B][n_groups][r_v] bf16 quantized
+ * row by row into position cur_pos[b]; rows with cur_pos outside [0, max_seq) are skipped. */
+int palu_append_latents_f8(const void* new_k, const void* new_v, const int32_t* cur_pos, void* k_codes, void* v_codes,
+                           int8_t* k_exp, int8_t* v_exp, const palu_decode_dims* dims, palu_stream_t stream);
 
 /*
  * palu_decode_attn over paged caches: every other argument, the workspace and the output as

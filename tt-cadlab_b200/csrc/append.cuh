@@ -7,8 +7,15 @@
 //    block is one 64-byte TMA row segment, and consecutive frequencies sit side by side so that the
 //    rotation runs on two frequencies per packed half2 instruction. fp16 holds every bf16 table value
 //    exactly (|cos|, |sin| <= 1; below 6e-5 fp16 is subnormal, an absolute error under 3e-8).
+//  * palu_quantize_f8_kernel: fp8 latent caches (the B200 form of the reference's block-float bfp8 latent
+//    caches, attention.py:159-169): each row of r latent values (one position of one latent head) becomes
+//    r e4m3 codes and one power-of-two exponent k, value = code * 2^k. k is the smallest integer with
+//    amax <= 448 * 2^k (448 = the largest e4m3 value), kept in [-120, 7]; scaling by 2^-k is exact, the codes
+//    round to nearest even with saturation, and codes below the smallest normal e4m3 value (exponent
+//    field 0) are flushed to a signed zero, so every stored code converts to bf16 by moving bit fields.
 #pragma once
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 
 #include "palu_common.cuh"
 
@@ -75,6 +82,64 @@ __global__ void palu_pack_cs_kernel(const void* cs_tab, long ld, int in_f32, uin
     }
     const __half2 h = __floats2half2_rn(a, bv);
     out[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+
+// ---- fp8 latent rows ---------------------------------------------------------------------------------
+struct QuantF8Params {
+  const __nv_bfloat16* src;  // rows of r bf16 values
+  long rows;                 // rows to quantize
+  int r;                     // values per row (<= 256)
+  uint8_t* codes;            // destination rows of r e4m3 codes
+  int8_t* exps;              // destination exponents, one per row
+  // Append mode (cur_pos set): source row i = (b, latent head) = (i / n_groups, i % n_groups) goes to
+  // destination row i * max_seq + cur_pos[b]; rows with cur_pos outside [0, max_seq) are skipped.
+  const int32_t* cur_pos;
+  int n_groups, max_seq;
+};
+
+// The row exponent: the smallest k with amax <= 448 * 2^k, kept in [-120, 7] (0 for an all-zero row). With
+// amax = m * 2^e, m in [0.5, 1): 448 * 2^k = 0.875 * 2^(k + 9), so k = e - 9 when m <= 0.875, else e - 8.
+PALU_DEVINL int f8_row_exponent(float amax) {
+  if (!(amax > 0.f)) return 0;
+  int e;
+  const float m = frexpf(amax, &e);
+  const int k = m <= 0.875f ? e - 9 : e - 8;
+  return k > 7 ? 7 : (k < -120 ? -120 : k);
+}
+PALU_DEVINL uint8_t f8_code(float y) {
+  uint8_t c = (uint8_t)__nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3);
+  return (c & 0x78) ? c : (uint8_t)(c & 0x80);  // exponent field 0: flush to a signed zero
+}
+
+// One warp per row: lane l holds values l, l + 32, ... (up to 8).
+__global__ void palu_quantize_f8_kernel(const QuantF8Params p) {
+  const int lane = threadIdx.x & 31;
+  const long warps = (long)gridDim.x * (blockDim.x >> 5);
+  for (long i = blockIdx.x * (long)(blockDim.x >> 5) + (threadIdx.x >> 5); i < p.rows; i += warps) {
+    long dst = i;
+    if (p.cur_pos) {
+      const int pos = p.cur_pos[i / p.n_groups];
+      if (pos < 0 || pos >= p.max_seq) continue;
+      dst = i * p.max_seq + pos;
+    }
+    float x[8];
+    float amax = 0.f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const int d = lane + 32 * c;
+      x[c] = d < p.r ? __bfloat162float(p.src[i * p.r + d]) : 0.f;
+      amax = fmaxf(amax, fabsf(x[c]));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const int k = f8_row_exponent(amax);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const int d = lane + 32 * c;
+      if (d < p.r) p.codes[dst * p.r + d] = f8_code(ldexpf(x[c], -k));
+    }
+    if (lane == 0) p.exps[dst] = (int8_t)k;
   }
 }
 

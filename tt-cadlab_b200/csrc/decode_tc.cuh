@@ -88,6 +88,11 @@ struct TcParams {
   // (griddepcontrol.wait) instead of being launched after the last one. With more CTAs than one wave the
   // trigger stays implicit at exit, so no merge CTA can hold an SM a decode CTA is still waiting for.
   int pdl_early;
+  // fp8 latent caches (the F8 kernels): e4m3 codes in the caches above, and per (batch row, latent head,
+  // position) the power-of-two exponent k of the row's scale, [B][n_groups][max_seq] int8 each; a cached
+  // value is code * 2^k.
+  const int8_t* k_exp;
+  const int8_t* v_exp;
 };
 
 // Work split: the tiles of one KV head over all batch rows, in row order (row b has ceil(L_b / 128)
@@ -330,6 +335,15 @@ PALU_DEVINL void mma_commit(uint32_t bar) {
 }
 PALU_DEVINL void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 PALU_DEVINL void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+// fp8 caches: two e4m3 codes at bits 8..15 and 24..31 of x, as the bf16 pair whose sign, exponent and
+// mantissa fields hold the code's: the value times 2^-120 exactly (bf16 and e4m3 share the subnormal
+// structure, and zero stays zero), so a multiply by 2^(120 + k) yields code * 2^k with no rounding.
+PALU_DEVINL uint32_t e4m3_pair_as_bf16x2(uint32_t x) { return ((x >> 4) & 0x07F007F0u) | (x & 0x80008000u); }
+PALU_DEVINL uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  const __nv_bfloat162 r =
+      __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&a), *reinterpret_cast<const __nv_bfloat162*>(&b));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
 PALU_DEVINL void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 PALU_DEVINL void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 PALU_DEVINL void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
@@ -455,10 +469,11 @@ PALU_DEVINL int role_of(int warp) {
 // PAGED: the caches are paged (TcParams.page_table set). A template parameter rather than a runtime branch,
 // so that the contiguous-cache kernel carries none of the paged producers' code: with it the body fit the
 // instruction cache worse, and dropping it measured 2-4 % faster on B200.
-template <int KBK, int KBV, bool PAGED, int NP>
+template <int KBK, int KBV, bool PAGED, int NP, bool F8 = false>
 __global__ void __launch_bounds__(kThreads, 1)
     palu_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                           const __grid_constant__ CUtensorMap tm_tab, const TcParams p) {
+  static_assert(!F8 || (NP == 2 && !PAGED), "fp8 latent caches: contiguous caches, latents at most 128 wide");
   using Lay = Layout<KBK, KBV, NP>;
   constexpr int NS_K = Lay::NS_K, NS_V = Lay::NS_V, T_SLOTS = Lay::T_SLOTS;
   constexpr int NS_T = NP * T_SLOTS;  // table chunk slots, [group][slot]
@@ -483,11 +498,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   // [g][x] pairs are double-buffered by the group-local tile index parity x.
   // V-full barriers are per (slot, use parity), so a parity wait is never more than one phase behind.
   // Drain barriers: [g][QK+PV issuer, reconstruct issuer]. One pipeline: REC[x] marks D_k[x] reconstructed
-  // (tiles j with j % 2 == x) and DKF[x] marks it read by RoPE.
+  // (tiles j with j % 2 == x) and DKF[x] marks it read by RoPE. fp8 caches: ST[slot] marks a slot's e4m3
+  // tile landed in its staging half (K slots, then V slots); KF / VF then mark it converted to bf16.
   constexpr int B_KF = 0, B_KE = B_KF + NS_K, B_VF = B_KE + NS_K, B_VE = B_VF + 2 * NS_V, B_TF = B_VE + NS_V,
                 B_TE = B_TF + NS_T, B_UF = B_TE + NS_T, B_REC = B_UF + 1, B_AF = B_REC + 4, B_AE = B_AF + 4,
                 B_SF = B_AE + 2, B_SR = B_SF + 4, B_PF = B_SR + 4, B_OF = B_PF + 4, B_OR = B_OF + 4,
-                B_MX = B_OR + 4, B_QF = B_MX + 4, B_DRAIN = B_QF + 4, B_DKF = B_DRAIN + 4, B_COUNT = B_DKF + 2;
+                B_MX = B_OR + 4, B_QF = B_MX + 4, B_DRAIN = B_QF + 4, B_DKF = B_DRAIN + 4, B_STK = B_DKF + 2, B_STV = B_STK + NS_K,
+                B_COUNT = B_STV + NS_V;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + B_COUNT);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
   int* s_range = reinterpret_cast<int*>(s_tmem + 4);      // n, b0, t0, cnt0 of this CTA's range
@@ -537,6 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int x = 0; x < 4; ++x) mbar_init(bar(B_DRAIN + x), 1);
     for (int x = 0; x < 2; ++x) mbar_init(bar(B_DKF + x), 8);  // one pipeline: the 8 RoPE warps read D_k[x]
+    for (int s = 0; s < NS_K + NS_V; ++s) mbar_init(bar(B_STK + s), 1);  // fp8: a staged tile has landed
     *s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
@@ -592,7 +610,115 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ============================== single-lane role warps ==============================
     const int g = warp < 4 ? 0 : 1, role = role_of(warp);
     const int n_g = g < NP ? (n - g + NP - 1) / NP : 0;  // this group's tiles: CTA-local t = g + NP j, j < n_g
-    if (lane == 0 && n_g > 0) {
+    if (F8 && (role == kRoleKT || role == kRoleV)) {
+      if (n_g > 0) {
+        // ---- fp8 producers (whole warp). Lane 0 issues the TMA of a tile's e4m3 codes into the upper half of
+        // its ring slot, up to the ring's depth ahead; the warp converts each landed tile in place into the
+        // bf16 tile the MMAs read (SWIZZLE_128B K-major boxes of 64 dims), row t multiplied by its power of
+        // two 2^k exactly; the K warp then issues the tile's 4 table chunks (after the conversion, as RoPE of
+        // the previous tile, which frees their slots, waits for it).
+        const bool kt = role == kRoleKT;
+        const int NS = kt ? NS_K : NS_V, ring = NS / NP;
+        const uint32_t slot_bytes = kt ? Lay::K_BYTES : Lay::V_BYTES, off0 = kt ? Lay::OFF_K : Lay::OFF_V;
+        const int nbox = kt ? KBK : KBV, row8 = nbox * 64;  // bf16 boxes per row; staged bytes per row
+        const int8_t* exps = kt ? p.k_exp : p.v_exp;
+        const CUtensorMap* tm = kt ? &tm_k : &tm_v;
+        const int b_st = kt ? B_STK : B_STV;
+        if (lane == 0) {
+          tma_prefetch_map(tm);
+          if (kt) tma_prefetch_map(&tm_tab);
+        }
+        GroupTiles<NP> iss, cv;
+        iss.init(p, seg0, g, n);
+        cv.init(p, seg0, g, n);
+        int ji = 0, jc = 0, issued_t = 0;
+        bool ok = true;
+        for (int j = 0; ok && j < n_g && cv.valid(); ++j, cv.next(p)) {
+          for (; ji < n_g && ji < j + ring && iss.valid(); ++ji, iss.next(p)) {
+            const int t = g + NP * ji, sb = t % NS, use = t / NS;
+            if (use >= 1 && !wait_all(bar((kt ? B_KE : B_VE) + sb), (use - 1) & 1)) {
+              ok = false;
+              break;
+            }
+            if (lane == 0) {
+              mbar_expect_tx(bar(b_st + sb), row8 * kTile);
+              tma_load_3d(sbase + off0 + sb * slot_bytes + slot_bytes / 2, tm, bar(b_st + sb), 0, iss.tile() * kTile,
+                          iss.s.b * p.n_groups + lat_head);
+            }
+          }
+          if (!ok) break;
+          const int t = g + NP * j, sb = t % NS, use = t / NS, row0 = cv.tile() * kTile;
+          const int8_t* erow = exps + ((size_t)cv.s.b * p.n_groups + lat_head) * p.max_seq;
+          int ex[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int pos = row0 + 32 * q + lane;
+            ex[q] = pos < p.max_seq ? __ldg(erow + pos) : 0;
+          }
+          if (!wait_all(bar(b_st + sb), use & 1)) {
+            ok = false;
+            break;
+          }
+          unsigned char* slot = smem + off0 + sb * slot_bytes;
+          const unsigned char* stage = slot + slot_bytes / 2;
+#pragma unroll 1
+          for (int q = 0; q < 4; ++q) {
+            // rows 32 q .. 32 q + 31, one per lane. Every lane reads its whole staged row before any lane
+            // writes: the bf16 rows of this batch overlap staged rows of this batch and earlier ones only.
+            const int r = 32 * q + lane;
+            uint4 in[2 * 4];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              if (i < nbox * 4) in[i] = reinterpret_cast<const uint4*>(stage + r * row8)[i];
+            __syncwarp();
+            const uint32_t s1 = (uint32_t)(247 + ex[q]) << 7, s2 = s1 | (s1 << 16);  // bf16 2^(120 + k), twice
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              if (i < nbox * 4) {
+                const uint32_t w[4] = {in[i].x, in[i].y, in[i].z, in[i].w};
+                uint32_t o[8];
+#pragma unroll
+                for (int x = 0; x < 4; ++x) {
+                  o[2 * x] = bf16x2_mul(e4m3_pair_as_bf16x2(__byte_perm(w[x], 0, 0x1404)), s2);
+                  o[2 * x + 1] = bf16x2_mul(e4m3_pair_as_bf16x2(__byte_perm(w[x], 0, 0x3424)), s2);
+                }
+                // elements 16 i .. 16 i + 15 = 16-byte chunks 2 (i % 4) and 2 (i % 4) + 1 of box i / 4
+                unsigned char* brow = slot + (i >> 2) * kBox + r * 128;
+                const int ch = 2 * (i & 3);
+                *reinterpret_cast<uint4*>(brow + ((ch ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                *reinterpret_cast<uint4*>(brow + (((ch + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+              }
+            }
+          }
+          fence_proxy_async();  // generic writes -> visible to the tensor core's reads
+          __syncwarp();
+          if (lane == 0) mbar_arrive(kt ? bar(B_KF + sb) : bar(B_VF + 2 * sb + (use & 1)));
+          jc = j + 1;
+          if (kt) {
+            for (int c = 0; c < 4; ++c) {
+              const int nc = 4 * j + c, ts = g * T_SLOTS + nc % T_SLOTS, tuse = nc / T_SLOTS;
+              if (tuse >= 1 && !wait_all(bar(B_TE + ts), (tuse - 1) & 1)) {
+                ok = false;
+                break;
+              }
+              if (lane == 0) {
+                mbar_expect_tx(bar(B_TF + ts), Lay::TCH_BYTES);
+                tma_load_2d(sbase + Lay::OFF_TAB + ts * Lay::TCH_BYTES, &tm_tab, bar(B_TF + ts), c * 16, row0);
+              }
+              issued_t = nc + 1;
+            }
+          }
+        }
+        if (*s_abort && lane == 0) {  // let every copy already issued land before the CTA can exit
+          for (int jj = jc; jj < ji; ++jj) {
+            const int t = g + NP * jj;
+            mbar_drain(bar(b_st + t % NS), (t / NS) & 1);
+          }
+          for (int nc = max(0, issued_t - T_SLOTS); nc < issued_t; ++nc)
+            mbar_drain(bar(B_TF + g * T_SLOTS + nc % T_SLOTS), (nc / T_SLOTS) & 1);
+        }
+      }
+    } else if (lane == 0 && n_g > 0) {
       if (role == kRoleKT || role == kRoleV) {
         // ---- TMA producers: K tile then its 4 table chunks (KT), or the V tile (V), per group tile.
         const bool kt = role == kRoleKT;

@@ -22,7 +22,7 @@ EXPORTED = ("palu_decode_attn", "palu_decode_attn_static", "palu_decode_attn_pag
             "palu_rope_q_append", "palu_add_rms_norm", "palu_swiglu",
             "palu_workspace_bytes", "palu_choose_splits", "palu_append_latents",
             "palu_plain_gqa_decode", "palu_pack_cs_table", "palu_set_kernel", "palu_kernel_for", "palu_read_status",
-            "palu_set_wait_limit",
+            "palu_set_wait_limit", "palu_decode_attn_f8", "palu_quantize_latents_f8", "palu_append_latents_f8",
             "palu_last_error", "palu_version")
 PALU_KERNEL_AUTO, PALU_KERNEL_MMA, PALU_KERNEL_TC = 0, 1, 2
 
@@ -55,6 +55,12 @@ def load() -> ctypes.CDLL:
     lib.palu_decode_attn.restype = ctypes.c_int
     lib.palu_decode_attn_static.argtypes = [vp, vp, vp, vp, i64, vp, vp, vp, vp, i32, dims_p, f32, vp]
     lib.palu_decode_attn_static.restype = ctypes.c_int
+    lib.palu_decode_attn_f8.argtypes = [vp, vp, vp, vp, vp, vp, i64, vp, vp, vp, vp, i32, vp, sz, dims_p, f32, vp]
+    lib.palu_decode_attn_f8.restype = ctypes.c_int
+    lib.palu_quantize_latents_f8.argtypes = [vp, i64, i32, vp, vp, vp]
+    lib.palu_quantize_latents_f8.restype = ctypes.c_int
+    lib.palu_append_latents_f8.argtypes = [vp, vp, vp, vp, vp, vp, vp, dims_p, vp]
+    lib.palu_append_latents_f8.restype = ctypes.c_int
     pages_p = ctypes.POINTER(PageTable)
     lib.palu_decode_attn_paged.argtypes = [vp, vp, vp, vp, i64, vp, vp, vp, pages_p, vp, i32, vp, sz, dims_p, f32, vp]
     lib.palu_decode_attn_paged.restype = ctypes.c_int

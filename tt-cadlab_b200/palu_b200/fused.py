@@ -200,6 +200,80 @@ def _check_by_default() -> bool:
     return os.environ.get("PALU_CHECK_STATUS", "") not in ("", "0")
 
 
+# ----------------------------------------------------------------------------------------------
+# fp8 latent caches: the B200 form of the reference's block-float latent caches (bfp8_b by default,
+# palu_tt/attention.py:159-169)
+# ----------------------------------------------------------------------------------------------
+
+class F8Latents:
+    """A latent cache held as e4m3 codes plus one power-of-two exponent per row: ``codes`` uint8
+    [..., r], ``exp`` int8 [...] (the codes' leading dims); the cached value is code * 2^exp. The
+    decode op takes a pair of these where it takes bf16 caches (``palu_sdpa_decode``, ``decode``)."""
+
+    __slots__ = ("codes", "exp")
+
+    def __init__(self, codes: torch.Tensor, exp: torch.Tensor):
+        if codes.dtype != torch.uint8 or exp.dtype != torch.int8:
+            raise RuntimeError(f"fp8 latents need uint8 codes and int8 exponents, got {codes.dtype} / {exp.dtype}")
+        if tuple(exp.shape) != tuple(codes.shape[:-1]):
+            raise RuntimeError(f"fp8 latents: exponents {tuple(exp.shape)} must be the codes' leading dims "
+                               f"{tuple(codes.shape[:-1])}")
+        self.codes, self.exp = codes, exp
+
+    @classmethod
+    def empty(cls, *shape, device=None) -> "F8Latents":
+        return cls(torch.zeros(*shape, dtype=torch.uint8, device=device),
+                   torch.zeros(*shape[:-1], dtype=torch.int8, device=device))
+
+    @property
+    def shape(self):
+        return self.codes.shape
+
+    @property
+    def device(self):
+        return self.codes.device
+
+    @property
+    def is_cuda(self) -> bool:
+        return self.codes.is_cuda
+
+    def dim(self) -> int:
+        return self.codes.dim()
+
+    def contiguous(self) -> "F8Latents":
+        return F8Latents(self.codes.contiguous(), self.exp.contiguous())
+
+    def dequantize(self) -> torch.Tensor:
+        """float32 values code * 2^exp (host-side inspection; the decode op reads the codes directly)."""
+        return self.codes.view(torch.float8_e4m3fn).float() * torch.exp2(self.exp.float()).unsqueeze(-1)
+
+
+def quantize_latents_f8(x: torch.Tensor) -> F8Latents:
+    """bf16 latents [..., r] (CUDA) -> F8Latents (palu_quantize_latents_f8): per row, the smallest exponent
+    k with max|row| <= 448 * 2^k (kept in [-120, 7]), codes = row * 2^-k rounded to nearest even e4m3."""
+    _lib.require_cuda(x)
+    xb = _bf16(x).contiguous()
+    r = xb.shape[-1]
+    out = F8Latents.empty(*xb.shape, device=xb.device)
+    _lib.check(_lib.load().palu_quantize_latents_f8(xb.data_ptr(), xb.numel() // r, r, out.codes.data_ptr(),
+                                                    out.exp.data_ptr(), _lib.stream_handle(xb.device)))
+    return out
+
+
+def append_latents_f8(new_k, new_v, cur_pos, k_cache: F8Latents, v_cache: F8Latents) -> None:
+    """Quantize one step's latents [B, n_groups, r] (bf16) into fp8 caches at cur_pos[b]
+    (palu_append_latents_f8); rows with cur_pos outside [0, S) are skipped."""
+    _lib.require_cuda(new_k, new_v, cur_pos, k_cache.codes, v_cache.codes)
+    B, G, S, r_k = k_cache.shape
+    r_v = v_cache.shape[3]
+    d = _lib.dims(B, G, G, G, r_k, r_v, S)
+    nk, nv = _bf16(new_k).contiguous(), _bf16(new_v).contiguous()
+    _lib.check(_lib.load().palu_append_latents_f8(
+        nk.data_ptr(), nv.data_ptr(), cur_pos.to(torch.int32).contiguous().data_ptr(), k_cache.codes.data_ptr(),
+        v_cache.codes.data_ptr(), k_cache.exp.data_ptr(), v_cache.exp.data_ptr(), ctypes.byref(d),
+        _lib.stream_handle(nk.device)))
+
+
 def decode(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, *, u_k_ld=HEAD_DIM, u_v=None, scale=None,
            out=None, out_dtype=torch.bfloat16, splits=0, workspace=None, page_table=None,
            check_status=None, _checked=False) -> torch.Tensor:
@@ -211,10 +285,17 @@ def decode(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, *, u_k_ld=HEAD_DIM, u_
     Paged caches: ``page_table`` [B, blocks per row] int32 and k_latent [n_blocks, n_groups, block_size,
     r_k], v_latent [n_blocks, n_groups, block_size, r_v]; a row then holds blocks per row x block_size
     positions (palu_decode_attn_paged).
+    fp8 caches: k_latent and v_latent as ``F8Latents`` (palu_decode_attn_f8; contiguous caches).
     ``check_status`` (default: the PALU_CHECK_STATUS environment variable) waits for the call and raises
     RuntimeError if a bounded device wait expired, as the reference op raises on a failed run."""
+    f8 = isinstance(k_latent, F8Latents)
+    if f8 != isinstance(v_latent, F8Latents):
+        raise RuntimeError("k_latent and v_latent must both be bf16 or both fp8 (F8Latents)")
+    if f8 and page_table is not None:
+        raise RuntimeError("fp8 latent caches are contiguous (no page table)")
     if not _checked:
-        _lib.require_cuda(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, u_v, page_table)
+        _lib.require_cuda(q, u_k, cs_pairs, cur_pos, u_v, page_table,
+                          *((k_latent.codes, k_latent.exp, v_latent.codes, v_latent.exp) if f8 else (k_latent, v_latent)))
     B, nh = q.shape[0], q.shape[1]
     n_groups, S, r_k = k_latent.shape[1], k_latent.shape[2], k_latent.shape[3]
     r_v = v_latent.shape[3]
@@ -230,7 +311,13 @@ def decode(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, *, u_k_ld=HEAD_DIM, u_
         workspace = _workspace_for(d, q.device, need)
     odt = _lib.PALU_F32 if out.dtype == torch.float32 else _lib.PALU_BF16
     sc = HEAD_DIM ** -0.5 if scale is None else float(scale)
-    if page_table is None:
+    if f8:
+        _lib.check(_lib.load().palu_decode_attn_f8(
+            q.data_ptr(), k_latent.codes.data_ptr(), v_latent.codes.data_ptr(), k_latent.exp.data_ptr(),
+            v_latent.exp.data_ptr(), u_k.data_ptr(), int(u_k_ld), _lib.ptr(u_v), cs_pairs.data_ptr(),
+            cur_pos.data_ptr(), out.data_ptr(), odt, workspace.data_ptr(), workspace.numel(), ctypes.byref(d), sc,
+            _lib.stream_handle(q.device)))
+    elif page_table is None:
         _lib.check(_lib.load().palu_decode_attn(
             q.data_ptr(), k_latent.data_ptr(), v_latent.data_ptr(), u_k.data_ptr(), int(u_k_ld), _lib.ptr(u_v),
             cs_pairs.data_ptr(), cur_pos.data_ptr(), out.data_ptr(), odt, workspace.data_ptr(), workspace.numel(),
@@ -321,9 +408,18 @@ def palu_sdpa_decode(q, k_latent, w_rot, cs_tab, v_latent, head_dim_v, cur_pos_t
         cores = _grid_cores(program_config)
         if h > 1 and cores is not None and B * (n_kv // h) > cores:
             raise RuntimeError(f"heads_per_core {h} needs {B * (n_kv // h)} cores, only {cores} available")
-    if k_latent.dtype != torch.bfloat16 or v_latent.dtype != torch.bfloat16:
-        raise RuntimeError("latent caches must be bf16 (block-float latent formats are not supported)")
-    _lib.require_cuda(q, k_latent, w_rot, cs_tab, v_latent, cur_pos_tensor, u_v)
+    f8 = isinstance(k_latent, F8Latents)
+    if f8 != isinstance(v_latent, F8Latents):
+        raise RuntimeError("k_latent and v_latent must both be bf16 or both fp8 (F8Latents)")
+    if f8:
+        if page_table_tensor is not None:
+            raise RuntimeError("fp8 latent caches are contiguous (no page_table_tensor)")
+        if r_k > 128 or r_v > 128:
+            raise RuntimeError(f"fp8 latent caches: r_k and r_v must be at most 128, got {r_k} / {r_v}")
+    elif k_latent.dtype != torch.bfloat16 or v_latent.dtype != torch.bfloat16:
+        raise RuntimeError("latent caches must be bf16 tensors or fp8 F8Latents")
+    _lib.require_cuda(q, w_rot, cs_tab, cur_pos_tensor, u_v,
+                      *((k_latent.codes, v_latent.codes) if f8 else (k_latent, v_latent)))
     pos = cur_pos_tensor.reshape(-1)
     if pos.numel() != B:
         raise RuntimeError(f"cur_pos_tensor must hold {B} positions, got {pos.numel()}")
