@@ -288,14 +288,20 @@ def run_reference(args, ws, rank):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(W: Workload, ws: int, batch: int, paged: int = 0, shard=None) -> dict:
+def workload_config(W: Workload, ws: int, batch: int, paged: int = 0, shard=None, latent: str = "bf16") -> dict:
     name = W.name if batch == W.batch else re.sub(r"_b\d+_", f"_b{batch}_", W.name)
     extra = {}
+    elem = 2
+    if latent == "f8":
+        name += "_f8"
+        elem = 1
+        extra["cache"] = ("fp8 latent caches: e4m3 codes + one int8 power-of-two exponent per (position, latent "
+                          "head), quantized from the bf16 latents (palu_quantize_latents_f8)")
     if paged:
         name += f"_paged{paged}"
         extra["cache"] = (f"paged: blocks of {paged} positions, each row's blocks a seeded random permutation of "
                           "the physical blocks")
-    lat_bytes = batch * ws * (len(shard.groups) if shard else W.n_groups) * W.seq * (W.r_k + W.r_v) * 2
+    lat_bytes = batch * ws * (len(shard.groups) if shard else W.n_groups) * W.seq * (W.r_k + W.r_v) * elem
     return {"workload": name, **extra, "model": W.model(), "global_batch": batch * ws, "seq_len": W.seq,
             "rank_k": W.r_k, "rank_v": W.r_v, "n_q_heads": N_Q, "n_kv_heads": N_KV, "latent_groups": W.n_groups,
             "kv_heads_per_gpu": N_KV // ws, "latent_replicas": shard.latent_replicas if shard else 1,
@@ -322,6 +328,14 @@ def run_layer(args, ws, rank, local):
     n_kv, n_q, n_g = len(shard.kv), len(shard.q), len(shard.groups)
     L = make_layer(dev, W, B, shard, seed=1234 + rank)
     S = W.seq
+    f8 = args.latent == "f8"
+    if f8:
+        if args.paged:
+            raise SystemExit("--latent f8 runs on contiguous caches (no --paged)")
+        L["k"], L["v"] = fused.quantize_latents_f8(L["k"]), fused.quantize_latents_f8(L["v"])
+        torch.cuda.synchronize()
+    append = fused.append_latents_f8 if f8 else (lambda nk, nv, p_, kc, vc, page_table=None:
+                                                 fused.append_latents(nk, nv, p_, kc, vc, page_table=page_table))
     pt = None
     if args.paged:
         # the same latents, each row's blocks scattered over the physical blocks by a seeded permutation
@@ -401,7 +415,7 @@ def run_layer(args, ws, rank, local):
 
     # ---- plain GQA comparison arm (identity config): the stock flash-decode over the rotated full K ----
     plain_ms = None
-    if W.identity and ws == 1 and not args.paged:
+    if W.identity and ws == 1 and not args.paged and not f8:
         kf = L["k"].float()
         kr = torch.stack([-kf[..., 1::2], kf[..., 0::2]], dim=-1).flatten(-2)
         k_rot = (kf * L["cos"].to(dev) + kr * L["sin"].to(dev)).to(torch.bfloat16)
@@ -447,7 +461,7 @@ def run_layer(args, ws, rank, local):
 
     def plugin_step():
         in_d.copy_(in_h, non_blocking=True)
-        fused.append_latents(nk_d, nv_d, pos_d, L["k"], L["v"], page_table=pt)
+        append(nk_d, nv_d, pos_d, L["k"], L["v"], **({"page_table": pt} if pt is not None else {}))
         o = fused.palu_sdpa_decode(q_d[None], L["k"], L["w_rot"], L["cs_tab"], L["v"], width, pos_d, u_v=u_v4,
                                    scale=HD ** -0.5, **pt_kw)
         torch.mm(o[0].view(B, n_q * width), L["wo"].t(), out=y)
@@ -471,7 +485,7 @@ def run_layer(args, ws, rank, local):
         # the same step without the host wait, captured once as a CUDA graph and replayed back to back
         def graph_body():
             in_d.copy_(in_h, non_blocking=True)
-            fused.append_latents(nk_d, nv_d, pos_d, L["k"], L["v"], page_table=pt)
+            append(nk_d, nv_d, pos_d, L["k"], L["v"], **({"page_table": pt} if pt is not None else {}))
             fused.decode(q_d, L["k"], L["v"], L["u"], L["cs"], pos_d, u_v=L["u_v"], out=out, workspace=ws_buf,
                          page_table=pt)
             torch.mm(out.view(B, n_q * width), L["wo"].t(), out=y)
@@ -499,12 +513,13 @@ def run_layer(args, ws, rank, local):
     d2h = y_h.numel() * y_h.element_size()
 
     # ---- roofline of the decode op on this rank ------------------------------------------------------
-    latent_bytes = B * n_g * S * (W.r_k + W.r_v) * 2
+    # fp8: one byte per code and one exponent byte per cached row of each cache
+    latent_bytes = B * n_g * S * ((W.r_k + W.r_v + 2) if f8 else (W.r_k + W.r_v) * 2)
     u_bytes = n_kv * W.r_k * HD * 2 + (n_kv * W.r_v * HD * 2 if W.grouped else 0)
     alg_bytes = latent_bytes + u_bytes
     achieved = alg_bytes / (op_ms * 1e-3) / 1e9
     peak, peak_kind = peaks()
-    tr = traffic_record(W.name)
+    tr = traffic_record(W.name + ("_f8" if f8 else ""))
     kern = _lib.kernel_for(d)
     kernel_name = ("palu_decode_tc_kernel + palu_combine_tc_kernel" if kern == _lib.PALU_KERNEL_TC
                    else "palu_decode_mma_kernel + palu_combine_kernel")
@@ -519,7 +534,8 @@ def run_layer(args, ws, rank, local):
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, on device)",
-            "config": workload_config(W, ws, b_gpu, args.paged, shard),
+            "config": workload_config(W, ws, b_gpu, args.paged, shard, args.latent),
+            "latent_dtype": "e4m3 + per-row exponent" if f8 else "bf16",
             "us_per_layer": ms * 1e3,
             "parts_us": {"decode_op": op_ms * 1e3, "wo_gemm": gemm_ms * 1e3, "all_reduce": ar_ms * 1e3},
             "all_reduce_share": ar_ms / ms if ms > 0 else None,
@@ -670,6 +686,8 @@ def main():
     ap.add_argument("--prefill-rows", type=int, default=8, help="decoder workload: batch rows per prefill call")
     ap.add_argument("--paged", type=int, default=0, metavar="BLOCK",
                     help="paged caches with blocks of BLOCK positions (0: contiguous caches)")
+    ap.add_argument("--latent", default="bf16", choices=["bf16", "f8"],
+                    help="latent cache format of the layer workload (f8: e4m3 codes + per-row exponent)")
     ap.add_argument("--kernel", default="auto", choices=["auto", "tc", "mma"],
                     help="decode kernel family: tcgen05 (tc), legacy mma.sync (mma) or the library's choice")
     args = ap.parse_args()

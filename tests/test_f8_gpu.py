@@ -1,11 +1,13 @@
 """fp8 latent caches on the GPU: the quantizer and the append against the oracle's format rule bit for bit,
 and the fp8 decode op (palu_decode_attn_f8) against the oracle on the dequantized caches.
 
-The fp8 op rebuilds each cached row's bf16 values exactly (code * 2^k has at most 4 significant bits), so
-on the same dequantized values it must equal the bf16 op bit for bit, and the oracle bar is the bf16
-path's (max-abs relative error <= 2e-2, mean-abs relative error <= 1e-3, fp32 output per row). Against
-the unquantized latents the bar is a PCC, like the reference's block-float test
-(tests/test_palu_sdpa_device.py:558-575: bfp4 latents, PCC >= 0.95); e4m3 rows are held to 0.99.
+The fp8 op converts each staged tile to f16 exactly (every e4m3 code is an f16 value; V rows are scaled by
+their 2^k, K row scales are applied to the scores), reconstructs K against U rounded to f16 and feeds P to
+the PV product as f16 hi + lo. On the dequantized caches it is held to the bf16 path's oracle bar (max-abs
+relative error <= 2e-2, mean-abs relative error <= 1e-3, fp32 output per row) and to within
+F8_VS_BF16 of the bf16 op on the same values. Against the unquantized latents the bar is a PCC, like the
+reference's block-float test (tests/test_palu_sdpa_device.py:558-575: bfp4 latents, PCC >= 0.95); e4m3
+rows are held to 0.99.
 """
 import pytest
 import torch
@@ -20,6 +22,7 @@ THETA = 500000.0
 LLAMA3 = {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
           "original_max_position_embeddings": 8192}
 SCALE = 128 ** -0.5
+F8_VS_BF16 = (5e-3, 2e-4)  # max-abs / mean-abs relative difference of the fp8 and bf16 ops on the same values
 
 
 def _close(out, ref, what):
@@ -123,26 +126,28 @@ def test_fp8_decode_matches_the_oracle_on_the_dequantized_caches(cuda, case):
     kc, vc = fused.quantize_latents_f8(k.to(cuda)), fused.quantize_latents_f8(v.to(cuda))
     kd, vd = f8.dequantize_rows(kc.codes.cpu(), kc.exp.cpu()), f8.dequantize_rows(vc.codes.cpu(), vc.exp.cpu())
     out = _run(cuda, q, kc, vc, u_k, u_v, pos, cos, sin).cpu()
-    # the same values as bf16 caches: the bf16 op gives the same bits
+    # the same values as bf16 caches through the bf16 op
     bf = _run(cuda, q, kd.bfloat16().to(cuda), vd.bfloat16().to(cuda), u_k, u_v, pos, cos, sin).cpu()
-    assert torch.equal(out, bf), f"fp8 and bf16 ops differ by {(out - bf).abs().max():.3e}"
+    mx, mn = rel_errors(out, bf)
+    assert mx <= F8_VS_BF16[0] and mn <= F8_VS_BF16[1], f"fp8 vs bf16 op: max {mx:.3e} mean {mn:.3e}"
     gs = n_kv // G
     ref = oracle.reference_decode(q.float(), oracle.expand_groups(kd, gs), u_k.float(), oracle.expand_groups(vd, gs),
                                   pos, cos, sin, SCALE, u_v=None if u_v is None else u_v.float())
     _close(out, ref, f"fp8 {case}")
 
 
-def test_fp8_equals_bf16_on_rows_of_every_magnitude(cuda):
-    """Rows scaled by e^(N(0, 2^2)) (exponents from about -20 to 7): the fp8 op rebuilds every row's values
-    exactly, so it equals the bf16 op on the dequantized caches bit for bit."""
+def test_fp8_matches_bf16_on_rows_of_every_magnitude(cuda):
+    """Rows scaled by e^(N(0, 2^2)) (exponents from about -20 to 7, V rows below 2^-14 carried as f16
+    subnormals): the fp8 op against the bf16 op on the dequantized caches."""
     from palu_b200 import fused
     q, k, v, u_k, _, pos, cos, sin = _case(44, 3, 8, 8, 1000, 64, 128, spread=2.0)
     kc, vc = fused.quantize_latents_f8(k.to(cuda)), fused.quantize_latents_f8(v.to(cuda))
     assert int(kc.exp.min()) < -14 and int(kc.exp.max()) > 0
     kd, vd = f8.dequantize_rows(kc.codes.cpu(), kc.exp.cpu()), f8.dequantize_rows(vc.codes.cpu(), vc.exp.cpu())
-    out = _run(cuda, q, kc, vc, u_k, None, pos, cos, sin)
-    bf = _run(cuda, q, kd.bfloat16().to(cuda), vd.bfloat16().to(cuda), u_k, None, pos, cos, sin)
-    assert torch.equal(out, bf)
+    out = _run(cuda, q, kc, vc, u_k, None, pos, cos, sin).cpu()
+    bf = _run(cuda, q, kd.bfloat16().to(cuda), vd.bfloat16().to(cuda), u_k, None, pos, cos, sin).cpu()
+    mx, mn = rel_errors(out, bf)
+    assert mx <= 2e-2 and mn <= 1e-3, f"fp8 vs bf16 op: max {mx:.3e} mean {mn:.3e}"
 
 
 def test_fp8_latents_track_the_unquantized_reference(cuda):

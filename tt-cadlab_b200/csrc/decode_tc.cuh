@@ -39,6 +39,7 @@
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 
 #include "palu_common.cuh"
 
@@ -335,14 +336,69 @@ PALU_DEVINL void mma_commit(uint32_t bar) {
 }
 PALU_DEVINL void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 PALU_DEVINL void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
-// fp8 caches: two e4m3 codes at bits 8..15 and 24..31 of x, as the bf16 pair whose sign, exponent and
-// mantissa fields hold the code's: the value times 2^-120 exactly (bf16 and e4m3 share the subnormal
-// structure, and zero stays zero), so a multiply by 2^(120 + k) yields code * 2^k with no rounding.
-PALU_DEVINL uint32_t e4m3_pair_as_bf16x2(uint32_t x) { return ((x >> 4) & 0x07F007F0u) | (x & 0x80008000u); }
-PALU_DEVINL uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
-  const __nv_bfloat162 r =
-      __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&a), *reinterpret_cast<const __nv_bfloat162*>(&b));
-  return *reinterpret_cast<const uint32_t*>(&r);
+// Four e4m3 codes (one 32-bit word, lowest byte first) -> two f16 pairs, exactly (every e4m3 value is an f16
+// value).
+PALU_DEVINL void e4m3x4_to_f16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  asm("{\n .reg .b16 a, b;\n mov.b32 {a, b}, %2;\n cvt.rn.f16x2.e4m3x2 %0, a;\n cvt.rn.f16x2.e4m3x2 %1, b;\n}\n"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
+}
+PALU_DEVINL uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+  const __half2 m = __hmul2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+  return *reinterpret_cast<const uint32_t*>(&m);
+}
+// 16 staged e4m3 codes of one cached row (v) -> codes 16 c .. 16 c + 15 of row r of f16 K-major SWIZZLE_128B
+// box `box` of the tile (its 16-byte chunks 2 c and 2 c + 1), converted exactly and, when SCALED,
+// multiplied by the f16 pair s2 = (2^k, 2^k).
+template <bool SCALED>
+PALU_DEVINL void f8_store_chunk(unsigned char* tile, int r, uint4 v, uint32_t s2, int box, int c) {
+  uint32_t o[8];
+  e4m3x4_to_f16x4(v.x, o[0], o[1]);
+  e4m3x4_to_f16x4(v.y, o[2], o[3]);
+  e4m3x4_to_f16x4(v.z, o[4], o[5]);
+  e4m3x4_to_f16x4(v.w, o[6], o[7]);
+  if constexpr (SCALED) {
+#pragma unroll
+    for (int x = 0; x < 8; ++x) o[x] = hmul2_u32(o[x], s2);
+  }
+  unsigned char* brow = tile + box * kBox + r * 128;
+  *reinterpret_cast<uint4*>(brow + (((2 * c) ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+  *reinterpret_cast<uint4*>(brow + (((2 * c + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+}
+// The f16 pair (2^k, 2^k): normal for k >= -14, subnormal down to 2^-24, 0 below (rows that small hold
+// values under 448 * 2^-25, which the f16 tile cannot carry).
+PALU_DEVINL uint32_t f8_scale_pair(int k) {
+  const uint32_t h = k >= -14 ? (uint32_t)(k + 15) << 10 : (k >= -24 ? 1u << (k + 24) : 0u);
+  return h | (h << 16);
+}
+// One cached row r of an NBOX-box tile converted in place, the codes staged at `stage` (NBOX x 64 per row).
+// One box: f16 row r overlaps staged rows 2 r - 128 and 2 r - 127 (other threads'), so `all_read` must
+// return only once every thread that owns those rows has read them (false: that wait gave up). Two boxes:
+// box 0 lies below the staging half, converted 16 codes at a time; box 1's row r is the staged row r
+// itself, so its 64 codes are read before any is written. Each thread starts at a chunk rotated by its row
+// so that the 8 threads of a shared-memory phase read distinct banks.
+template <int NBOX, bool SCALED, class AllRead>
+PALU_DEVINL bool f8_convert_row(unsigned char* tile, const unsigned char* stage, int r, int k, AllRead all_read) {
+  const uint32_t s2 = SCALED ? f8_scale_pair(k) : 0u;
+  const uint4* src = reinterpret_cast<const uint4*>(stage + r * (NBOX * 64));
+  const int rot = NBOX == 1 ? (r >> 1) : r;
+  if constexpr (NBOX == 1) {
+    uint4 in[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) in[i] = src[(i + rot) & 3];
+    if (!all_read()) return false;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) f8_store_chunk<SCALED>(tile, r, in[i], s2, 0, (i + rot) & 3);
+  } else {
+#pragma unroll 1
+    for (int i = 0; i < 4; ++i) f8_store_chunk<SCALED>(tile, r, src[(i + rot) & 3], s2, 0, (i + rot) & 3);
+    uint4 in[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) in[i] = src[4 + ((i + rot) & 3)];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) f8_store_chunk<SCALED>(tile, r, in[i], s2, 1, (i + rot) & 3);
+  }
+  return true;
 }
 PALU_DEVINL void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 PALU_DEVINL void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
@@ -499,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // V-full barriers are per (slot, use parity), so a parity wait is never more than one phase behind.
   // Drain barriers: [g][QK+PV issuer, reconstruct issuer]. One pipeline: REC[x] marks D_k[x] reconstructed
   // (tiles j with j % 2 == x) and DKF[x] marks it read by RoPE. fp8 caches: ST[slot] marks a slot's e4m3
-  // tile landed in its staging half (K slots, then V slots); KF / VF then mark it converted to bf16.
+  // tile landed in its staging half (K slots, then V slots); KF / VF then mark it converted to f16.
   constexpr int B_KF = 0, B_KE = B_KF + NS_K, B_VF = B_KE + NS_K, B_VE = B_VF + 2 * NS_V, B_TF = B_VE + NS_V,
                 B_TE = B_TF + NS_T, B_UF = B_TE + NS_T, B_REC = B_UF + 1, B_AF = B_REC + 4, B_AE = B_AF + 4,
                 B_SF = B_AE + 2, B_SR = B_SF + 4, B_PF = B_SR + 4, B_OF = B_PF + 4, B_OR = B_OF + 4,
@@ -614,14 +670,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (n_g > 0) {
         // ---- fp8 producers (whole warp). Lane 0 issues the TMA of a tile's e4m3 codes into the upper half of
         // its ring slot, up to the ring's depth ahead; the warp converts each landed tile in place into the
-        // bf16 tile the MMAs read (SWIZZLE_128B K-major boxes of 64 dims), row t multiplied by its power of
-        // two 2^k exactly; the K warp then issues the tile's 4 table chunks (after the conversion, as RoPE of
-        // the previous tile, which frees their slots, waits for it).
+        // f16 tile the MMAs read (SWIZZLE_128B K-major boxes of 64 dims): K codes as they are (their row
+        // scales are applied to the scores), V codes times their row's 2^k. The K warp then issues the
+        // tile's 4 table chunks (after the conversion: RoPE of the previous tile, which frees their slots,
+        // waits for it).
         const bool kt = role == kRoleKT;
         const int NS = kt ? NS_K : NS_V, ring = NS / NP;
         const uint32_t slot_bytes = kt ? Lay::K_BYTES : Lay::V_BYTES, off0 = kt ? Lay::OFF_K : Lay::OFF_V;
-        const int nbox = kt ? KBK : KBV, row8 = nbox * 64;  // bf16 boxes per row; staged bytes per row
-        const int8_t* exps = kt ? p.k_exp : p.v_exp;
+        const int row8 = (kt ? KBK : KBV) * 64;  // staged codes per row
         const CUtensorMap* tm = kt ? &tm_k : &tm_v;
         const int b_st = kt ? B_STK : B_STV;
         if (lane == 0) {
@@ -632,28 +688,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         iss.init(p, seg0, g, n);
         cv.init(p, seg0, g, n);
         int ji = 0, jc = 0, issued_t = 0;
-        bool ok = true;
-        for (int j = 0; ok && j < n_g && cv.valid(); ++j, cv.next(p)) {
-          for (; ji < n_g && ji < j + ring && iss.valid(); ++ji, iss.next(p)) {
-            const int t = g + NP * ji, sb = t % NS, use = t / NS;
-            if (use >= 1 && !wait_all(bar((kt ? B_KE : B_VE) + sb), (use - 1) & 1)) {
-              ok = false;
-              break;
-            }
-            if (lane == 0) {
-              mbar_expect_tx(bar(b_st + sb), row8 * kTile);
-              tma_load_3d(sbase + off0 + sb * slot_bytes + slot_bytes / 2, tm, bar(b_st + sb), 0, iss.tile() * kTile,
-                          iss.s.b * p.n_groups + lat_head);
-            }
+        // The TMA of tile ji into its slot, once the slot's previous tile is consumed. A tile is issued `ring`
+        // tiles ahead, after the conversion of the tile before it, so a conversion starts as soon as its
+        // slot's previous tile is consumed, with its codes already landed.
+        auto issue_next = [&]() -> bool {
+          const int t = g + NP * ji, sb = t % NS, use = t / NS;
+          if (use >= 1 && !wait_all(bar((kt ? B_KE : B_VE) + sb), (use - 1) & 1)) return false;
+          if (lane == 0) {
+            mbar_expect_tx(bar(b_st + sb), row8 * kTile);
+            tma_load_3d(sbase + off0 + sb * slot_bytes + slot_bytes / 2, tm, bar(b_st + sb), 0, iss.tile() * kTile,
+                        iss.s.b * p.n_groups + lat_head);
           }
-          if (!ok) break;
+          ++ji;
+          iss.next(p);
+          return true;
+        };
+        bool ok = true;
+        while (ok && ji < n_g && ji < ring && iss.valid()) ok = issue_next();
+        for (int j = 0; ok && j < n_g && cv.valid(); ++j, cv.next(p)) {
           const int t = g + NP * j, sb = t % NS, use = t / NS, row0 = cv.tile() * kTile;
-          const int8_t* erow = exps + ((size_t)cv.s.b * p.n_groups + lat_head) * p.max_seq;
-          int ex[4];
+          uint32_t ex4 = 0;  // V: the exponents of rows lane, 32 + lane, 64 + lane, 96 + lane, one byte each
+          if (!kt) {
+            const int8_t* erow = p.v_exp + ((size_t)cv.s.b * p.n_groups + lat_head) * p.max_seq;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int pos = row0 + 32 * q + lane;
-            ex[q] = pos < p.max_seq ? __ldg(erow + pos) : 0;
+            for (int q = 0; q < 4; ++q) {
+              const int pos = row0 + 32 * q + lane;
+              ex4 |= (uint32_t)(uint8_t)(pos < p.max_seq ? __ldg(erow + pos) : 0) << (8 * q);
+            }
           }
           if (!wait_all(bar(b_st + sb), use & 1)) {
             ok = false;
@@ -661,33 +722,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           unsigned char* slot = smem + off0 + sb * slot_bytes;
           const unsigned char* stage = slot + slot_bytes / 2;
+          // rows 32 q .. 32 q + 31, one per lane, batch by batch: with 64-code rows the f16 rows of a batch
+          // overlap staged rows of this batch and earlier ones only
+          auto warp_read = [] {
+            __syncwarp();
+            return true;
+          };
 #pragma unroll 1
           for (int q = 0; q < 4; ++q) {
-            // rows 32 q .. 32 q + 31, one per lane. Every lane reads its whole staged row before any lane
-            // writes: the bf16 rows of this batch overlap staged rows of this batch and earlier ones only.
             const int r = 32 * q + lane;
-            uint4 in[2 * 4];
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              if (i < nbox * 4) in[i] = reinterpret_cast<const uint4*>(stage + r * row8)[i];
-            __syncwarp();
-            const uint32_t s1 = (uint32_t)(247 + ex[q]) << 7, s2 = s1 | (s1 << 16);  // bf16 2^(120 + k), twice
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              if (i < nbox * 4) {
-                const uint32_t w[4] = {in[i].x, in[i].y, in[i].z, in[i].w};
-                uint32_t o[8];
-#pragma unroll
-                for (int x = 0; x < 4; ++x) {
-                  o[2 * x] = bf16x2_mul(e4m3_pair_as_bf16x2(__byte_perm(w[x], 0, 0x1404)), s2);
-                  o[2 * x + 1] = bf16x2_mul(e4m3_pair_as_bf16x2(__byte_perm(w[x], 0, 0x3424)), s2);
-                }
-                // elements 16 i .. 16 i + 15 = 16-byte chunks 2 (i % 4) and 2 (i % 4) + 1 of box i / 4
-                unsigned char* brow = slot + (i >> 2) * kBox + r * 128;
-                const int ch = 2 * (i & 3);
-                *reinterpret_cast<uint4*>(brow + ((ch ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-                *reinterpret_cast<uint4*>(brow + (((ch + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
-              }
+            if (kt) {
+              f8_convert_row<KBK, false>(slot, stage, r, 0, warp_read);
+            } else {
+              f8_convert_row<KBV, true>(slot, stage, r, (int)(int8_t)(ex4 >> (8 * q)), warp_read);
             }
           }
           fence_proxy_async();  // generic writes -> visible to the tensor core's reads
@@ -708,6 +755,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               issued_t = nc + 1;
             }
           }
+          if (ok && ji < n_g && iss.valid()) ok = issue_next();
         }
         if (*s_abort && lane == 0) {  // let every copy already issued land before the CTA can exit
           for (int jj = jc; jj < ji; ++jj) {
@@ -839,7 +887,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           constexpr uint32_t ID_QK = idesc_f16(16, 0, false, false);
           // bf16 V^T (MN-major) x bf16 P. A V latent at most 64 wide is one M = 64 block: with M = 128 the
           // MMA read every V row twice (measured 1.6 % faster at the bench workload with M = 64).
-          constexpr uint32_t ID_PV = idesc_f16(16, 1, true, false, KBV == 1 ? 64 : 128);
+          constexpr uint32_t ID_PV = idesc_f16(16, F8 ? 0 : 1, true, false, KBV == 1 ? 64 : 128);  // f16 | bf16
           static_assert(KBV != 1 || NMB == 1, "an M = 64 PV block holds the whole V latent");
           const uint32_t v_lbo = p.rv > 64 ? kBox : 0;  // V: stride between the 64-dim halves of an M = 128 block
           GroupTiles<NP> it, pit;  // QK(j) and PV(j - 1) tiles
@@ -916,7 +964,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           // ---- reconstruct(j + 1) in two halves: D_k columns 64 h .. 64 h + 63 (frequencies 32 h .. + 31) once
           // RoPE(j) has read them, so the reconstruction of one half overlaps the rotation of the other.
-          constexpr uint32_t ID_REC = idesc_f16(64, 1, false, true);  // bf16 lat x bf16 U (MN-major), N = 64
+          // bf16 lat x bf16 U (MN-major), N = 64; f16 x f16 for fp8 caches
+          constexpr uint32_t ID_REC = idesc_f16(64, F8 ? 0 : 1, false, true);
           const uint32_t sU = sbase + Lay::OFF_U;
           const uint32_t u_lbo = p.rk * 128;  // U: stride between the two 64-column N-blocks
           auto recon = [&](int j, int h) -> bool {
@@ -986,10 +1035,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = e >> 3, a = e & 7;
         const uint4* src = reinterpret_cast<const uint4*>(p.u_k + ((size_t)kvh * p.rk + r) * p.ld_u + 16 * a);
         const uint4 x0 = src[0], x1 = src[1];
-        const uint4 ev = make_uint4(__byte_perm(x0.x, x0.y, 0x5410), __byte_perm(x0.z, x0.w, 0x5410),
-                                    __byte_perm(x1.x, x1.y, 0x5410), __byte_perm(x1.z, x1.w, 0x5410));
-        const uint4 od = make_uint4(__byte_perm(x0.x, x0.y, 0x7632), __byte_perm(x0.z, x0.w, 0x7632),
-                                    __byte_perm(x1.x, x1.y, 0x7632), __byte_perm(x1.z, x1.w, 0x7632));
+        uint4 ev = make_uint4(__byte_perm(x0.x, x0.y, 0x5410), __byte_perm(x0.z, x0.w, 0x5410),
+                              __byte_perm(x1.x, x1.y, 0x5410), __byte_perm(x1.z, x1.w, 0x5410));
+        uint4 od = make_uint4(__byte_perm(x0.x, x0.y, 0x7632), __byte_perm(x0.z, x0.w, 0x7632),
+                              __byte_perm(x1.x, x1.y, 0x7632), __byte_perm(x1.z, x1.w, 0x7632));
+        if constexpr (F8) {  // fp8 caches: the reconstruction runs on f16 operands (U rounded to f16)
+          auto h2 = [](uint32_t w) {
+            const float2 f = unpack_bf16(w);
+            return pack_half2(f.x, f.y);
+          };
+          ev = make_uint4(h2(ev.x), h2(ev.y), h2(ev.z), h2(ev.w));
+          od = make_uint4(h2(od.x), h2(od.y), h2(od.z), h2(od.w));
+        }
         unsigned char* urow = smem + Lay::OFF_U + (a >> 2) * p.rk * 128 + r * 128;
         *reinterpret_cast<uint4*>(urow + (((a & 3) ^ (r & 7)) << 4)) = ev;
         *reinterpret_cast<uint4*>(urow + (((4 + (a & 3)) ^ (r & 7)) << 4)) = od;
@@ -1158,6 +1215,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           // ---- softmax(j) -------------------------------------------------------------------------------
           if (x < cnt) {
             const int j = j0 + x;
+            // fp8 caches: K rows were rebuilt from their codes, so the score of row t carries its row scale
+            // 2^k (RoPE and the dot product are linear in the row), applied here with the softmax scale
+            float sl2 = p.scale_log2;
+            if constexpr (F8) {
+              const int kpos = (sg.ta + (kf - sg.kb) + NP * x) * kTile + row;
+              if (kpos < p.max_seq)
+                sl2 = ldexpf(sl2, __ldg(p.k_exp + ((size_t)sg.b * p.n_groups + lat_head) * p.max_seq + kpos));
+            }
             if (!wait_all(bar(B_SF + 2 * g + (j & 1)), (j >> 1) & 1)) {
               ok = false;
               break;
@@ -1174,7 +1239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float xs[4], mx[4];
 #pragma unroll
             for (int h = 0; h < 4; ++h) {
-              xs[h] = (valid && h < p.rep) ? __uint_as_float(sc[h]) * p.scale_log2 : -INFINITY;
+              xs[h] = (valid && h < p.rep) ? __uint_as_float(sc[h]) * sl2 : -INFINITY;
               mx[h] = warp_max(xs[h]);
             }
             // The 4 warps' maxima meet through a double-buffered mbarrier (bounded wait, unlike bar.sync).
@@ -1201,6 +1266,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 alpha0[h] = alpha;
               l_run[h] = l_run[h] * alpha + pv;
               m_run[h] = m_new;
+              if constexpr (F8) {  // P as f16 hi + lo (the V tile is f16)
+                const __half hi = __float2half_rn(pv);
+                const __half lo = __float2half_rn(pv - __half2float(hi));
+                *reinterpret_cast<__half*>(sP + sw128_offset(h, row, 16)) = hi;
+                *reinterpret_cast<__half*>(sP + sw128_offset(4 + h, row, 16)) = lo;
+                continue;
+              }
               const __nv_bfloat16 hi = __float2bfloat16_rn(pv);
               const __nv_bfloat16 lo = __float2bfloat16_rn(pv - __bfloat162float(hi));
               *reinterpret_cast<__nv_bfloat16*>(sP + sw128_offset(h, row, 16)) = hi;
