@@ -116,13 +116,31 @@ def ptr(t) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_handle(device: torch.device) -> int:
+    """The raw handle of the current stream on ``device`` (the decode step's host path calls this every
+    step: the direct lookup costs well under a microsecond, torch.cuda.current_stream several)."""
+    if _RAW_STREAM is not None:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        return _RAW_STREAM(idx)
     return torch.cuda.current_stream(device).cuda_stream
 
 
+_DIMS_CACHE: dict = {}
+
+
 def dims(batch, n_q, n_kv, n_groups, r_k, r_v, max_seq, splits=0) -> DecodeDims:
-    return DecodeDims(int(batch), int(n_q), int(n_kv), int(n_groups), 128, int(r_k), int(r_v), int(max_seq),
-                      int(splits))
+    """The DecodeDims of a shape, built once per shape (the library only reads it)."""
+    key = (batch, n_q, n_kv, n_groups, r_k, r_v, max_seq, splits)
+    d = _DIMS_CACHE.get(key)
+    if d is None:
+        if len(_DIMS_CACHE) > 256:
+            _DIMS_CACHE.clear()
+        d = _DIMS_CACHE[key] = DecodeDims(int(batch), int(n_q), int(n_kv), int(n_groups), 128, int(r_k), int(r_v),
+                                          int(max_seq), int(splits))
+    return d
 
 
 def pages(table: torch.Tensor, block_size: int, n_blocks: int) -> PageTable:
@@ -133,8 +151,18 @@ def pages(table: torch.Tensor, block_size: int, n_blocks: int) -> PageTable:
     return PageTable(table.data_ptr(), int(table.stride(0)), int(block_size), int(n_blocks))
 
 
+_WSB_CACHE: dict = {}
+
+
 def workspace_bytes(d: DecodeDims) -> int:
-    return int(load().palu_workspace_bytes(ctypes.byref(d)))
+    """palu_workspace_bytes(d), cached per shape and kernel choice (set_kernel can change it)."""
+    key = (d.batch, d.n_q_heads, d.n_kv_heads, d.n_groups, d.r_k, d.r_v, d.max_seq, d.splits, _KERNEL[0])
+    n = _WSB_CACHE.get(key)
+    if n is None:
+        if len(_WSB_CACHE) > 256:
+            _WSB_CACHE.clear()
+        n = _WSB_CACHE[key] = int(load().palu_workspace_bytes(ctypes.byref(d)))
+    return n
 
 
 def new_workspace(d: DecodeDims, device) -> torch.Tensor:
@@ -146,9 +174,13 @@ def choose_splits(d: DecodeDims) -> int:
     return int(load().palu_choose_splits(ctypes.byref(d)))
 
 
+_KERNEL = [PALU_KERNEL_AUTO]
+
+
 def set_kernel(which: int) -> None:
     """Choose the decode kernel family (PALU_KERNEL_AUTO / _MMA / _TC) for this process."""
     check(load().palu_set_kernel(int(which)))
+    _KERNEL[0] = int(which)
 
 
 def set_wait_limit(wait_ns: int = 0, starve_v: bool = False) -> None:
