@@ -389,12 +389,25 @@ def run_layer(args, ws, rank, local):
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     with ClockSampler(local) as clk:
         # The timed region can be a few ms, shorter than nvidia-smi's 200 ms sampling period, so the
-        # sampler also covers a soak of the same step (same load, untimed) right before it.
-        soak_end = time.perf_counter() + args.clock_soak
-        while time.perf_counter() < soak_end:
-            for _ in range(20):
+        # sampler also covers a soak of the same step (same load, untimed) right before it. Every rank runs
+        # the same number of soak steps (each step holds a collective at N > 1): sized from 5 steps' wall
+        # time, the largest count over ranks.
+        n_soak = 0
+        if args.clock_soak > 0:
+            torch.cuda.synchronize()
+            t_s = time.perf_counter()
+            for _ in range(5):
                 step()
             torch.cuda.synchronize()
+            per_step = max((time.perf_counter() - t_s) / 5, 1e-6)
+            n = torch.tensor([float(min(100000, int(args.clock_soak / per_step) + 1))], device=dev)
+            if ws > 1:
+                dist.all_reduce(n, op=dist.ReduceOp.MAX)
+            n_soak = int(n.item())
+        for i in range(n_soak):
+            step()
+            if i % 20 == 19:
+                torch.cuda.synchronize()
         barrier()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
