@@ -297,11 +297,16 @@ def workload_config(W: Workload, ws: int, batch: int, paged: int = 0, shard=None
         elem = 1
         extra["cache"] = ("fp8 latent caches: e4m3 codes + one int8 power-of-two exponent per (position, latent "
                           "head), quantized from the bf16 latents (palu_quantize_latents_f8)")
+    elif latent == "f4":
+        name += "_f4"
+        elem = 0.5
+        extra["cache"] = ("fp4 latent caches: e2m1 codes, two per byte, + one int8 power-of-two exponent per 16 "
+                          "values, quantized from the bf16 latents (palu_quantize_latents_f4)")
     if paged:
         name += f"_paged{paged}"
         extra["cache"] = (f"paged: blocks of {paged} positions, each row's blocks a seeded random permutation of "
                           "the physical blocks")
-    lat_bytes = batch * ws * (len(shard.groups) if shard else W.n_groups) * W.seq * (W.r_k + W.r_v) * elem
+    lat_bytes = int(batch * ws * (len(shard.groups) if shard else W.n_groups) * W.seq * (W.r_k + W.r_v) * elem)
     return {"workload": name, **extra, "model": W.model(), "global_batch": batch * ws, "seq_len": W.seq,
             "rank_k": W.r_k, "rank_v": W.r_v, "n_q_heads": N_Q, "n_kv_heads": N_KV, "latent_groups": W.n_groups,
             "kv_heads_per_gpu": N_KV // ws, "latent_replicas": shard.latent_replicas if shard else 1,
@@ -328,11 +333,12 @@ def run_layer(args, ws, rank, local):
     n_kv, n_q, n_g = len(shard.kv), len(shard.q), len(shard.groups)
     L = make_layer(dev, W, B, shard, seed=1234 + rank)
     S = W.seq
-    f8 = args.latent == "f8"
+    f8 = args.latent in ("f8", "f4")
     if f8:
         if args.paged:
-            raise SystemExit("--latent f8 runs on contiguous caches (no --paged)")
-        L["k"], L["v"] = fused.quantize_latents_f8(L["k"]), fused.quantize_latents_f8(L["v"])
+            raise SystemExit("--latent f8 / f4 run on contiguous caches (no --paged)")
+        quant = fused.quantize_latents_f4 if args.latent == "f4" else fused.quantize_latents_f8
+        L["k"], L["v"] = quant(L["k"]), quant(L["v"])
         torch.cuda.synchronize()
     append = fused.append_latents_f8 if f8 else (lambda nk, nv, p_, kc, vc, page_table=None:
                                                  fused.append_latents(nk, nv, p_, kc, vc, page_table=page_table))
@@ -526,13 +532,17 @@ def run_layer(args, ws, rank, local):
     d2h = y_h.numel() * y_h.element_size()
 
     # ---- roofline of the decode op on this rank ------------------------------------------------------
-    # fp8: one byte per code and one exponent byte per cached row of each cache
-    latent_bytes = B * n_g * S * ((W.r_k + W.r_v + 2) if f8 else (W.r_k + W.r_v) * 2)
+    # fp8: one byte per code and one exponent byte per cached row of each cache; fp4: half a byte per code
+    # and one exponent byte per 16 codes
+    if args.latent == "f4":
+        latent_bytes = B * n_g * S * ((W.r_k + W.r_v) // 2 + (W.r_k + W.r_v) // 16)
+    else:
+        latent_bytes = B * n_g * S * ((W.r_k + W.r_v + 2) if f8 else (W.r_k + W.r_v) * 2)
     u_bytes = n_kv * W.r_k * HD * 2 + (n_kv * W.r_v * HD * 2 if W.grouped else 0)
     alg_bytes = latent_bytes + u_bytes
     achieved = alg_bytes / (op_ms * 1e-3) / 1e9
     peak, peak_kind = peaks()
-    tr = traffic_record(W.name + ("_f8" if f8 else ""))
+    tr = traffic_record(W.name + ("_" + args.latent if f8 else ""))
     kern = _lib.kernel_for(d)
     kernel_name = ("palu_decode_tc_kernel + palu_combine_tc_kernel" if kern == _lib.PALU_KERNEL_TC
                    else "palu_decode_mma_kernel + palu_combine_kernel")
@@ -548,7 +558,7 @@ def run_layer(args, ws, rank, local):
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, on device)",
             "config": workload_config(W, ws, b_gpu, args.paged, shard, args.latent),
-            "latent_dtype": "e4m3 + per-row exponent" if f8 else "bf16",
+            "latent_dtype": {"f8": "e4m3 + per-row exponent", "f4": "e2m1 + per-16 exponent"}.get(args.latent, "bf16"),
             "us_per_layer": ms * 1e3,
             "parts_us": {"decode_op": op_ms * 1e3, "wo_gemm": gemm_ms * 1e3, "all_reduce": ar_ms * 1e3},
             "all_reduce_share": ar_ms / ms if ms > 0 else None,
@@ -699,8 +709,9 @@ def main():
     ap.add_argument("--prefill-rows", type=int, default=8, help="decoder workload: batch rows per prefill call")
     ap.add_argument("--paged", type=int, default=0, metavar="BLOCK",
                     help="paged caches with blocks of BLOCK positions (0: contiguous caches)")
-    ap.add_argument("--latent", default="bf16", choices=["bf16", "f8"],
-                    help="latent cache format of the layer workload (f8: e4m3 codes + per-row exponent)")
+    ap.add_argument("--latent", default="bf16", choices=["bf16", "f8", "f4"],
+                    help="latent cache format of the layer workload (f8: e4m3 codes + per-row exponent; "
+                         "f4: e2m1 codes + per-16 exponent)")
     ap.add_argument("--kernel", default="auto", choices=["auto", "tc", "mma"],
                     help="decode kernel family: tcgen05 (tc), legacy mma.sync (mma) or the library's choice")
     args = ap.parse_args()

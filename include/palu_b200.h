@@ -37,6 +37,9 @@
  *                             (bfp8_b by default, bfp4_b per side: palu_tt/attention.py:159-169;
  *                             tests/test_palu_sdpa_device.py:558-575), in the B200 form: e4m3 codes with
  *                             one power-of-two scale per (position, latent head).
+ *   palu_decode_attn_f4 / palu_append_latents_f4 / palu_quantize_latents_f4
+ *                          <- the same over bfp4_b latent caches, in the B200 form: e2m1 codes with one
+ *                             power-of-two scale per block of 16 values.
  */
 #ifndef PALU_B200_H
 #define PALU_B200_H
@@ -172,6 +175,23 @@ int palu_quantize_latents_f8(const void* latents, int64_t rows, int32_t r, void*
 /* palu_append_latents into fp8 caches: new_k [B][n_groups][r_k], new_v [B][n_groups][r_v] bf16 quantized
  * row by row into position cur_pos[b]; rows with cur_pos outside [0, max_seq) are skipped. */
 int palu_append_latents_f8(const void* new_k, const void* new_v, const int32_t* cur_pos, void* k_codes, void* v_codes,
+                           int8_t* k_exp, int8_t* v_exp, const palu_decode_dims* dims, palu_stream_t stream);
+
+/*
+ * fp4 latent caches. k_codes [B][n_groups][max_seq][r_k / 2] and v_codes [...][r_v / 2] hold two e2m1 codes per
+ * byte (the first value in the low nibble), k_exp [B][n_groups][max_seq][r_k / 16] and v_exp [...][r_v / 16]
+ * int8 the exponent k of each block of 16 values: the cached value is code * 2^k. k is the smallest integer
+ * with max|block| <= 6 * 2^k, kept in [-120, 7] (0 for an all-zero block); the codes round to nearest even
+ * with saturation. palu_decode_attn_f4 is palu_decode_attn over such caches, envelope r_k, r_v in {64, 128},
+ * contiguous caches, the tcgen05 kernel; the others as their fp8 counterparts (r a multiple of 16).
+ */
+int palu_decode_attn_f4(const void* q, const void* k_codes, const void* v_codes, const int8_t* k_exp,
+                        const int8_t* v_exp, const void* u_k, int64_t u_k_ld, const void* u_v, const void* cs_pairs,
+                        const int32_t* cur_pos, void* out, int32_t out_dtype, void* workspace, size_t workspace_bytes,
+                        const palu_decode_dims* dims, float scale, palu_stream_t stream);
+int palu_quantize_latents_f4(const void* latents, int64_t rows, int32_t r, void* codes, int8_t* exps,
+                             palu_stream_t stream);
+int palu_append_latents_f4(const void* new_k, const void* new_v, const int32_t* cur_pos, void* k_codes, void* v_codes,
                            int8_t* k_exp, int8_t* v_exp, const palu_decode_dims* dims, palu_stream_t stream);
 
 /*

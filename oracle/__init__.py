@@ -31,5 +31,5 @@ from oracle.palu_ref import (  # noqa: F401
     input_checksums,
 )
 from oracle.metrics import rel_errors, rowwise_rel_errors  # noqa: F401
-from oracle import f8  # noqa: F401
+from oracle import f4, f8  # noqa: F401
 from oracle.paged import paged_append, paged_gather, paged_scatter, shuffled_page_table  # noqa: F401

@@ -86,3 +86,36 @@ def test_fp8_caches_through_the_reference_surface_are_checked():
         fused.palu_sdpa_decode(q, k, w, cs, fused.F8Latents.empty(2, 8, 256, 64), 64, pos)
     with pytest.raises(RuntimeError, match="leading dims"):
         fused.F8Latents(torch.zeros(2, 4, dtype=torch.uint8), torch.zeros(3, dtype=torch.int8))
+
+
+def test_fp4_block_exponents_and_rounding():
+    """The e2m1 rule (oracle/f4.py): the smallest exponent that fits 6 * 2^k, nearest code with ties to
+    the even code, saturation at 6."""
+    from oracle import f4
+    g = torch.Generator().manual_seed(6)
+    amax = torch.exp(torch.randn(20000, generator=g) * 6)
+    k = f4.block_exponents(amax).double()
+    inside = (k > f4.K_MIN) & (k < f4.K_MAX)
+    a = amax.double()
+    assert torch.all(a[inside] <= 6 * torch.exp2(k[inside]))
+    assert torch.all(a[inside] > 6 * torch.exp2(k[inside] - 1))
+    # one block scaled by 2^1 (max 7): ties go to the even code
+    x = torch.tensor([[0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 7.0, -0.25, -0.75, 0, 0, 0, 0, 0, 6.0]])
+    codes, exp = f4.quantize_rows(x)
+    assert exp.item() == 1
+    want = torch.tensor([[0.0, 1.0, 1.0, 2.0, 2.0, 4.0, 4.0, 8.0, -0.0, -1.0, 0, 0, 0, 0, 0, 6.0]])
+    assert torch.equal(f4.dequantize_rows(codes, exp), want)
+    assert codes.shape == (1, 8) and (codes[0, 0] & 15).item() == 0 and (codes[0, 0] >> 4).item() == 1
+
+
+def test_fp4_round_trip_within_e2m1_precision():
+    from oracle import f4
+    g = torch.Generator().manual_seed(7)
+    x = (torch.randn(2048, 128, generator=g) * torch.exp(torch.randn(2048, 1, generator=g))).bfloat16()
+    codes, exp = f4.quantize_rows(x)
+    assert codes.shape == (2048, 64) and exp.shape == (2048, 8)
+    d, xf = f4.dequantize_rows(codes, exp), x.float()
+    step = torch.exp2(exp.float()).repeat_interleave(16, dim=-1)
+    # e2m1 spacing is at most 2 (between 4 and 6) in units of 2^k: half a step is at most 1
+    assert torch.all((d - xf).abs() <= step * (1 + 1e-6))
+    assert torch.all(d.abs() <= 6 * step)

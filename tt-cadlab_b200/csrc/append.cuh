@@ -13,8 +13,13 @@
 //    amax <= 448 * 2^k (448 = the largest e4m3 value), kept in [-120, 7]; scaling by 2^-k is exact, the codes
 //    round to nearest even with saturation, and codes below the smallest normal e4m3 value (exponent
 //    field 0) are flushed to a signed zero, so every stored code converts to bf16 by moving bit fields.
+//  * palu_quantize_f4_kernel: fp4 latent caches (the B200 form of the reference's bfp4 latent caches): e2m1
+//    codes, two per byte (the first value in the low nibble), with one power-of-two exponent per block of 16
+//    values: k is the smallest integer with max|block| <= 6 * 2^k (6 = the largest e2m1 value), kept in
+//    [-120, 7]; the codes are the block times 2^-k rounded to nearest even with saturation.
 #pragma once
 #include <cuda_fp16.h>
+#include <cuda_fp4.h>
 #include <cuda_fp8.h>
 
 #include "palu_common.cuh"
@@ -140,6 +145,56 @@ __global__ void palu_quantize_f8_kernel(const QuantF8Params p) {
       if (d < p.r) p.codes[dst * p.r + d] = f8_code(ldexpf(x[c], -k));
     }
     if (lane == 0) p.exps[dst] = (int8_t)k;
+  }
+}
+
+// ---- fp4 latent rows -----------------------------------------------------------------------------------
+struct QuantF4Params {
+  const __nv_bfloat16* src;  // rows of r bf16 values
+  long rows;
+  int r;                     // values per row: a multiple of 16, <= 256
+  uint8_t* codes;            // destination rows of r / 2 bytes
+  int8_t* exps;              // destination rows of r / 16 block exponents
+  const int32_t* cur_pos;    // append mode, as QuantF8Params
+  int n_groups, max_seq;
+};
+
+// amax = m * 2^e, m in [0.5, 1): 6 * 2^k = 0.75 * 2^(k + 3), so k = e - 3 when m <= 0.75, else e - 2.
+PALU_DEVINL int f4_block_exponent(float amax) {
+  if (!(amax > 0.f)) return 0;
+  int e;
+  const float m = frexpf(amax, &e);
+  const int k = m <= 0.75f ? e - 3 : e - 2;
+  return k > 7 ? 7 : (k < -120 ? -120 : k);
+}
+
+// One warp per row: lane l holds the value pairs 2 (l + 32 c), 2 (l + 32 c) + 1; a block of 16 values is 8 lanes.
+__global__ void palu_quantize_f4_kernel(const QuantF4Params p) {
+  const int lane = threadIdx.x & 31;
+  const long warps = (long)gridDim.x * (blockDim.x >> 5);
+  for (long i = blockIdx.x * (long)(blockDim.x >> 5) + (threadIdx.x >> 5); i < p.rows; i += warps) {
+    long dst = i;
+    if (p.cur_pos) {
+      const int pos = p.cur_pos[i / p.n_groups];
+      if (pos < 0 || pos >= p.max_seq) continue;
+      dst = i * p.max_seq + pos;
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int pr = lane + 32 * c, d0 = 2 * pr;  // value pair index, first value
+      const bool in = d0 < p.r;
+      const float x0 = in ? __bfloat162float(p.src[i * p.r + d0]) : 0.f;
+      const float x1 = in ? __bfloat162float(p.src[i * p.r + d0 + 1]) : 0.f;
+      float amax = fmaxf(fabsf(x0), fabsf(x1));
+#pragma unroll
+      for (int o = 4; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const int k = f4_block_exponent(amax);
+      if (in) {
+        p.codes[dst * (p.r / 2) + pr] = (uint8_t)__nv_cvt_float2_to_fp4x2(make_float2(ldexpf(x0, -k), ldexpf(x1, -k)),
+                                                                          __NV_E2M1, cudaRoundNearest);
+        if ((lane & 7) == 0) p.exps[dst * (p.r / 16) + (pr >> 3)] = (int8_t)k;
+      }
+    }
   }
 }
 

@@ -39,6 +39,7 @@
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
+#include <cuda_fp4.h>
 #include <cuda_fp8.h>
 
 #include "palu_common.cuh"
@@ -91,7 +92,8 @@ struct TcParams {
   int pdl_early;
   // fp8 latent caches (the F8 kernels): e4m3 codes in the caches above, and per (batch row, latent head,
   // position) the power-of-two exponent k of the row's scale, [B][n_groups][max_seq] int8 each; a cached
-  // value is code * 2^k.
+  // value is code * 2^k. fp4 caches (F8 and F4): e2m1 codes, two per byte (the first in the low nibble),
+  // and one exponent per 16 values of a row, [B][n_groups][max_seq][r / 16].
   const int8_t* k_exp;
   const int8_t* v_exp;
 };
@@ -400,6 +402,38 @@ PALU_DEVINL bool f8_convert_row(unsigned char* tile, const unsigned char* stage,
   }
   return true;
 }
+// fp4: 16 staged e2m1 codes of one row (v: 8 bytes, the first code of each byte in its low nibble) ->
+// codes 16 c .. 16 c + 15 of row r of f16 box `box` (chunks 2 c, 2 c + 1), converted exactly and multiplied by
+// the block's f16 pair s2 = (2^k, 2^k).
+PALU_DEVINL void f4_store_chunk(unsigned char* tile, int r, uint2 v, uint32_t s2, int box, int c) {
+  uint32_t o[8];
+#pragma unroll
+  for (int x = 0; x < 8; ++x) {
+    const uint32_t w = x < 4 ? v.x : v.y;
+    const __half2_raw h = __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)((w >> (8 * (x & 3))) & 0xFFu), __NV_E2M1);
+    o[x] = hmul2_u32((uint32_t)h.x | ((uint32_t)h.y << 16), s2);
+  }
+  unsigned char* brow = tile + box * kBox + r * 128;
+  *reinterpret_cast<uint4*>(brow + (((2 * c) ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+  *reinterpret_cast<uint4*>(brow + (((2 * c + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+}
+// One fp4 row r of an NBOX-box tile converted in place: staged at `stage`, NBOX x 32 bytes per row, with the
+// staged tile at the end of the slot. f16 rows of 32-row batches 0..2 lie below the staging area; batch 3's
+// overlap staged rows of every batch, this one's included, so `all_read` returns once every thread of the warp
+// has read its staged row. e8: the row's NBOX x 4 block exponents, one byte each.
+template <int NBOX, class AllRead>
+PALU_DEVINL bool f4_convert_row(unsigned char* tile, const unsigned char* stage, int r, const uint32_t (&e8)[2],
+                                AllRead all_read) {
+  const uint2* src = reinterpret_cast<const uint2*>(stage + r * (NBOX * 32));
+  uint2 in[NBOX * 4];
+#pragma unroll
+  for (int i = 0; i < NBOX * 4; ++i) in[i] = src[i];
+  if (!all_read()) return false;
+#pragma unroll
+  for (int i = 0; i < NBOX * 4; ++i)
+    f4_store_chunk(tile, r, in[i], f8_scale_pair((int)(int8_t)(e8[i >> 2] >> (8 * (i & 3)))), i >> 2, i & 3);
+  return true;
+}
 PALU_DEVINL void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 PALU_DEVINL void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 PALU_DEVINL void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
@@ -525,11 +559,12 @@ PALU_DEVINL int role_of(int warp) {
 // PAGED: the caches are paged (TcParams.page_table set). A template parameter rather than a runtime branch,
 // so that the contiguous-cache kernel carries none of the paged producers' code: with it the body fit the
 // instruction cache worse, and dropping it measured 2-4 % faster on B200.
-template <int KBK, int KBV, bool PAGED, int NP, bool F8 = false>
+template <int KBK, int KBV, bool PAGED, int NP, bool F8 = false, bool F4 = false>
 __global__ void __launch_bounds__(kThreads, 1)
     palu_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                           const __grid_constant__ CUtensorMap tm_tab, const TcParams p) {
   static_assert(!F8 || (NP == 2 && !PAGED), "fp8 latent caches: contiguous caches, latents at most 128 wide");
+  static_assert(!F4 || F8, "fp4 caches run the low-bit producers of the F8 kernels");
   using Lay = Layout<KBK, KBV, NP>;
   constexpr int NS_K = Lay::NS_K, NS_V = Lay::NS_V, T_SLOTS = Lay::T_SLOTS;
   constexpr int NS_T = NP * T_SLOTS;  // table chunk slots, [group][slot]
@@ -677,7 +712,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool kt = role == kRoleKT;
         const int NS = kt ? NS_K : NS_V, ring = NS / NP;
         const uint32_t slot_bytes = kt ? Lay::K_BYTES : Lay::V_BYTES, off0 = kt ? Lay::OFF_K : Lay::OFF_V;
-        const int row8 = (kt ? KBK : KBV) * 64;  // staged codes per row
+        const int row8 = (kt ? KBK : KBV) * (F4 ? 32 : 64);        // staged bytes per row
+        const uint32_t stage_off = slot_bytes - (uint32_t)row8 * kTile;  // the staged tile ends the slot
         const CUtensorMap* tm = kt ? &tm_k : &tm_v;
         const int b_st = kt ? B_STK : B_STV;
         if (lane == 0) {
@@ -696,7 +732,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (use >= 1 && !wait_all(bar((kt ? B_KE : B_VE) + sb), (use - 1) & 1)) return false;
           if (lane == 0) {
             mbar_expect_tx(bar(b_st + sb), row8 * kTile);
-            tma_load_3d(sbase + off0 + sb * slot_bytes + slot_bytes / 2, tm, bar(b_st + sb), 0, iss.tile() * kTile,
+            tma_load_3d(sbase + off0 + sb * slot_bytes + stage_off, tm, bar(b_st + sb), 0, iss.tile() * kTile,
                         iss.s.b * p.n_groups + lat_head);
           }
           ++ji;
@@ -708,7 +744,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; ok && j < n_g && cv.valid(); ++j, cv.next(p)) {
           const int t = g + NP * j, sb = t % NS, use = t / NS, row0 = cv.tile() * kTile;
           uint32_t ex4 = 0;  // V: the exponents of rows lane, 32 + lane, 64 + lane, 96 + lane, one byte each
-          if (!kt) {
+          if (!kt && !F4) {
             const int8_t* erow = p.v_exp + ((size_t)cv.s.b * p.n_groups + lat_head) * p.max_seq;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
@@ -721,7 +757,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           unsigned char* slot = smem + off0 + sb * slot_bytes;
-          const unsigned char* stage = slot + slot_bytes / 2;
+          const unsigned char* stage = slot + stage_off;
           // rows 32 q .. 32 q + 31, one per lane, batch by batch: with 64-code rows the f16 rows of a batch
           // overlap staged rows of this batch and earlier ones only
           auto warp_read = [] {
@@ -731,7 +767,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
           for (int q = 0; q < 4; ++q) {
             const int r = 32 * q + lane;
-            if (kt) {
+            if constexpr (F4) {
+              // fp4: the row's block exponents (r / 16 of them), then the row
+              const int nb = kt ? KBK : KBV, pos = row0 + r;
+              const int8_t* ep = (kt ? p.k_exp : p.v_exp) +
+                                 (((size_t)cv.s.b * p.n_groups + lat_head) * p.max_seq + pos) * (nb * 4);
+              uint32_t e8[2] = {0u, 0u};
+              if (pos < p.max_seq) {
+                e8[0] = __ldg(reinterpret_cast<const uint32_t*>(ep));
+                if (nb == 2) e8[1] = __ldg(reinterpret_cast<const uint32_t*>(ep) + 1);
+              }
+              if (kt) f4_convert_row<KBK>(slot, stage, r, e8, warp_read);
+              else f4_convert_row<KBV>(slot, stage, r, e8, warp_read);
+            } else if (kt) {
               f8_convert_row<KBK, false>(slot, stage, r, 0, warp_read);
             } else {
               f8_convert_row<KBV, true>(slot, stage, r, (int)(int8_t)(ex4 >> (8 * q)), warp_read);
@@ -1218,7 +1266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // fp8 caches: K rows were rebuilt from their codes, so the score of row t carries its row scale
             // 2^k (RoPE and the dot product are linear in the row), applied here with the softmax scale
             float sl2 = p.scale_log2;
-            if constexpr (F8) {
+            if constexpr (F8 && !F4) {
               const int kpos = (sg.ta + (kf - sg.kb) + NP * x) * kTile + row;
               if (kpos < p.max_seq)
                 sl2 = ldexpf(sl2, __ldg(p.k_exp + ((size_t)sg.b * p.n_groups + lat_head) * p.max_seq + kpos));

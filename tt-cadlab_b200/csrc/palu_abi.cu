@@ -199,11 +199,11 @@ void set_pages(Params& p, const palu_page_table* pg) {
   while (pg && (1 << p.blk_shift) < pg->block_size) ++p.blk_shift;
 }
 
-template <int KBK, int KBV, bool PAGED, int NP = 2, bool F8 = false>
+template <int KBK, int KBV, bool PAGED, int NP = 2, bool F8 = false, bool F4 = false>
 int launch_tc(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mt, const palu::tc::TcParams& p,
               cudaStream_t stream) {
   using Lay = palu::tc::Layout<KBK, KBV, NP>;
-  auto kern = palu::tc::palu_decode_tc_kernel<KBK, KBV, PAGED, NP, F8>;
+  auto kern = palu::tc::palu_decode_tc_kernel<KBK, KBV, PAGED, NP, F8, F4>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::TOTAL) != cudaSuccess)
     return cuda_check("cudaFuncSetAttribute(decode tc)");
   kern<<<dim3(p.ctas, p.n_kv, 1), palu::tc::kThreads, Lay::TOTAL, stream>>>(mk, mv, mt, p);
@@ -213,7 +213,7 @@ int launch_tc(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& m
 int run_tc(const void* q, const void* k, const void* v, const void* u_k, int64_t u_k_ld, const void* cs_pairs,
            const int32_t* cur_pos, void* workspace, float* ws_o, float* ws_ml, const palu_decode_dims* d, int splits,
            float scale, const palu_page_table* pg, cudaStream_t stream, const int8_t* k_exp = nullptr,
-           const int8_t* v_exp = nullptr) {
+           const int8_t* v_exp = nullptr, bool f4 = false) {
   const bool f8 = k_exp != nullptr;
   CUtensorMap mk, mv, mt;
   // Contiguous caches: one item per (batch row, latent head) of max_seq rows, 128-row boxes. Paged caches:
@@ -222,10 +222,13 @@ int run_tc(const void* q, const void* k, const void* v, const void* u_k, int64_t
   const cuuint64_t rows = pg ? (cuuint64_t)pg->block_size : (cuuint64_t)d->max_seq;
   const cuuint32_t box_rows = pg ? (cuuint32_t)pg->block_size : 128;
   if (f8) {
-    // e4m3 codes: one box per tile of 64 or 128 codes per row (the kernel's staged rows), no swizzle
-    const cuuint64_t dk[3] = {(cuuint64_t)d->r_k, rows, items}, dv[3] = {(cuuint64_t)d->r_v, rows, items};
-    const cuuint64_t sk[2] = {(cuuint64_t)d->r_k, rows * d->r_k}, sv[2] = {(cuuint64_t)d->r_v, rows * d->r_v};
-    const cuuint32_t bk[3] = {d->r_k > 64 ? 128u : 64u, box_rows, 1}, bv[3] = {d->r_v > 64 ? 128u : 64u, box_rows, 1};
+    // e4m3 codes: one box per tile of 64 or 128 codes per row (the kernel's staged rows), no swizzle; e2m1
+    // codes: rows of r / 2 bytes, one box of 32 or 64 bytes per row
+    const cuuint64_t wk = f4 ? d->r_k / 2 : d->r_k, wv = f4 ? d->r_v / 2 : d->r_v;
+    const cuuint64_t dk[3] = {wk, rows, items}, dv[3] = {wv, rows, items};
+    const cuuint64_t sk[2] = {wk, rows * wk}, sv[2] = {wv, rows * wv};
+    const cuuint32_t unit = f4 ? 32u : 64u;
+    const cuuint32_t bk[3] = {d->r_k > 64 ? 2 * unit : unit, box_rows, 1}, bv[3] = {d->r_v > 64 ? 2 * unit : unit, box_rows, 1};
     if (int st = encode(&mk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, k, dk, sk, bk, "k_lat (fp8)", CU_TENSOR_MAP_SWIZZLE_NONE))
       return st;
     if (int st = encode(&mv, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, v, dv, sv, bv, "v_lat (fp8)", CU_TENSOR_MAP_SWIZZLE_NONE))
@@ -278,6 +281,12 @@ int run_tc(const void* q, const void* k, const void* v, const void* u_k, int64_t
   p.v_exp = v_exp;
   if (f8) {  // fp8 caches: contiguous, latents at most 128 wide (checked by the caller)
     const int kbk8 = d->r_k > 64 ? 2 : 1, kbv8 = d->r_v > 64 ? 2 : 1;
+    if (f4) {
+      if (kbk8 == 1 && kbv8 == 1) return launch_tc<1, 1, false, 2, true, true>(mk, mv, mt, p, stream);
+      if (kbk8 == 1 && kbv8 == 2) return launch_tc<1, 2, false, 2, true, true>(mk, mv, mt, p, stream);
+      if (kbk8 == 2 && kbv8 == 1) return launch_tc<2, 1, false, 2, true, true>(mk, mv, mt, p, stream);
+      return launch_tc<2, 2, false, 2, true, true>(mk, mv, mt, p, stream);
+    }
     if (kbk8 == 1 && kbv8 == 1) return launch_tc<1, 1, false, 2, true>(mk, mv, mt, p, stream);
     if (kbk8 == 1 && kbv8 == 2) return launch_tc<1, 2, false, 2, true>(mk, mv, mt, p, stream);
     if (kbk8 == 2 && kbv8 == 1) return launch_tc<2, 1, false, 2, true>(mk, mv, mt, p, stream);
@@ -340,7 +349,7 @@ int run_decode(bool recon, const void* q, const void* k, const void* v, const vo
                const void* u_v, const void* cs_pairs, const int32_t* cur_pos, void* out, int32_t out_dtype,
                void* workspace, size_t workspace_bytes, const palu_decode_dims* d, float scale,
                cudaStream_t stream, const palu_page_table* pg = nullptr, const int8_t* k_exp = nullptr,
-               const int8_t* v_exp = nullptr) {
+               const int8_t* v_exp = nullptr, bool f4 = false) {
   int st = validate(d, recon, u_v != nullptr);
   if (st) return st;
   const bool f8 = k_exp != nullptr || v_exp != nullptr;
@@ -348,6 +357,8 @@ int run_decode(bool recon, const void* q, const void* k, const void* v, const vo
     if (!k_exp || !v_exp) return fail(PALU_ERR_INVALID, "fp8 latents need both exponent arrays");
     if (d->r_k > 128 || d->r_v > 128)
       return fail(PALU_ERR_INVALID, "fp8 latents: r_k and r_v must be at most 128 (got %d, %d)", d->r_k, d->r_v);
+    if (f4 && ((d->r_k != 64 && d->r_k != 128) || (d->r_v != 64 && d->r_v != 128)))
+      return fail(PALU_ERR_INVALID, "fp4 latents: r_k and r_v must be 64 or 128 (got %d, %d)", d->r_k, d->r_v);
     if (!use_tc(d, recon))
       return fail(PALU_ERR_INVALID, "fp8 latents run on the tcgen05 kernel only (palu_set_kernel selects mma.sync)");
   }
@@ -393,7 +404,7 @@ int run_decode(bool recon, const void* q, const void* k, const void* v, const vo
   set_pages(p, pg);
   if (tc) {
     st = run_tc(q, k, v, u_k, u_k_ld, cs_pairs, cur_pos, workspace, ws_o, ws_ml, d, splits, scale, pg, stream, k_exp,
-                v_exp);
+                v_exp, f4);
     if (st) return st;
     palu::CombineTcParams c;
     c.status = static_cast<const int*>(workspace);
@@ -546,6 +557,24 @@ int quantize_f8(const void* src, long rows, int r, void* codes, void* exps, cons
   return cuda_check("fp8 quantize kernel launch");
 }
 
+// fp4 rows: as quantize_f8, into r / 2 code bytes and r / 16 block exponents per row.
+int quantize_f4(const void* src, long rows, int r, void* codes, void* exps, const int32_t* cur_pos, int n_groups,
+                int max_seq, cudaStream_t stream) {
+  if (rows <= 0) return PALU_OK;
+  palu::QuantF4Params p;
+  p.src = static_cast<const __nv_bfloat16*>(src);
+  p.rows = rows;
+  p.r = r;
+  p.codes = static_cast<uint8_t*>(codes);
+  p.exps = static_cast<int8_t*>(exps);
+  p.cur_pos = cur_pos;
+  p.n_groups = n_groups;
+  p.max_seq = max_seq;
+  const long blocks = (rows + 7) / 8;
+  palu::palu_quantize_f4_kernel<<<(int)(blocks < 8192 ? blocks : 8192), 256, 0, stream>>>(p);
+  return cuda_check("fp4 quantize kernel launch");
+}
+
 }  // namespace
 
 extern "C" {
@@ -664,6 +693,43 @@ int palu_append_latents_f8(const void* new_k, const void* new_v, const int32_t* 
   const long rows = (long)d->batch * d->n_groups;
   if (int st = quantize_f8(new_k, rows, d->r_k, k_codes, k_exp, cur_pos, d->n_groups, d->max_seq, stream)) return st;
   return quantize_f8(new_v, rows, d->r_v, v_codes, v_exp, cur_pos, d->n_groups, d->max_seq, stream);
+}
+
+int palu_decode_attn_f4(const void* q, const void* k_codes, const void* v_codes, const int8_t* k_exp,
+                        const int8_t* v_exp, const void* u_k, int64_t u_k_ld, const void* u_v, const void* cs_pairs,
+                        const int32_t* cur_pos, void* out, int32_t out_dtype, void* workspace, size_t workspace_bytes,
+                        const palu_decode_dims* dims, float scale, palu_stream_t stream) {
+  g_err.clear();
+  if (!k_exp || !v_exp) return fail(PALU_ERR_INVALID, "fp4 latents need both exponent arrays");
+  return run_decode(true, q, k_codes, v_codes, u_k, u_k_ld, u_v, cs_pairs, cur_pos, out, out_dtype, workspace,
+                    workspace_bytes, dims, scale, stream, nullptr, k_exp, v_exp, true);
+}
+
+int palu_quantize_latents_f4(const void* latents, int64_t rows, int32_t r, void* codes, int8_t* exps,
+                             palu_stream_t stream) {
+  g_err.clear();
+  if (rows < 0 || r < 16 || r > 256 || r % 16 != 0)
+    return fail(PALU_ERR_INVALID, "quantize_latents_f4: rows >= 0 and r a multiple of 16 in [16, 256] (got %lld, %d)",
+                (long long)rows, r);
+  if (rows > 0 && (!latents || !codes || !exps)) return fail(PALU_ERR_INVALID, "quantize_latents_f4: every pointer must be set");
+  return quantize_f4(latents, (long)rows, r, codes, exps, nullptr, 1, 1, stream);
+}
+
+int palu_append_latents_f4(const void* new_k, const void* new_v, const int32_t* cur_pos, void* k_codes, void* v_codes,
+                           int8_t* k_exp, int8_t* v_exp, const palu_decode_dims* d, palu_stream_t stream) {
+  g_err.clear();
+  if (!d) return fail(PALU_ERR_INVALID, "dims is NULL");
+  if (!new_k || !new_v || !cur_pos || !k_codes || !v_codes || !k_exp || !v_exp)
+    return fail(PALU_ERR_INVALID, "append_latents_f4: every pointer must be set");
+  if (d->batch <= 0 || d->n_groups <= 0 || d->max_seq <= 0)
+    return fail(PALU_ERR_INVALID, "append: batch, n_groups and max_seq must be positive");
+  auto r_ok = [](int r) { return r >= 16 && r <= 256 && r % 16 == 0; };
+  if (!r_ok(d->r_k) || !r_ok(d->r_v))
+    return fail(PALU_ERR_INVALID, "append_latents_f4: r_k and r_v must be multiples of 16 in [16, 256] (got %d, %d)",
+                d->r_k, d->r_v);
+  const long rows = (long)d->batch * d->n_groups;
+  if (int st = quantize_f4(new_k, rows, d->r_k, k_codes, k_exp, cur_pos, d->n_groups, d->max_seq, stream)) return st;
+  return quantize_f4(new_v, rows, d->r_v, v_codes, v_exp, cur_pos, d->n_groups, d->max_seq, stream);
 }
 
 int palu_decode_attn_paged(const void* q, const void* k_cache, const void* v_cache, const void* u_k, int64_t u_k_ld,

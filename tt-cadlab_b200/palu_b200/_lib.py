@@ -23,6 +23,7 @@ EXPORTED = ("palu_decode_attn", "palu_decode_attn_static", "palu_decode_attn_pag
             "palu_workspace_bytes", "palu_choose_splits", "palu_append_latents",
             "palu_plain_gqa_decode", "palu_pack_cs_table", "palu_set_kernel", "palu_kernel_for", "palu_read_status",
             "palu_set_wait_limit", "palu_decode_attn_f8", "palu_quantize_latents_f8", "palu_append_latents_f8",
+            "palu_decode_attn_f4", "palu_quantize_latents_f4", "palu_append_latents_f4",
             "palu_last_error", "palu_version")
 PALU_KERNEL_AUTO, PALU_KERNEL_MMA, PALU_KERNEL_TC = 0, 1, 2
 
@@ -61,6 +62,13 @@ def load() -> ctypes.CDLL:
     lib.palu_quantize_latents_f8.restype = ctypes.c_int
     lib.palu_append_latents_f8.argtypes = [vp, vp, vp, vp, vp, vp, vp, dims_p, vp]
     lib.palu_append_latents_f8.restype = ctypes.c_int
+    for f in ("f4",):
+        getattr(lib, f"palu_decode_attn_{f}").argtypes = lib.palu_decode_attn_f8.argtypes
+        getattr(lib, f"palu_decode_attn_{f}").restype = ctypes.c_int
+        getattr(lib, f"palu_quantize_latents_{f}").argtypes = lib.palu_quantize_latents_f8.argtypes
+        getattr(lib, f"palu_quantize_latents_{f}").restype = ctypes.c_int
+        getattr(lib, f"palu_append_latents_{f}").argtypes = lib.palu_append_latents_f8.argtypes
+        getattr(lib, f"palu_append_latents_{f}").restype = ctypes.c_int
     pages_p = ctypes.POINTER(PageTable)
     lib.palu_decode_attn_paged.argtypes = [vp, vp, vp, vp, i64, vp, vp, vp, pages_p, vp, i32, vp, sz, dims_p, f32, vp]
     lib.palu_decode_attn_paged.restype = ctypes.c_int

@@ -211,6 +211,7 @@ class F8Latents:
     decode op takes a pair of these where it takes bf16 caches (``palu_sdpa_decode``, ``decode``)."""
 
     __slots__ = ("codes", "exp")
+    fmt = "f8"
 
     def __init__(self, codes: torch.Tensor, exp: torch.Tensor):
         if codes.dtype != torch.uint8 or exp.dtype != torch.int8:
@@ -248,6 +249,45 @@ class F8Latents:
         return self.codes.view(torch.float8_e4m3fn).float() * torch.exp2(self.exp.float()).unsqueeze(-1)
 
 
+class F4Latents(F8Latents):
+    """A latent cache held as e2m1 codes, two per byte (the first value in the low nibble), plus one
+    power-of-two exponent per block of 16 values: ``codes`` uint8 [..., r / 2], ``exp`` int8 [..., r / 16];
+    the cached value is code * 2^exp. ``shape`` reports the logical [..., r]."""
+
+    __slots__ = ()
+    fmt = "f4"
+
+    def __init__(self, codes: torch.Tensor, exp: torch.Tensor):
+        if codes.dtype != torch.uint8 or exp.dtype != torch.int8:
+            raise RuntimeError(f"fp4 latents need uint8 codes and int8 exponents, got {codes.dtype} / {exp.dtype}")
+        if codes.shape[-1] % 8 or tuple(exp.shape) != (*codes.shape[:-1], codes.shape[-1] // 8):
+            raise RuntimeError(f"fp4 latents: exponents {tuple(exp.shape)} must be [..., r / 16] for codes "
+                               f"{tuple(codes.shape)}")
+        self.codes, self.exp = codes, exp
+
+    @classmethod
+    def empty(cls, *shape, device=None) -> "F4Latents":
+        *lead, r = shape
+        return cls(torch.zeros(*lead, r // 2, dtype=torch.uint8, device=device),
+                   torch.zeros(*lead, r // 16, dtype=torch.int8, device=device))
+
+    @property
+    def shape(self):
+        return torch.Size((*self.codes.shape[:-1], 2 * self.codes.shape[-1]))
+
+    def contiguous(self) -> "F4Latents":
+        return F4Latents(self.codes.contiguous(), self.exp.contiguous())
+
+    def dequantize(self) -> torch.Tensor:
+        """float32 values code * 2^exp (host-side inspection)."""
+        lut = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], device=self.codes.device)
+        c = self.codes.long()
+        nib = torch.stack([c & 15, c >> 4], dim=-1).flatten(-2)
+        val = lut[nib & 7] * torch.where(nib >= 8, -1.0, 1.0)
+        sc = torch.exp2(self.exp.float()).repeat_interleave(16, dim=-1)
+        return val * sc
+
+
 def quantize_latents_f8(x: torch.Tensor) -> F8Latents:
     """bf16 latents [..., r] (CUDA) -> F8Latents (palu_quantize_latents_f8): per row, the smallest exponent
     k with max|row| <= 448 * 2^k (kept in [-120, 7]), codes = row * 2^-k rounded to nearest even e4m3."""
@@ -260,15 +300,31 @@ def quantize_latents_f8(x: torch.Tensor) -> F8Latents:
     return out
 
 
+def quantize_latents_f4(x: torch.Tensor) -> F4Latents:
+    """bf16 latents [..., r] (CUDA, r a multiple of 16) -> F4Latents (palu_quantize_latents_f4): per block of 16
+    values the smallest exponent k with max|block| <= 6 * 2^k (kept in [-120, 7]), codes = block * 2^-k
+    rounded to nearest even e2m1."""
+    _lib.require_cuda(x)
+    xb = _bf16(x).contiguous()
+    r = xb.shape[-1]
+    out = F4Latents.empty(*xb.shape, device=xb.device)
+    _lib.check(_lib.load().palu_quantize_latents_f4(xb.data_ptr(), xb.numel() // r, r, out.codes.data_ptr(),
+                                                    out.exp.data_ptr(), _lib.stream_handle(xb.device)))
+    return out
+
+
 def append_latents_f8(new_k, new_v, cur_pos, k_cache: F8Latents, v_cache: F8Latents) -> None:
-    """Quantize one step's latents [B, n_groups, r] (bf16) into fp8 caches at cur_pos[b]
-    (palu_append_latents_f8); rows with cur_pos outside [0, S) are skipped."""
+    """Quantize one step's latents [B, n_groups, r] (bf16) into fp8 (or fp4, with F4Latents) caches at
+    cur_pos[b] (palu_append_latents_f8 / _f4); rows with cur_pos outside [0, S) are skipped."""
+    if k_cache.fmt != v_cache.fmt:
+        raise RuntimeError("k and v caches must hold the same low-bit format")
     _lib.require_cuda(new_k, new_v, cur_pos, k_cache.codes, v_cache.codes)
     B, G, S, r_k = k_cache.shape
     r_v = v_cache.shape[3]
     d = _lib.dims(B, G, G, G, r_k, r_v, S)
     nk, nv = _bf16(new_k).contiguous(), _bf16(new_v).contiguous()
-    _lib.check(_lib.load().palu_append_latents_f8(
+    fn = _lib.load().palu_append_latents_f4 if k_cache.fmt == "f4" else _lib.load().palu_append_latents_f8
+    _lib.check(fn(
         nk.data_ptr(), nv.data_ptr(), cur_pos.to(torch.int32).contiguous().data_ptr(), k_cache.codes.data_ptr(),
         v_cache.codes.data_ptr(), k_cache.exp.data_ptr(), v_cache.exp.data_ptr(), ctypes.byref(d),
         _lib.stream_handle(nk.device)))
@@ -289,8 +345,8 @@ def decode(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, *, u_k_ld=HEAD_DIM, u_
     ``check_status`` (default: the PALU_CHECK_STATUS environment variable) waits for the call and raises
     RuntimeError if a bounded device wait expired, as the reference op raises on a failed run."""
     f8 = isinstance(k_latent, F8Latents)
-    if f8 != isinstance(v_latent, F8Latents):
-        raise RuntimeError("k_latent and v_latent must both be bf16 or both fp8 (F8Latents)")
+    if f8 != isinstance(v_latent, F8Latents) or (f8 and k_latent.fmt != v_latent.fmt):
+        raise RuntimeError("k_latent and v_latent must both be bf16 or both fp8 (F8Latents) or both fp4 (F4Latents)")
     if f8 and page_table is not None:
         raise RuntimeError("fp8 latent caches are contiguous (no page table)")
     if not _checked:
@@ -312,7 +368,8 @@ def decode(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, *, u_k_ld=HEAD_DIM, u_
     odt = _lib.PALU_F32 if out.dtype == torch.float32 else _lib.PALU_BF16
     sc = HEAD_DIM ** -0.5 if scale is None else float(scale)
     if f8:
-        _lib.check(_lib.load().palu_decode_attn_f8(
+        fn = _lib.load().palu_decode_attn_f4 if k_latent.fmt == "f4" else _lib.load().palu_decode_attn_f8
+        _lib.check(fn(
             q.data_ptr(), k_latent.codes.data_ptr(), v_latent.codes.data_ptr(), k_latent.exp.data_ptr(),
             v_latent.exp.data_ptr(), u_k.data_ptr(), int(u_k_ld), _lib.ptr(u_v), cs_pairs.data_ptr(),
             cur_pos.data_ptr(), out.data_ptr(), odt, workspace.data_ptr(), workspace.numel(), ctypes.byref(d), sc,
@@ -409,8 +466,8 @@ def palu_sdpa_decode(q, k_latent, w_rot, cs_tab, v_latent, head_dim_v, cur_pos_t
         if h > 1 and cores is not None and B * (n_kv // h) > cores:
             raise RuntimeError(f"heads_per_core {h} needs {B * (n_kv // h)} cores, only {cores} available")
     f8 = isinstance(k_latent, F8Latents)
-    if f8 != isinstance(v_latent, F8Latents):
-        raise RuntimeError("k_latent and v_latent must both be bf16 or both fp8 (F8Latents)")
+    if f8 != isinstance(v_latent, F8Latents) or (f8 and k_latent.fmt != v_latent.fmt):
+        raise RuntimeError("k_latent and v_latent must both be bf16 or both fp8 (F8Latents) or both fp4 (F4Latents)")
     if f8:
         if page_table_tensor is not None:
             raise RuntimeError("fp8 latent caches are contiguous (no page_table_tensor)")
