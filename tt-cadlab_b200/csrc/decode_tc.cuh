@@ -405,14 +405,18 @@ PALU_DEVINL bool f8_convert_row(unsigned char* tile, const unsigned char* stage,
 // fp4: 16 staged e2m1 codes of one row (v: 8 bytes, the first code of each byte in its low nibble) ->
 // codes 16 c .. 16 c + 15 of row r of f16 box `box` (chunks 2 c, 2 c + 1), converted exactly and multiplied by
 // the block's f16 pair s2 = (2^k, 2^k).
+PALU_DEVINL void e2m1x8_to_f16x8(uint32_t w, uint32_t& o0, uint32_t& o1, uint32_t& o2, uint32_t& o3) {
+  asm("{\n .reg .b8 a, b, c, d;\n mov.b32 {a, b, c, d}, %4;\n cvt.rn.f16x2.e2m1x2 %0, a;\n"
+      " cvt.rn.f16x2.e2m1x2 %1, b;\n cvt.rn.f16x2.e2m1x2 %2, c;\n cvt.rn.f16x2.e2m1x2 %3, d;\n}\n"
+      : "=r"(o0), "=r"(o1), "=r"(o2), "=r"(o3)
+      : "r"(w));
+}
 PALU_DEVINL void f4_store_chunk(unsigned char* tile, int r, uint2 v, uint32_t s2, int box, int c) {
   uint32_t o[8];
+  e2m1x8_to_f16x8(v.x, o[0], o[1], o[2], o[3]);
+  e2m1x8_to_f16x8(v.y, o[4], o[5], o[6], o[7]);
 #pragma unroll
-  for (int x = 0; x < 8; ++x) {
-    const uint32_t w = x < 4 ? v.x : v.y;
-    const __half2_raw h = __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)((w >> (8 * (x & 3))) & 0xFFu), __NV_E2M1);
-    o[x] = hmul2_u32((uint32_t)h.x | ((uint32_t)h.y << 16), s2);
-  }
+  for (int x = 0; x < 8; ++x) o[x] = hmul2_u32(o[x], s2);
   unsigned char* brow = tile + box * kBox + r * 128;
   *reinterpret_cast<uint4*>(brow + (((2 * c) ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
   *reinterpret_cast<uint4*>(brow + (((2 * c + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
