@@ -560,8 +560,9 @@ def run_layer(args, ws, rank, local):
             "config": workload_config(W, ws, b_gpu, args.paged, shard, args.latent),
             "latent_dtype": {"f8": "e4m3 + per-row exponent", "f4": "e2m1 + per-16 exponent"}.get(args.latent, "bf16"),
             "us_per_layer": ms * 1e3,
-            "parts_us": {"decode_op": op_ms * 1e3, "wo_gemm": gemm_ms * 1e3, "all_reduce": ar_ms * 1e3},
-            "all_reduce_share": ar_ms / ms if ms > 0 else None,
+            "parts_us": {"decode_op": op_ms * 1e3, "wo_gemm": gemm_ms * 1e3,
+                         "all_reduce": ar_ms * 1e3 if ws > 1 else None},  # one GPU: no collective in the step
+            "all_reduce_share": ar_ms / ms if ms > 0 and ws > 1 else None,
             "decode_op_us": op_ms * 1e3, "latent_GBps": achieved,
             "e2e": {"value": B / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,

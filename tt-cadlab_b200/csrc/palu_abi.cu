@@ -202,7 +202,7 @@ void set_pages(Params& p, const palu_page_table* pg) {
 template <int KBK, int KBV, bool PAGED, int NP = 2, bool F8 = false, bool F4 = false>
 int launch_tc(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mt, const palu::tc::TcParams& p,
               cudaStream_t stream) {
-  using Lay = palu::tc::Layout<KBK, KBV, NP>;
+  using Lay = palu::tc::Layout<KBK, KBV, NP, F8>;
   auto kern = palu::tc::palu_decode_tc_kernel<KBK, KBV, PAGED, NP, F8, F4>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::TOTAL) != cudaSuccess)
     return cuda_check("cudaFuncSetAttribute(decode tc)");
