@@ -33,9 +33,13 @@
 // status code, all roles stop (the multi-lane warps agree on it, so none is left divergent), copies and
 // MMAs in flight are drained, and TMEM is freed.
 // Latents wider than 128 (up to 256: the grouped G-LRD caches) run the same roles with ONE pipeline per CTA
-// (NP = 1; group 1's warps only help stage U_k): U_k alone is then 64 KB and a K or V tile 64 KB, so a single
-// K and V stage per CTA is what fits in shared memory; V^T is then two M = 128 blocks (latent dims 0..127 and
-// 128..255) whose PV results sit in TMEM columns 256..319, the columns group 1 would have used.
+// (NP = 1; group 1's warps only help stage U_k): U_k alone is then 64 KB and a K or V tile 64 KB, so K streams
+// through a ring of 64-wide boxes into a double-buffered D_k, a single V stage fits, and V^T is two M = 128
+// blocks (latent dims 0..127 and 128..255) whose PV results sit in TMEM columns 256..319, the columns group 1
+// would have used.
+// Low-bit latent caches (F8: e4m3 codes with a scale per row; F4: e2m1 codes with a scale per 16 values) keep
+// the two pipelines; their K and V producer warps work as whole warps, converting each tile landed by TMA in
+// place into the f16 tile the MMAs read, and the reconstruction and PV run on f16 operands.
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -47,8 +51,8 @@
 namespace palu {
 namespace tc {
 
-// Warps: 8 single-lane role warps (see role_of), then 8 RoPE warps and 8 softmax warps (4 per group). A
-// RoPE or softmax warp w owns TMEM lanes 32 (w % 4) .. + 31.
+// Warps: 8 role warps (see role_of; single-lane, except the low-bit producers), then 8 RoPE warps and 8
+// softmax warps (4 per group). A RoPE or softmax warp w owns TMEM lanes 32 (w % 4) .. + 31.
 constexpr int kRoleWarps = 8;
 constexpr int kRopeWarp0 = kRoleWarps;
 constexpr int kSoftWarp0 = kRoleWarps + 8;
@@ -705,7 +709,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const RowSeg seg0{s_range[1], s_range[2], s_range[3], 0};  // its first segment
 
   if (warp < kRoleWarps) {
-    // ============================== single-lane role warps ==============================
+    // ============================== role warps ==============================
     const int g = warp < 4 ? 0 : 1, role = role_of(warp);
     const int n_g = g < NP ? (n - g + NP - 1) / NP : 0;  // this group's tiles: CTA-local t = g + NP j, j < n_g
     if (F8 && (role == kRoleKT || role == kRoleV)) {
