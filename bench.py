@@ -623,7 +623,7 @@ def run_decoder(args, ws, rank, local):
         gp = torch.Generator(device=dev).manual_seed(99)
         pt = torch.randperm(B * per_row, generator=gp, device=dev).view(B, per_row).to(torch.int32)
     model = PaluDecoder(cfg, ranks, max_batch=B, max_seq=max_seq, seed=11, device=str(dev), rank=rank, world=ws,
-                        paged_attention_config=pc)
+                        paged_attention_config=pc, latent_dtype=args.latent)
     # the prompt: random token ids (every rank draws the same), prefilled a few rows at a time
     prompt = torch.randint(0, cfg.vocab, (B, ctx), generator=torch.Generator().manual_seed(8)).to(dev)
     t_pre = time.perf_counter()
@@ -677,13 +677,15 @@ def run_decoder(args, ws, rank, local):
             "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random weights, random prompt token ids, greedy generation)",
-            "config": {"workload": f"decoder_32l_b{B}_ctx{ctx}_gen{gen}" + (f"_paged{args.paged}" if args.paged else ""),
+            "config": {"workload": f"decoder_32l_b{B}_ctx{ctx}_gen{gen}" + (f"_paged{args.paged}" if args.paged else "")
+                       + ("" if args.latent == "bf16" else f"_{args.latent}"),
                        "layers": cfg.n_layers, "batch": B, "prompt": ctx, "generated": gen,
                        "ranks": "per layer and per KV head from {32,48,64,96,128}, seed 7",
                        "layer_widths_rk_rv": widths,
                        "latent_bytes_per_token_step": sum(8 * (rk + rv) * 2 for rk, rv in widths),
                        "parallelism": f"tp{ws} (KV heads + MLP hidden)",
-                       "cache": f"paged, blocks of {args.paged}" if args.paged else "contiguous"},
+                       "cache": (f"paged, blocks of {args.paged}" if args.paged else "contiguous")
+                       + ("" if args.latent == "bf16" else f", {args.latent} latents")},
             "prefill_s": prefill_s, "generated_tokens_sample": toks[:2, :8].tolist(),
             "gpu_launches": None, "clocks": clk.summary()}), flush=True)
     if ws > 1:

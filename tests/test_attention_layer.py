@@ -163,3 +163,37 @@ def test_glrd_layer_matches_oracle_layer_on_gpu(cuda):
     layer, x_pre, x_d, y_pre, y_d = _glrd_layer("cuda")
     _check(layer.forward_prefill(x_pre), y_pre, "G-LRD prefill")
     _check(layer.forward_decode(x_d[:, 0], torch.full((2,), x_pre.shape[1], dtype=torch.int32)), y_d[:, 0], "G-LRD decode")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("latent_dtype,bar", [("f8", 0.99), ("f4", 0.95)])
+def test_layer_with_low_bit_latent_caches(cuda, latent_dtype, bar):
+    """The layer with the reference's low-bit latent-cache option (latent_dtype; bfp8 / bfp4 on the reference,
+    e4m3 / e2m1 with power-of-two scales here): prefill and two decode steps against the same layer on bf16
+    caches, PCC >= 0.99 (fp8) and >= 0.95 (fp4, the reference's bar for bfp4 latents)."""
+    from palu_b200.attention import PaluAttention
+    from palu_b200.convert import LowRank
+    g = torch.Generator().manual_seed(41)
+    nh, nkv, hd, r_k, r_v = 8, 4, 128, 64, 128
+    dim = nh * hd
+    bf = lambda t: t.to(torch.bfloat16).float()
+    wq, wo = bf(torch.randn(dim, dim, generator=g) / dim ** 0.5), bf(torch.randn(dim, dim, generator=g) / dim ** 0.5)
+    lr = LowRank(k_VT=bf(torch.randn(nkv, r_k, dim, generator=g) / dim ** 0.5),
+                 k_U=bf(torch.randn(nkv, hd, r_k, generator=g) / r_k ** 0.5),
+                 v_VT=bf(torch.randn(nkv, r_v, dim, generator=g) / dim ** 0.5),
+                 v_U=bf(torch.randn(nkv, hd, r_v, generator=g) / r_v ** 0.5))
+    layers = [PaluAttention(wq, wo, lr, nh, nkv, max_batch=2, max_seq=96, device="cuda", latent_dtype=ld)
+              for ld in ("bf16", latent_dtype)]
+    B, P = 2, 40
+    x_pre = bf(torch.randn(B, P, dim, generator=g))
+    xs = [bf(torch.randn(B, dim, generator=g)) for _ in range(2)]
+    outs = []
+    for layer in layers:
+        o = [layer.forward_prefill(x_pre).cpu()]
+        for i, x in enumerate(xs):
+            o.append(layer.forward_decode(x, torch.full((B,), P + i, dtype=torch.int32)).cpu())
+        outs.append(o)
+    for a, b in zip(*outs):
+        a, b = a.double().flatten(), b.double().flatten()
+        a, b = a - a.mean(), b - b.mean()
+        assert float((a @ b) / (a.norm() * b.norm())) >= bar

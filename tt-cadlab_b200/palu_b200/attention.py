@@ -68,7 +68,7 @@ class PaluAttention:
                  rope_scaling: Optional[dict] = LLAMA3_SCALING, shard: Optional[KVShard] = None,
                  device: str = "cuda", cache_dtype: torch.dtype = torch.bfloat16,
                  proj_dtype: torch.dtype = torch.float32,
-                 paged_attention_config: Optional[PagedAttentionConfig] = None):
+                 paged_attention_config: Optional[PagedAttentionConfig] = None, latent_dtype: str = "bf16"):
         if head_dim != fused.HEAD_DIM:
             raise RuntimeError(f"head_dim must be {fused.HEAD_DIM}, got {head_dim}")
         gs = lowrank.group_size
@@ -129,12 +129,23 @@ class PaluAttention:
                            .contiguous())
 
         self.paged = paged_attention_config
+        # Latent-cache format (the reference's latent_dtype: bfp8 by default, bfp4 per side, attention.py:
+        # 159-169): "bf16", or the B200 block-scaled forms "f8" (e4m3) and "f4" (e2m1), contiguous caches.
+        if latent_dtype not in ("bf16", "f8", "f4"):
+            raise RuntimeError(f"latent_dtype must be bf16, f8 or f4, got {latent_dtype!r}")
+        if latent_dtype != "bf16" and paged_attention_config is not None:
+            raise RuntimeError("low-bit latent caches are contiguous (no paged_attention_config)")
+        self.latent_dtype = latent_dtype
         # a paged row holds whole blocks: the tables cover max_seq rounded up to a block
         tab_len = max_seq if self.paged is None else -(-max_seq // self.paged.block_size) * self.paged.block_size
         cos, sin = fused.cos_sin_tables(head_dim, tab_len, rope_theta, rope_scaling)
         self.cos, self.sin = cos.to(dev), sin.to(dev)                                      # fp32 [>= S, hd]
         self.cs_tab = fused.cs_table(cos, sin, tab_len)[None, None].to(dev, bf)           # [1, 1, S, 2hd]
-        if self.paged is None:
+        if latent_dtype != "bf16":
+            cls = fused.F4Latents if latent_dtype == "f4" else fused.F8Latents
+            self.k_cache = cls.empty(max_batch, self.ng, max_seq, self.r_k, device=dev)
+            self.v_cache = cls.empty(max_batch, self.ng, max_seq, self.r_v, device=dev)
+        elif self.paged is None:
             self.k_cache = torch.zeros(max_batch, self.ng, max_seq, self.r_k, dtype=cache_dtype, device=dev)
             self.v_cache = torch.zeros(max_batch, self.ng, max_seq, self.r_v, dtype=cache_dtype, device=dev)
         else:
@@ -144,7 +155,7 @@ class PaluAttention:
         self.scale = head_dim ** -0.5
         # The two device ops of a decode step (the CUDA library; the tests substitute CPU models here to
         # check the layer algebra on a machine without a GPU).
-        self.append_op = fused.append_latents
+        self.append_op = fused.append_latents if latent_dtype == "bf16" else fused.append_latents_f8
         self.attend_op = fused.palu_sdpa_decode
 
     # ---- RoPE on q (Meta-interleaved pairs, rotary_embedding_llama) ----------------------------------
@@ -171,7 +182,8 @@ class PaluAttention:
         """Whether the step's q rotation and latent append run as the library's one fused kernel: on CUDA,
         with bf16 caches and the library's append (tests that substitute CPU models of the device ops take
         the tensor-op path, which computes the same values)."""
-        return (qkv.is_cuda and self.append_op is fused.append_latents and self.k_cache.dtype == torch.bfloat16
+        return (qkv.is_cuda and self.append_op is fused.append_latents and self.latent_dtype == "bf16"
+                and self.k_cache.dtype == torch.bfloat16
                 and qkv.dtype in (torch.bfloat16, torch.float32))
 
     def _check_pages(self, page_table: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
@@ -231,8 +243,9 @@ class PaluAttention:
             nq, nk = self.nh * self.head_dim, self.ng * self.r_k
             q = qkv[:, :nq].float().view(B, self.nh, self.head_dim)
             q = self._rotate(q, pos.clamp(min=0).long()).to(torch.bfloat16)
-            k_new = qkv[:, nq:nq + nk].reshape(B, self.ng, self.r_k).to(self.k_cache.dtype)
-            v_new = qkv[:, nq + nk:].reshape(B, self.ng, self.r_v).to(self.v_cache.dtype)
+            cdt = self.k_cache.dtype if self.latent_dtype == "bf16" else torch.bfloat16
+            k_new = qkv[:, nq:nq + nk].reshape(B, self.ng, self.r_k).to(cdt)
+            v_new = qkv[:, nq + nk:].reshape(B, self.ng, self.r_v).to(cdt)
             self.append_op(k_new, v_new, pos, kc, vc, **paged)
         # bf16 projections take the op's output in bf16: the rounding _out's input cast would apply anyway
         odt = torch.bfloat16 if self.proj_dtype == torch.bfloat16 else torch.float32
@@ -267,7 +280,15 @@ class PaluAttention:
         lat_k = (xp @ self.wk_lat.T).float().view(B, P, self.ng, self.r_k).transpose(1, 2)
         lat_v = (xp @ self.wv_lat.T).float().view(B, P, self.ng, self.r_v).transpose(1, 2)
         pt = self._check_pages(page_table)
-        if pt is None:
+        if self.latent_dtype != "bf16":
+            # quantize the prompt's rows into the low-bit caches; attention runs on the values they hold
+            quant = fused.quantize_latents_f4 if self.latent_dtype == "f4" else fused.quantize_latents_f8
+            ck_q, cv_q = quant(lat_k.to(torch.bfloat16)), quant(lat_v.to(torch.bfloat16))
+            for cache, qd in ((self.k_cache, ck_q), (self.v_cache, cv_q)):
+                cache.codes[rows, :, :P] = qd.codes
+                cache.exp[rows, :, :P] = qd.exp
+            ck, cv = ck_q.dequantize(), cv_q.dequantize()
+        elif pt is None:
             self.k_cache[rows, :, :P] = lat_k.to(self.k_cache.dtype)
             self.v_cache[rows, :, :P] = lat_v.to(self.v_cache.dtype)
             ck, cv = self.k_cache[rows, :, :P], self.v_cache[rows, :, :P]

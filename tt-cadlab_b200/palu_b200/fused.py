@@ -244,6 +244,12 @@ class F8Latents:
     def contiguous(self) -> "F8Latents":
         return F8Latents(self.codes.contiguous(), self.exp.contiguous())
 
+    def __getitem__(self, rows):
+        """Leading-dimension selection (cache rows): a view of the same format."""
+        if not isinstance(rows, slice):
+            raise TypeError("low-bit latent caches index their leading (batch row) dimension by a slice")
+        return type(self)(self.codes[rows], self.exp[rows])
+
     def dequantize(self) -> torch.Tensor:
         """float32 values code * 2^exp (host-side inspection; the decode op reads the codes directly)."""
         return self.codes.view(torch.float8_e4m3fn).float() * torch.exp2(self.exp.float()).unsqueeze(-1)
