@@ -288,9 +288,14 @@ def run_reference(args, ws, rank):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(W: Workload, ws: int, batch: int, paged: int = 0, shard=None, latent: str = "bf16") -> dict:
+def workload_config(W: Workload, ws: int, batch: int, paged: int = 0, shard=None, latent: str = "bf16",
+                    rope: str = "") -> dict:
     name = W.name if batch == W.batch else re.sub(r"_b\d+_", f"_b{batch}_", W.name)
     extra = {}
+    if rope:
+        extra["rope"] = ("chunk-relative (the reference op's Phase 2: keys by table rows 0..127, the query "
+                         "rotated per 128-position chunk)" if rope == "relative"
+                         else "absolute (Phase 1: every key rotated by its own table row)")
     elem = 2
     if latent == "f8":
         name += "_f8"
@@ -363,9 +368,13 @@ def run_layer(args, ws, rank, local):
     ws_buf = _lib.new_workspace(d, dev)
     stream = torch.cuda.current_stream(dev)
 
+    rel = args.rope == "relative"
+    p2_kw = ({"rot_step": fused.rot_step_table(L["cos"], L["sin"], 128).to(dev), "trans_mat": fused.trans_mat_tile()}
+             if rel else {})
+
     def op():
         fused.decode(L["q"], L["k"], L["v"], L["u"], L["cs"], L["pos"], u_v=L["u_v"], out=out, workspace=ws_buf,
-                     page_table=pt)
+                     page_table=pt, chunk_relative=rel)
 
     def step(ev=None):
         if ev:
@@ -482,7 +491,7 @@ def run_layer(args, ws, rank, local):
         in_d.copy_(in_h, non_blocking=True)
         append(nk_d, nv_d, pos_d, L["k"], L["v"], **({"page_table": pt} if pt is not None else {}))
         o = fused.palu_sdpa_decode(q_d[None], L["k"], L["w_rot"], L["cs_tab"], L["v"], width, pos_d, u_v=u_v4,
-                                   scale=HD ** -0.5, **pt_kw)
+                                   scale=HD ** -0.5, **pt_kw, **p2_kw)
         torch.mm(o[0].view(B, n_q * width), L["wo"].t(), out=y)
         if ws > 1:
             dist.all_reduce(y)
@@ -557,7 +566,7 @@ def run_layer(args, ws, rank, local):
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, on device)",
-            "config": workload_config(W, ws, b_gpu, args.paged, shard, args.latent),
+            "config": workload_config(W, ws, b_gpu, args.paged, shard, args.latent, args.rope),
             "latent_dtype": {"f8": "e4m3 + per-row exponent", "f4": "e2m1 + per-16 exponent"}.get(args.latent, "bf16"),
             "us_per_layer": ms * 1e3,
             "parts_us": {"decode_op": op_ms * 1e3, "wo_gemm": gemm_ms * 1e3,
@@ -623,7 +632,8 @@ def run_decoder(args, ws, rank, local):
         gp = torch.Generator(device=dev).manual_seed(99)
         pt = torch.randperm(B * per_row, generator=gp, device=dev).view(B, per_row).to(torch.int32)
     model = PaluDecoder(cfg, ranks, max_batch=B, max_seq=max_seq, seed=11, device=str(dev), rank=rank, world=ws,
-                        paged_attention_config=pc, latent_dtype=args.latent)
+                        paged_attention_config=pc, latent_dtype=args.latent,
+                        cs_recurrence=args.rope == "relative")
     # the prompt: random token ids (every rank draws the same), prefilled a few rows at a time
     prompt = torch.randint(0, cfg.vocab, (B, ctx), generator=torch.Generator().manual_seed(8)).to(dev)
     t_pre = time.perf_counter()
@@ -684,6 +694,7 @@ def run_decoder(args, ws, rank, local):
                        "layer_widths_rk_rv": widths,
                        "latent_bytes_per_token_step": sum(8 * (rk + rv) * 2 for rk, rv in widths),
                        "parallelism": f"tp{ws} (KV heads + MLP hidden)",
+                       "rope": "chunk-relative (Phase 2)" if args.rope == "relative" else "absolute (Phase 1)",
                        "cache": (f"paged, blocks of {args.paged}" if args.paged else "contiguous")
                        + ("" if args.latent == "bf16" else f", {args.latent} latents")},
             "prefill_s": prefill_s, "generated_tokens_sample": toks[:2, :8].tolist(),
@@ -715,6 +726,9 @@ def main():
     ap.add_argument("--latent", default="bf16", choices=["bf16", "f8", "f4"],
                     help="latent cache format of the layer workload (f8: e4m3 codes + per-row exponent; "
                          "f4: e2m1 codes + per-16 exponent)")
+    ap.add_argument("--rope", default="relative", choices=["relative", "absolute"],
+                    help="the op's RoPE form: chunk-relative (the reference's Phase 2, rot_step passed: its "
+                         "published kernel) or absolute (Phase 1: every key's own table row)")
     ap.add_argument("--kernel", default="auto", choices=["auto", "tc", "mma"],
                     help="decode kernel family: tcgen05 (tc), legacy mma.sync (mma) or the library's choice")
     args = ap.parse_args()

@@ -291,6 +291,24 @@ int palu_set_kernel(int32_t which);
  */
 int palu_set_wait_limit(int64_t wait_ns, int32_t starve_v);
 
+/*
+ * RoPE form of the decode calls this host thread makes after it (thread-local; PALU_ROPE_ABSOLUTE by
+ * default). Replaces the reference op's Phase 1 / Phase 2 switch: palu_sdpa_decode rotates each key with
+ * the table row of its position unless rot_step and trans_mat are passed (Phase 2: chunk-relative
+ * angles, the query rotated per chunk; palu_tt/fused.py:1-14, attention.py:74-75 and 633-639, switched
+ * by PaluRuntime.cs_recurrence, convert.py:36).
+ *   PALU_ROPE_ABSOLUTE         key position p rotated by table row p (Phase 1).
+ *   PALU_ROPE_CHUNK_RELATIVE   Phase 2 with 128-position chunks: key position p = 128 t + j rotated by
+ *                              table row j, the query of chunk t rotated back by row 128 t (fp32, rounded
+ *                              once to fp16), so R_p is taken as R_{128 t} R_j. Equal to the absolute form
+ *                              for an exact rotation table, within the table's rounding otherwise (a bf16
+ *                              table moves the output by ~2e-3 mean relative; an fp32 table, packed to fp16,
+ *                              by ~2e-4). The tcgen05 kernel reads rows 0..127 once per CTA instead of every
+ *                              key's row. The mma.sync kernel has no chunk-relative form: its calls fail.
+ */
+enum palu_rope_mode { PALU_ROPE_ABSOLUTE = 0, PALU_ROPE_CHUNK_RELATIVE = 1 };
+int palu_set_rope_mode(int32_t mode);
+
 /* The kernel family a palu_decode_attn call with these dims would run (PALU_KERNEL_MMA or _TC). */
 int32_t palu_kernel_for(const palu_decode_dims* dims);
 

@@ -18,6 +18,7 @@ from oracle.palu_ref import (  # noqa: F401
     cs_table,
     expand_groups,
     llama3_scale_freqs,
+    phase2_tables,
     reference_decode,
     reference_decode_streamed,
     rope_freqs,

@@ -105,6 +105,23 @@ def rot_step_table(cos: torch.Tensor, sin: torch.Tensor, chunk: int) -> torch.Te
     return torch.cat([cos[chunk], sin[chunk]]).expand(32, -1).contiguous().float()
 
 
+def phase2_tables(cos: torch.Tensor, sin: torch.Tensor, chunk: int = 128):
+    """Effective per-position [cos | sin] of chunk-relative RoPE (the reference's Phase 2, fused.py:1-14):
+    key position p = chunk * t + j is rotated by the table's chunk-relative row j and the query by row
+    chunk * t the other way, which equals rotating the key by the composition R_{chunk t} R_j
+    (2-D rotations commute, fused.py:9-11):
+    cos'(p) = cos(p0) cos(j) - sin(p0) sin(j), sin'(p) = sin(p0) cos(j) + cos(p0) sin(j), p0 = chunk * t,
+    in fp32 from the given table values. For an exact table this is the table itself; a rounded table
+    (bf16, fp16) gives a rotation that differs from row p by the rounding of rows p0 and j. The B200 form
+    uses chunk 128 and reads the base rotation from row p0 directly (the reference steps it with the fp32
+    rot_step recurrence, fused.py:76-79)."""
+    S = cos.shape[0]
+    p = torch.arange(S)
+    p0, j = (p // chunk) * chunk, p % chunk
+    c, s = cos.float(), sin.float()
+    return c[p0] * c[j] - s[p0] * s[j], s[p0] * c[j] + c[p0] * s[j]
+
+
 # ----------------------------------------------------------------------------------------------
 # The op model (fused.py:82-107)
 # ----------------------------------------------------------------------------------------------

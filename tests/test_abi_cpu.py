@@ -160,3 +160,12 @@ def test_decoder_step_entry_points_validate_before_any_cuda_call():
     assert st == _lib.PALU_ERR_INVALID and "dtype" in lib.palu_last_error().decode()
     st = lib.palu_swiglu(z, 100, 64, z, 4, None)
     assert st == _lib.PALU_ERR_INVALID and "2 f" in lib.palu_last_error().decode()
+
+
+def test_rope_mode_setter_validates_without_a_gpu():
+    """palu_set_rope_mode (the op's Phase 1 / Phase 2 switch) takes the two modes and refuses others."""
+    lib = _lib.load()
+    assert lib.palu_set_rope_mode(_lib.PALU_ROPE_CHUNK_RELATIVE) == _lib.PALU_OK
+    assert lib.palu_set_rope_mode(_lib.PALU_ROPE_ABSOLUTE) == _lib.PALU_OK
+    assert lib.palu_set_rope_mode(7) == _lib.PALU_ERR_INVALID
+    assert b"RoPE mode" in lib.palu_last_error()

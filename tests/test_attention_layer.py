@@ -46,14 +46,17 @@ def _cpu_ops(layer):
                 kc[b, :, p] = new_k[b].to(kc.dtype)
                 vc[b, :, p] = new_v[b].to(vc.dtype)
 
-    def attend(q, kc, w_rot, cs_tab, vc, head_dim_v, pos, u_v=None, scale=None, out_dtype=None):
+    def attend(q, kc, w_rot, cs_tab, vc, head_dim_v, pos, u_v=None, scale=None, out_dtype=None, rot_step=None,
+               trans_mat=None):
         gs = w_rot.shape[1] // kc.shape[1]
         S = kc.shape[2]
         cs = cs_tab[0, 0, :S].float()
+        cos, sin = cs[:, :128], cs[:, 128:]
+        if rot_step is not None:  # Phase 2: chunk-relative angles (the op's rule, oracle.phase2_tables)
+            cos, sin = oracle.phase2_tables(cos, sin)
         u_v_ = None if u_v is None else u_v[0].float()
         return oracle.reference_decode(q.float(), oracle.expand_groups(kc.float(), gs), w_rot[0, :, :, :128].float(),
-                                       oracle.expand_groups(vc.float(), gs), pos.long(), cs[:, :128], cs[:, 128:],
-                                       scale, u_v=u_v_)
+                                       oracle.expand_groups(vc.float(), gs), pos.long(), cos, sin, scale, u_v=u_v_)
     layer.append_op, layer.attend_op = append, attend
 
 
@@ -120,9 +123,9 @@ def test_layer_matches_reference_layer_on_gpu(cuda):
     assert fused.workspace_status() == 0
 
 
-def _glrd_case(seed=3):
+def _glrd_case(seed=3, P=20):
     """A G-LRD layer (2 groups of 2 KV heads, ranks 48 / 96) and the oracle layer (reference.py:14-55) on it:
-    a 20-token prefill and one decode step."""
+    a P-token prefill and one decode step."""
     from palu_b200.convert import LowRank
     g = torch.Generator().manual_seed(seed)
     nh, nkv, gs, hd, r_k, r_v = 8, 4, 2, 128, 48, 96
@@ -138,16 +141,17 @@ def _glrd_case(seed=3):
                rope_scaling={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
                              "original_max_position_embeddings": 8192})
     ref = oracle.PaluRefAttention(cfg, w, lr)
-    B, P = 2, 20
+    B = 2
     x_pre, x_d = bf(torch.randn(B, P, dim, generator=g)), bf(torch.randn(B, 1, dim, generator=g))
     return cfg, w, lr, x_pre, x_d, ref.forward(x_pre, 0), ref.forward(x_d, P)
 
 
-def _glrd_layer(device):
+def _glrd_layer(device, P=20, max_seq=48, cs_recurrence=False):
     from palu_b200.attention import PaluAttention
-    cfg, w, lr, x_pre, x_d, y_pre, y_d = _glrd_case()
+    cfg, w, lr, x_pre, x_d, y_pre, y_d = _glrd_case(P=P)
     layer = PaluAttention(w["q"], w["o"], lr, cfg["num_attention_heads"], cfg["num_key_value_heads"], max_batch=2,
-                          max_seq=48, rope_scaling=cfg["rope_scaling"], device=device)
+                          max_seq=max_seq, rope_scaling=cfg["rope_scaling"], device=device,
+                          cs_recurrence=cs_recurrence)
     return layer, x_pre, x_d, y_pre, y_d
 
 
@@ -156,6 +160,24 @@ def test_glrd_layer_matches_oracle_layer_on_cpu_models():
     _cpu_ops(layer)
     _check(layer.forward_prefill(x_pre), y_pre, "G-LRD prefill")
     _check(layer.forward_decode(x_d[:, 0], torch.full((2,), x_pre.shape[1], dtype=torch.int32)), y_d[:, 0], "G-LRD decode")
+
+
+def test_glrd_layer_phase2_matches_oracle_layer_on_cpu_models():
+    """cs_recurrence=True (the reference's Phase 2): a 300-token prefill, so the decode step's keys span
+    three 128-position chunks, still within the layer bar against the oracle layer's exact RoPE."""
+    layer, x_pre, x_d, y_pre, y_d = _glrd_layer("cpu", P=300, max_seq=320, cs_recurrence=True)
+    _cpu_ops(layer)
+    _check(layer.forward_prefill(x_pre), y_pre, "G-LRD prefill")
+    _check(layer.forward_decode(x_d[:, 0], torch.full((2,), x_pre.shape[1], dtype=torch.int32)), y_d[:, 0],
+           "G-LRD Phase 2 decode")
+
+
+@pytest.mark.gpu
+def test_glrd_layer_phase2_matches_oracle_layer_on_gpu(cuda):
+    layer, x_pre, x_d, y_pre, y_d = _glrd_layer("cuda", P=300, max_seq=320, cs_recurrence=True)
+    _check(layer.forward_prefill(x_pre), y_pre, "G-LRD prefill")
+    _check(layer.forward_decode(x_d[:, 0], torch.full((2,), x_pre.shape[1], dtype=torch.int32)), y_d[:, 0],
+           "G-LRD Phase 2 decode")
 
 
 @pytest.mark.gpu

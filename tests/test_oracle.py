@@ -120,3 +120,16 @@ def test_metrics_are_relative_and_rowwise():
     assert math.isclose(mx, 0.001, rel_tol=1e-4) and math.isclose(mn, 0.001 / 2.02, rel_tol=1e-4)
     rmx, rmn = oracle.rowwise_rel_errors(out, ref)
     assert math.isclose(rmx, 0.1, rel_tol=1e-4) and math.isclose(rmn, 0.05, rel_tol=1e-4)
+
+
+def test_phase2_tables_compose_chunk_base_and_relative_rows():
+    """The chunk-relative rule (fused.py:1-14): exact on the first chunk (base row 0 is the identity), and for
+    an fp32 table equal to the table within fp32 angle rounding; a bf16 table differs by its rounding."""
+    cos, sin = oracle.cos_sin_tables(128, 4096, 500000.0, None)
+    cos, sin = cos[:4096], sin[:4096]
+    c2, s2 = oracle.phase2_tables(cos, sin)
+    assert torch.equal(c2[:128], cos[:128]) and torch.equal(s2[:128], sin[:128])
+    assert (c2 - cos).abs().max() < 5e-4 and (s2 - sin).abs().max() < 5e-4
+    cb, sb = cos.bfloat16().float(), sin.bfloat16().float()
+    c3, _ = oracle.phase2_tables(cb, sb)
+    assert 1e-4 < (c3 - cb).abs().max() < 2e-2

@@ -100,7 +100,16 @@ struct TcParams {
   // and one exponent per 16 values of a row, [B][n_groups][max_seq][r / 16].
   const int8_t* k_exp;
   const int8_t* v_exp;
+  // Chunk-relative RoPE (the reference's Phase 2, fused.py:1-14): nonzero rotates key position
+  // p = 128 t + j by the table rows j (0..127, loaded once per CTA) and rotates the query of tile t by
+  // row 128 t the other way, R_p = R_{128 t} R_j, instead of reading row p for every key. `cs` is the
+  // packed table (palu_pack_cs_table rows) the query rotation reads.
+  int rel;
+  const uint32_t* cs;
 };
+// Whether a layout holds the four table chunk slots that chunk-relative RoPE keeps for rows 0..127.
+template <class Lay, int NP>
+__host__ __device__ constexpr bool rel_fits() { return NP * Lay::T_SLOTS >= 4; }
 
 // Work split: the tiles of one KV head over all batch rows, in row order (row b has ceil(L_b / 128)
 // tiles, L_b = cur_pos[b] + 1 clamped to [0, max_seq]), are cut into `ctas` equal contiguous ranges, one
@@ -579,6 +588,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   using Lay = Layout<KBK, KBV, NP, F8>;
   constexpr int NS_K = Lay::NS_K, NS_V = Lay::NS_V, T_SLOTS = Lay::T_SLOTS;
   constexpr int NS_T = NP * T_SLOTS;  // table chunk slots, [group][slot]
+  // Chunk-relative RoPE: slots 0..3 hold table rows 0..127 (chunk c in slot c) for the whole kernel, loaded
+  // once by group 0's K producer; nothing releases or refills them.
+  const bool rel = rel_fits<Lay, NP>() && p.rel != 0;
   // V^T as PV's A operand: one M = 64 block (V at most 64 wide), one M = 128 block (at most 128), or two M = 128
   // blocks (at most 256; a block's rows past the latent width are the TMA's zero fill).
   constexpr int NMB = KBV <= 2 ? 1 : 2;
@@ -730,6 +742,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           tma_prefetch_map(tm);
           if (kt) tma_prefetch_map(&tm_tab);
+          if (kt && rel && g == 0) {  // chunk-relative RoPE: table rows 0..127 into slots 0..3, once
+            for (int c = 0; c < 4; ++c) {
+              mbar_expect_tx(bar(B_TF + c), Lay::TCH_BYTES);
+              tma_load_2d(sbase + Lay::OFF_TAB + c * Lay::TCH_BYTES, &tm_tab, bar(B_TF + c), c * 16, 0);
+            }
+          }
         }
         GroupTiles<NP> iss, cv;
         iss.init(p, seg0, g, n);
@@ -800,7 +818,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(kt ? bar(B_KF + sb) : bar(B_VF + 2 * sb + (use & 1)));
           jc = j + 1;
-          if (kt) {
+          if (kt && !rel) {
             for (int c = 0; c < 4; ++c) {
               const int nc = 4 * j + c, ts = g * T_SLOTS + nc % T_SLOTS, tuse = nc / T_SLOTS;
               if (tuse >= 1 && !wait_all(bar(B_TE + ts), (tuse - 1) & 1)) {
@@ -823,6 +841,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           for (int nc = max(0, issued_t - T_SLOTS); nc < issued_t; ++nc)
             mbar_drain(bar(B_TF + g * T_SLOTS + nc % T_SLOTS), (nc / T_SLOTS) & 1);
+          if (kt && rel && g == 0)
+            for (int c = 0; c < 4; ++c) mbar_drain(bar(B_TF + c), 0);
         }
       }
     } else if (lane == 0 && n_g > 0) {
@@ -839,6 +859,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         int kbn = 0;
         GroupTiles<NP> it;
         it.init(p, seg0, g, n);
+        if (kt && rel && g == 0) {  // chunk-relative RoPE: table rows 0..127 into slots 0..3, once
+          for (int c = 0; c < 4; ++c) {
+            mbar_expect_tx(bar(B_TF + c), Lay::TCH_BYTES);
+            tma_load_2d(sbase + Lay::OFF_TAB + c * Lay::TCH_BYTES, &tm_tab, bar(B_TF + c), c * 16, 0);
+          }
+        }
         for (int j = 0; j < n_g && it.valid(); ++j, it.next(p)) {
           const int t = g + NP * j, row = it.tile() * kTile, item_lat = it.s.b * p.n_groups + lat_head;
           const int sb = kt ? t % NS_K : t % NS_V, use = kt ? t / NS_K : t / NS_V;
@@ -903,7 +929,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             issued_kv = j + 1;
           }
-          if (kt) {
+          if (kt && !rel) {
             bool ok = true;
             for (int c = 0; c < 4; ++c) {
               const int nc = 4 * j + c, ts = g * T_SLOTS + nc % T_SLOTS, tuse = nc / T_SLOTS;
@@ -932,6 +958,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           for (int nc = max(0, issued_t - T_SLOTS); nc < issued_t; ++nc)
             mbar_drain(bar(B_TF + g * T_SLOTS + nc % T_SLOTS), (nc / T_SLOTS) & 1);
+          if (kt && rel && g == 0)
+            for (int c = 0; c < 4; ++c) mbar_drain(bar(B_TF + c), 0);
         }
       } else {
         const uint32_t tg = tmem + g * kGrpCols;
@@ -954,8 +982,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           pit.init(p, seg0, g, n);
           for (int j = 0; j <= n_g; ++j) {
             if (j < n_g) {
-              const int qb = it.sigma & 1;
-              if (it.first() && !wait(bar(B_QF + 2 * g + qb), (it.sigma >> 1) & 1)) break;
+              // Q buffer: per group segment (the row's q), or per tile with chunk-relative RoPE (the q of the
+              // tile's row rotated by the tile's base position)
+              const int qb = rel ? (j & 1) : (it.sigma & 1);
+              if ((rel || it.first()) && !wait(bar(B_QF + 2 * g + qb), ((rel ? j : it.sigma) >> 1) & 1)) break;
               if (j >= 2 && !wait(bar(B_SR + 2 * g + (j & 1)), ((j >> 1) - 1) & 1)) break;
               const uint32_t sQ = sbase + Lay::OFF_Q + (2 * g + qb) * Lay::Q_BYTES;
               it.next(p);
@@ -1115,7 +1145,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(bar(B_UF));
     }
     const int n_g = NP == 2 ? (n - g + 1) / 2 : n;
-    for (int i = 0; i < n_g; ++i) {
+    // chunk-relative RoPE: the fixed table rows 0..127 (slots 0..3), waited for once
+    bool tab_ok = true;
+    if (rel && n_g > 0)
+      for (int c = 0; c < 4 && tab_ok; ++c) tab_ok = wait_all(bar(B_TF + c), 0);
+    for (int i = 0; tab_ok && i < n_g; ++i) {
       // ---- RoPE(i), by halves: D_k columns 64 h .. 64 h + 31 hold the even dims of frequencies 32 h + c,
       // columns 64 h + 32 + c their odd dims; chunk ch = 2 h + sub rotates frequencies 16 ch .. 16 ch + 15.
       // K_rot -> fp16 A columns. Finishing half h releases D_k half h (reconstruction of tile i + 1) and
@@ -1133,12 +1167,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           fence_after();
         }
-        const int n = i * 4 + ch, sb = g * T_SLOTS + n % T_SLOTS;
+        const int n = i * 4 + ch, sb = rel ? ch : g * T_SLOTS + n % T_SLOTS;
         // The chunk's D_k columns load while this warp waits for and reads its table chunk.
         uint32_t ke[16], ko[16];
         tmem_ld16(dk + 64 * h + 16 * sub, ke);
         tmem_ld16(dk + 64 * h + 32 + 16 * sub, ko);
-        if (!wait_all(bar(B_TF + sb), (n / T_SLOTS) & 1)) {
+        if (!rel && !wait_all(bar(B_TF + sb), (n / T_SLOTS) & 1)) {
           tmem_wait_ld_regs(ke, ko);
           ok = false;
           break;
@@ -1178,9 +1212,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         // (TMA), so the reads are ordered before the release by fence.proxy.async. Without the fence the
         // refill overwrote rows whose reads were still in flight (the first rows of the chunk, which the TMA
         // writes first): on B200 a few percent of calls then differed in the last bits of one batch row.
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_TE + sb));
+        if (!rel) {
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(B_TE + sb));
+        }
         if (sub == 0 && i >= 1) {
           // A half h still feeds half h of QK(i - 1) until those MMAs complete: their commit is AE (h = 0)
           // or the scores barrier (h = 1).
@@ -1214,23 +1250,42 @@ __global__ void __launch_bounds__(kThreads, 1)
     // head's query heads; the rest stay zero) x 128 dims in [even | odd] order: K-block 0 = even dims,
     // K-block 1 = odd dims (64 fp16 per 128-B row). Item (row, 16-byte chunk of 8 reordered dims); bf16
     // q is exact in fp16. The QK issuer waits for the buffer's barrier.
-    auto stage_q = [&](int b_row, int buf) {
+    // Chunk-relative RoPE (`tile` >= 0): the q of the tile's row rotated by the tile's base position
+    // p0 = 128 tile the other way, q' = R_{p0}^T q (q'(2f) = q(2f) cos + q(2f+1) sin, q'(2f+1) = q(2f+1) cos -
+    // q(2f) sin, with the packed table's row p0), in fp32 and rounded once to fp16, so that
+    // q' . R_j k = q . R_{p0 + j} k.
+    auto stage_q = [&](int b_row, int tile, int buf) {
       const int tq = quarter * 32 + lane;
       if (tq < p.rep * 16) {
-        const int r = tq >> 4, chunk = tq & 15;
+        const int r = tq >> 4, chunk = tq & 15, c8 = chunk & 7;
         const uint4* qr = reinterpret_cast<const uint4*>(p.q + ((size_t)b_row * p.n_q + kvh * p.rep + r) * kHeadDim +
-                                                         16 * (chunk & 7));
-        const uint4 x0 = qr[0], x1 = qr[1];  // source dims 16 (chunk & 7) .. + 15
-        const uint32_t sel = chunk < 8 ? 0x5410u : 0x7632u;  // even (low) or odd (high) halves
-        const uint32_t bw[4] = {__byte_perm(x0.x, x0.y, sel), __byte_perm(x0.z, x0.w, sel),
-                                __byte_perm(x1.x, x1.y, sel), __byte_perm(x1.z, x1.w, sel)};
+                                                         16 * c8);
+        const uint4 x0 = qr[0], x1 = qr[1];  // source dims 16 c8 .. + 15: (even, odd) of frequencies 8 c8 .. + 7
         uint32_t w[4];
+        if (tile >= 0) {
+          // cosines of frequencies 8 c8 .. + 7 at p0: packed words 16 (c8 >> 1) + 4 (c8 & 1) .. + 3; sines 8 words on
+          const uint4* tr = reinterpret_cast<const uint4*>(p.cs + (size_t)tile * kTile * 64 + 16 * (c8 >> 1) + 4 * (c8 & 1));
+          const uint4 cw = __ldg(tr), sw = __ldg(tr + 2);
+          const uint32_t qw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+          const uint32_t cv[4] = {cw.x, cw.y, cw.z, cw.w}, sv[4] = {sw.x, sw.y, sw.z, sw.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = unpack_bf16(bw[i]);
-          w[i] = pack_half2(f.x, f.y);
+          for (int i = 0; i < 4; ++i) {  // frequencies 8 c8 + 2 i (a) and 8 c8 + 2 i + 1 (b)
+            const float2 c = __half22float2(u32_as_half2(cv[i])), sn = __half22float2(u32_as_half2(sv[i]));
+            const float2 a = unpack_bf16(qw[2 * i]), b = unpack_bf16(qw[2 * i + 1]);
+            w[i] = chunk < 8 ? pack_half2(a.x * c.x + a.y * sn.x, b.x * c.y + b.y * sn.y)
+                             : pack_half2(a.y * c.x - a.x * sn.x, b.y * c.y - b.x * sn.y);
+          }
+        } else {
+          const uint32_t sel = chunk < 8 ? 0x5410u : 0x7632u;  // even (low) or odd (high) halves
+          const uint32_t bw[4] = {__byte_perm(x0.x, x0.y, sel), __byte_perm(x0.z, x0.w, sel),
+                                  __byte_perm(x1.x, x1.y, sel), __byte_perm(x1.z, x1.w, sel)};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = unpack_bf16(bw[i]);
+            w[i] = pack_half2(f.x, f.y);
+          }
         }
-        const uint32_t off = (chunk >> 3) * 2048 + r * 128 + (((chunk & 7) ^ (r & 7)) << 4);
+        const uint32_t off = (chunk >> 3) * 2048 + r * 128 + ((c8 ^ (r & 7)) << 4);
         *reinterpret_cast<uint4*>(smem + Lay::OFF_Q + (2 * g + buf) * Lay::Q_BYTES + off) =
             make_uint4(w[0], w[1], w[2], w[3]);
       }
@@ -1240,12 +1295,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     // Q for the group's first two segments now; at the start of segment sigma >= 1, the one after it
     // (buffer (sigma + 1) & 1 last fed QK of segment sigma - 1, all of whose scores are read by then).
+    // Chunk-relative RoPE: Q per tile instead, tiles 0 and 1 now and tile j + 2 once softmax(j) has seen the
+    // scores of QK(j), the last reader of buffer j & 1.
     GroupTiles<NP> qa;
     qa.init(p, seg0, g, n);
     if (g < NP && qa.valid()) {
-      stage_q(qa.s.b, 0);
-      qa.next_segment(p);
-      if (qa.valid()) stage_q(qa.s.b, 1);
+      if (rel) {
+        stage_q(qa.s.b, qa.tile(), 0);
+        qa.next(p);
+        if (qa.valid()) {
+          stage_q(qa.s.b, qa.tile(), 1);
+          qa.next(p);
+        }
+      } else {
+        stage_q(qa.s.b, -1, 0);
+        qa.next_segment(p);
+        if (qa.valid()) stage_q(qa.s.b, -1, 1);
+      }
     }
     // alphaN: softmax scale of tiles j with j%2 == N; o_acc[mb][h]: latent dim 128 mb + row of head h
     float m_run[4], l_run[4], o_acc[NMB][4], alpha0[4], alpha1[4];
@@ -1262,9 +1328,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int cnt = seg_group_count<NP>(sg, g), kf = seg_group_first<NP>(sg, g);
       if (cnt > 0) {
-        if (sigma >= 1) {
+        if (sigma >= 1 && !rel) {
           qa.next_segment(p);
-          if (qa.valid()) stage_q(qa.s.b, (sigma + 1) & 1);
+          if (qa.valid()) stage_q(qa.s.b, -1, (sigma + 1) & 1);
         }
         const int L = row_len(p, sg.b);
         // softmax(j) then accumulate(j - 1) per step; the segment's last tile is accumulated before its
@@ -1341,6 +1407,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(B_PF + 2 * g + (j & 1)));
+            if (rel && qa.valid()) {  // Q of tile j + 2 into buffer j & 1
+              stage_q(qa.s.b, qa.tile(), j & 1);
+              qa.next(p);
+            }
           }
           // ---- accumulate(j - 1) --------------------------------------------------------------------------
           if (x >= 1) {

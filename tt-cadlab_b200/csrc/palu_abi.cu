@@ -117,6 +117,8 @@ size_t ws_bytes(const palu_decode_dims* d, int splits) {
 // ---- tcgen05 path: availability, split planning, tensor maps ---------------------------------------
 
 int g_kernel_choice = PALU_KERNEL_AUTO;
+// RoPE form of this host thread's decode calls (palu_set_rope_mode).
+thread_local int g_rope_mode = PALU_ROPE_ABSOLUTE;
 // Timeout-path test hook (palu_set_wait_limit): the bound on every device wait, and the V-starve switch.
 std::atomic<unsigned long long> g_wait_ns{palu::tc::kWaitNs};
 std::atomic<int> g_starve_v{0};
@@ -204,6 +206,8 @@ int launch_tc(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& m
               cudaStream_t stream) {
   using Lay = palu::tc::Layout<KBK, KBV, NP, F8>;
   auto kern = palu::tc::palu_decode_tc_kernel<KBK, KBV, PAGED, NP, F8, F4>;
+  if (p.rel && !palu::tc::rel_fits<Lay, NP>())
+    return fail(PALU_ERR_INVALID, "chunk-relative RoPE: this kernel layout has no room for the fixed table rows");
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::TOTAL) != cudaSuccess)
     return cuda_check("cudaFuncSetAttribute(decode tc)");
   kern<<<dim3(p.ctas, p.n_kv, 1), palu::tc::kThreads, Lay::TOTAL, stream>>>(mk, mv, mt, p);
@@ -279,6 +283,8 @@ int run_tc(const void* q, const void* k, const void* v, const void* u_k, int64_t
   p.pdl_early = (long)splits * d->n_kv_heads <= device_sms();
   p.k_exp = k_exp;
   p.v_exp = v_exp;
+  p.rel = g_rope_mode == PALU_ROPE_CHUNK_RELATIVE;
+  p.cs = static_cast<const uint32_t*>(cs_pairs);
   if (f8) {  // fp8 caches: contiguous, latents at most 128 wide (checked by the caller)
     const int kbk8 = d->r_k > 64 ? 2 : 1, kbv8 = d->r_v > 64 ? 2 : 1;
     if (f4) {
@@ -368,6 +374,8 @@ int run_decode(bool recon, const void* q, const void* k, const void* v, const vo
     return fail(PALU_ERR_INVALID, "w_rot/u_k row length %lld must be >= 128 and a multiple of 8", (long long)u_k_ld);
   if (out_dtype != PALU_BF16 && out_dtype != PALU_F32) return fail(PALU_ERR_INVALID, "out_dtype must be bf16 or f32");
   const bool tc = use_tc(d, recon);
+  if (recon && !tc && g_rope_mode == PALU_ROPE_CHUNK_RELATIVE)
+    return fail(PALU_ERR_INVALID, "chunk-relative RoPE runs on the tcgen05 kernel only (palu_set_kernel selects mma.sync)");
   const int splits = tc ? choose_splits_tc(d) : choose_splits(d);
   const size_t need = tc ? ws_tc_bytes(d, splits) : ws_bytes(d, splits);
   if (!workspace || workspace_bytes < need)
@@ -600,6 +608,14 @@ int palu_set_kernel(int32_t which) {
   if (which != PALU_KERNEL_AUTO && which != PALU_KERNEL_MMA && which != PALU_KERNEL_TC)
     return fail(PALU_ERR_INVALID, "kernel choice must be PALU_KERNEL_AUTO, _MMA or _TC");
   g_kernel_choice = which;
+  return PALU_OK;
+}
+
+int palu_set_rope_mode(int32_t mode) {
+  g_err.clear();
+  if (mode != PALU_ROPE_ABSOLUTE && mode != PALU_ROPE_CHUNK_RELATIVE)
+    return fail(PALU_ERR_INVALID, "RoPE mode must be PALU_ROPE_ABSOLUTE or PALU_ROPE_CHUNK_RELATIVE");
+  g_rope_mode = mode;
   return PALU_OK;
 }
 

@@ -6,6 +6,7 @@ directory. There is no fallback: if the library or a CUDA device is missing, eve
 from __future__ import annotations
 
 import ctypes
+import threading
 import os
 from pathlib import Path
 
@@ -21,11 +22,13 @@ PALU_BF16, PALU_F32 = 0, 1
 EXPORTED = ("palu_decode_attn", "palu_decode_attn_static", "palu_decode_attn_paged", "palu_append_latents_paged",
             "palu_rope_q_append", "palu_add_rms_norm", "palu_swiglu",
             "palu_workspace_bytes", "palu_choose_splits", "palu_append_latents",
-            "palu_plain_gqa_decode", "palu_pack_cs_table", "palu_set_kernel", "palu_kernel_for", "palu_read_status",
+            "palu_plain_gqa_decode", "palu_pack_cs_table", "palu_set_kernel", "palu_set_rope_mode", "palu_kernel_for",
+            "palu_read_status",
             "palu_set_wait_limit", "palu_decode_attn_f8", "palu_quantize_latents_f8", "palu_append_latents_f8",
             "palu_decode_attn_f4", "palu_quantize_latents_f4", "palu_append_latents_f4",
             "palu_last_error", "palu_version")
 PALU_KERNEL_AUTO, PALU_KERNEL_MMA, PALU_KERNEL_TC = 0, 1, 2
+PALU_ROPE_ABSOLUTE, PALU_ROPE_CHUNK_RELATIVE = 0, 1
 
 
 class DecodeDims(ctypes.Structure):
@@ -92,6 +95,8 @@ def load() -> ctypes.CDLL:
     lib.palu_pack_cs_table.restype = ctypes.c_int
     lib.palu_set_kernel.argtypes = [i32]
     lib.palu_set_kernel.restype = ctypes.c_int
+    lib.palu_set_rope_mode.argtypes = [i32]
+    lib.palu_set_rope_mode.restype = ctypes.c_int
     lib.palu_set_wait_limit.argtypes = [i64, i32]
     lib.palu_set_wait_limit.restype = ctypes.c_int
     lib.palu_kernel_for.argtypes = [dims_p]
@@ -189,6 +194,19 @@ def set_kernel(which: int) -> None:
     """Choose the decode kernel family (PALU_KERNEL_AUTO / _MMA / _TC) for this process."""
     check(load().palu_set_kernel(int(which)))
     _KERNEL[0] = int(which)
+
+
+_ROPE = threading.local()
+
+
+def set_rope_mode(mode: int) -> None:
+    """RoPE form of this thread's following decode calls (palu_set_rope_mode, thread-local in the library):
+    PALU_ROPE_ABSOLUTE (the reference op's Phase 1) or PALU_ROPE_CHUNK_RELATIVE (its Phase 2). The library
+    call is made only when the thread's mode changes."""
+    mode = int(mode)
+    if getattr(_ROPE, "mode", PALU_ROPE_ABSOLUTE) != mode:
+        check(load().palu_set_rope_mode(mode))
+        _ROPE.mode = mode
 
 
 def set_wait_limit(wait_ns: int = 0, starve_v: bool = False) -> None:

@@ -68,7 +68,8 @@ class PaluAttention:
                  rope_scaling: Optional[dict] = LLAMA3_SCALING, shard: Optional[KVShard] = None,
                  device: str = "cuda", cache_dtype: torch.dtype = torch.bfloat16,
                  proj_dtype: torch.dtype = torch.float32,
-                 paged_attention_config: Optional[PagedAttentionConfig] = None, latent_dtype: str = "bf16"):
+                 paged_attention_config: Optional[PagedAttentionConfig] = None, latent_dtype: str = "bf16",
+                 cs_recurrence: bool = False):
         if head_dim != fused.HEAD_DIM:
             raise RuntimeError(f"head_dim must be {fused.HEAD_DIM}, got {head_dim}")
         gs = lowrank.group_size
@@ -141,6 +142,10 @@ class PaluAttention:
         cos, sin = fused.cos_sin_tables(head_dim, tab_len, rope_theta, rope_scaling)
         self.cos, self.sin = cos.to(dev), sin.to(dev)                                      # fp32 [>= S, hd]
         self.cs_tab = fused.cs_table(cos, sin, tab_len)[None, None].to(dev, bf)           # [1, 1, S, 2hd]
+        # The reference's PaluRuntime.cs_recurrence (convert.py:36; attention.py:74-75, 152): the op's Phase 2,
+        # chunk-relative key angles with the query rotated per chunk, switched on by rot_step / trans_mat.
+        self.phase2 = ({"rot_step": fused.rot_step_table(cos, sin, min(128, tab_len - 1)).to(dev), "trans_mat": fused.trans_mat_tile()}
+                       if cs_recurrence else {})
         if latent_dtype != "bf16":
             cls = fused.F4Latents if latent_dtype == "f4" else fused.F8Latents
             self.k_cache = cls.empty(max_batch, self.ng, max_seq, self.r_k, device=dev)
@@ -250,7 +255,7 @@ class PaluAttention:
         # bf16 projections take the op's output in bf16: the rounding _out's input cast would apply anyway
         odt = torch.bfloat16 if self.proj_dtype == torch.bfloat16 else torch.float32
         attn = self.attend_op(q[None], kc, self.w_rot, self.cs_tab, vc, self.head_dim_v, pos, u_v=self.u_v,
-                              scale=self.scale, out_dtype=odt,
+                              scale=self.scale, out_dtype=odt, **self.phase2,
                               **({"page_table_tensor": pt} if pt is not None else {}))[0]
         y = self._out(attn, out_fp32)
         return y.view(1, 1, B, self.dim) if shape4 else y

@@ -10,10 +10,14 @@ tests/test_palu_sdpa_device.py:84-88, 255-258). The op itself runs in libpalu_b2
 * V is either the latent itself (absorbed into ``wo``, M-LRD) or rebuilt per head through ``u_v``
   (G-LRD), and the split-K partials are merged by a second kernel.
 
-Tensix-only knobs (``rot_step``/``trans_mat`` Phase 2 tables, ``rot_mode``, ``table_mcast``,
-``heads_per_core``, ``program_config``, ``compute_kernel_config``, ``memory_config``) are accepted and
-validated the way the reference validates them, and do not change the B200 computation: the B200
-kernels always read the table by absolute position and always share a group latent across the group.
+``rot_step``/``trans_mat`` keep the reference's meaning as the Phase 2 switch (fused.py:1-14): passed
+together, the keys are rotated by chunk-relative angles (table rows 0..127, read once per CTA) and the
+query by each 128-position chunk's base row, R_p = R_{128 t} R_j; their contents are not read (the B200
+kernel takes the base rotation from the table row itself, so no fp32 recurrence accumulates). Without
+them (Phase 1) every key is rotated by its own table row. The other Tensix-only knobs (``rot_mode``,
+``table_mcast``, ``heads_per_core``, ``program_config``, ``compute_kernel_config``, ``memory_config``)
+are accepted and validated the way the reference validates them and do not change the B200
+computation: the B200 kernels always share a group latent across the group.
 """
 from __future__ import annotations
 
@@ -102,8 +106,9 @@ def cs_table(cos: torch.Tensor, sin: torch.Tensor, seq_len: int) -> torch.Tensor
 
 
 def rot_step_table(cos: torch.Tensor, sin: torch.Tensor, chunk: int) -> torch.Tensor:
-    """[32, 2 hd] fp32 [cos(c f) | sin(c f)] rows (fused.py:76-79). Accepted by the op for surface
-    compatibility; the B200 kernels read absolute positions and do not need it."""
+    """[32, 2 hd] fp32 [cos(c f) | sin(c f)] rows (fused.py:76-79). Passing it (with ``trans_mat``) to
+    ``palu_sdpa_decode`` selects Phase 2; the B200 kernel reads each chunk's base rotation from the table
+    row itself, so the contents are not used."""
     return torch.cat([cos[chunk], sin[chunk]]).expand(32, -1).contiguous().float()
 
 
@@ -338,7 +343,7 @@ def append_latents_f8(new_k, new_v, cur_pos, k_cache: F8Latents, v_cache: F8Late
 
 def decode(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, *, u_k_ld=HEAD_DIM, u_v=None, scale=None,
            out=None, out_dtype=torch.bfloat16, splits=0, workspace=None, page_table=None,
-           check_status=None, _checked=False) -> torch.Tensor:
+           check_status=None, chunk_relative=False, _checked=False) -> torch.Tensor:
     """Low-level entry (no reference-surface validation): the arrays are already in the library's layout.
 
     q [B, nh, 128] bf16; k_latent [B, n_groups, S, r_k]; v_latent [B, n_groups, S, r_v]; u_k rows of
@@ -349,7 +354,9 @@ def decode(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, *, u_k_ld=HEAD_DIM, u_
     positions (palu_decode_attn_paged).
     fp8 caches: k_latent and v_latent as ``F8Latents`` (palu_decode_attn_f8; contiguous caches).
     ``check_status`` (default: the PALU_CHECK_STATUS environment variable) waits for the call and raises
-    RuntimeError if a bounded device wait expired, as the reference op raises on a failed run."""
+    RuntimeError if a bounded device wait expired, as the reference op raises on a failed run.
+    ``chunk_relative`` selects the reference op's Phase 2 RoPE (palu_set_rope_mode): key position
+    p = 128 t + j rotated by table row j and the query of chunk t rotated back by row 128 t."""
     f8 = isinstance(k_latent, F8Latents)
     if f8 != isinstance(v_latent, F8Latents) or (f8 and k_latent.fmt != v_latent.fmt):
         raise RuntimeError("k_latent and v_latent must both be bf16 or both fp8 (F8Latents) or both fp4 (F4Latents)")
@@ -373,6 +380,7 @@ def decode(q, k_latent, v_latent, u_k, cs_pairs, cur_pos, *, u_k_ld=HEAD_DIM, u_
         workspace = _workspace_for(d, q.device, need)
     odt = _lib.PALU_F32 if out.dtype == torch.float32 else _lib.PALU_BF16
     sc = HEAD_DIM ** -0.5 if scale is None else float(scale)
+    _lib.set_rope_mode(_lib.PALU_ROPE_CHUNK_RELATIVE if chunk_relative else _lib.PALU_ROPE_ABSOLUTE)
     if f8:
         fn = _lib.load().palu_decode_attn_f4 if k_latent.fmt == "f4" else _lib.load().palu_decode_attn_f8
         _lib.check(fn(
@@ -492,7 +500,7 @@ def palu_sdpa_decode(q, k_latent, w_rot, cs_tab, v_latent, head_dim_v, cur_pos_t
     out = decode(_bf16(q[0]), k_latent.contiguous(), v_latent.contiguous(), wb, pack_cs_table(cs_tab), pos,
                  u_k_ld=wb.shape[-1], u_v=_bf16(u_v.reshape(n_kv, r_v, HEAD_DIM)) if u_v is not None else None,
                  scale=scale, out_dtype=out_dtype, splits=splits, page_table=pt, check_status=check_status,
-                 _checked=True)
+                 chunk_relative=rot_step is not None, _checked=True)
     return out.unsqueeze(0)
 
 

@@ -91,7 +91,8 @@ class PaluDecoder:
     def __init__(self, cfg: DecoderConfig, ranks: Sequence[Tuple[int, int]], *, max_batch: int, max_seq: int,
                  seed: int = 0, device: str = "cuda", rank: int = 0, world: int = 1,
                  proj_dtype: torch.dtype = torch.bfloat16, keep_source: bool = False,
-                 paged_attention_config: Optional[PagedAttentionConfig] = None, latent_dtype: str = "bf16"):
+                 paged_attention_config: Optional[PagedAttentionConfig] = None, latent_dtype: str = "bf16",
+                 cs_recurrence: bool = False):
         if len(ranks) != cfg.n_layers:
             raise ValueError(f"{len(ranks)} rank pairs for {cfg.n_layers} layers")
         if cfg.ffn_dim % world or cfg.n_kv_heads % world:
@@ -134,7 +135,8 @@ class PaluDecoder:
             attn = PaluAttention(wq, wo, lr, cfg.n_heads, cfg.n_kv_heads, max_batch=max_batch,
                                  max_seq=max_seq, head_dim=hd, rope_theta=cfg.rope_theta,
                                  rope_scaling=cfg.rope_scaling, shard=shard, device=device, proj_dtype=dt,
-                                 paged_attention_config=paged_attention_config, latent_dtype=latent_dtype)
+                                 paged_attention_config=paged_attention_config, latent_dtype=latent_dtype,
+                                 cs_recurrence=cs_recurrence)
             w1f = randn(cfg.ffn_dim, D, scale=D ** -0.5)
             w3f = randn(cfg.ffn_dim, D, scale=D ** -0.5)
             w2f = randn(D, cfg.ffn_dim, scale=cfg.ffn_dim ** -0.5)
