@@ -102,8 +102,9 @@ struct TcParams {
   const int8_t* v_exp;
   // Chunk-relative RoPE (the reference's Phase 2, fused.py:1-14): nonzero rotates key position
   // p = 128 t + j by the table rows j (0..127, loaded once per CTA) and rotates the query of tile t by
-  // row 128 t the other way, R_p = R_{128 t} R_j, instead of reading row p for every key. `cs` is the
-  // packed table (palu_pack_cs_table rows) the query rotation reads.
+  // row 128 t the other way, R_p = R_{128 t} R_j, instead of reading row p for every key. The host launches
+  // the kernel's REL instantiation for it. `cs` is the packed table (palu_pack_cs_table rows) the query
+  // rotation reads.
   int rel;
   const uint32_t* cs;
 };
@@ -579,7 +580,10 @@ PALU_DEVINL int role_of(int warp) {
 // PAGED: the caches are paged (TcParams.page_table set). A template parameter rather than a runtime branch,
 // so that the contiguous-cache kernel carries none of the paged producers' code: with it the body fit the
 // instruction cache worse, and dropping it measured 2-4 % faster on B200.
-template <int KBK, int KBV, bool PAGED, int NP, bool F8 = false, bool F4 = false>
+// REL: chunk-relative RoPE (TcParams.rel), likewise a template parameter: with both RoPE forms behind a runtime
+// flag the chunk-relative kernel measured 151.9 us at the bench workload against 141.5 us for the specialised
+// body (no_instruction stalls 1.47 per issued instruction against 0.83 before the flag).
+template <int KBK, int KBV, bool PAGED, int NP, bool F8 = false, bool F4 = false, bool REL = false>
 __global__ void __launch_bounds__(kThreads, 1)
     palu_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                           const __grid_constant__ CUtensorMap tm_tab, const TcParams p) {
@@ -590,7 +594,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int NS_T = NP * T_SLOTS;  // table chunk slots, [group][slot]
   // Chunk-relative RoPE: slots 0..3 hold table rows 0..127 (chunk c in slot c) for the whole kernel, loaded
   // once by group 0's K producer; nothing releases or refills them.
-  const bool rel = rel_fits<Lay, NP>() && p.rel != 0;
+  constexpr bool rel = REL && rel_fits<Lay, NP>();
   // V^T as PV's A operand: one M = 64 block (V at most 64 wide), one M = 128 block (at most 128), or two M = 128
   // blocks (at most 256; a block's rows past the latent width are the TMA's zero fill).
   constexpr int NMB = KBV <= 2 ? 1 : 2;

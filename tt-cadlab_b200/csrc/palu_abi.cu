@@ -201,17 +201,26 @@ void set_pages(Params& p, const palu_page_table* pg) {
   while (pg && (1 << p.blk_shift) < pg->block_size) ++p.blk_shift;
 }
 
-template <int KBK, int KBV, bool PAGED, int NP = 2, bool F8 = false, bool F4 = false>
-int launch_tc(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mt, const palu::tc::TcParams& p,
-              cudaStream_t stream) {
+template <int KBK, int KBV, bool PAGED, int NP, bool F8, bool F4, bool REL>
+int launch_tc_form(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mt, const palu::tc::TcParams& p,
+                   cudaStream_t stream) {
   using Lay = palu::tc::Layout<KBK, KBV, NP, F8>;
-  auto kern = palu::tc::palu_decode_tc_kernel<KBK, KBV, PAGED, NP, F8, F4>;
-  if (p.rel && !palu::tc::rel_fits<Lay, NP>())
-    return fail(PALU_ERR_INVALID, "chunk-relative RoPE: this kernel layout has no room for the fixed table rows");
+  auto kern = palu::tc::palu_decode_tc_kernel<KBK, KBV, PAGED, NP, F8, F4, REL>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::TOTAL) != cudaSuccess)
     return cuda_check("cudaFuncSetAttribute(decode tc)");
   kern<<<dim3(p.ctas, p.n_kv, 1), palu::tc::kThreads, Lay::TOTAL, stream>>>(mk, mv, mt, p);
   return cuda_check("decode tc kernel launch");
+}
+
+// The RoPE form is a template parameter of the kernel (one body per form); p.rel picks the instantiation.
+template <int KBK, int KBV, bool PAGED, int NP = 2, bool F8 = false, bool F4 = false>
+int launch_tc(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mt, const palu::tc::TcParams& p,
+              cudaStream_t stream) {
+  using Lay = palu::tc::Layout<KBK, KBV, NP, F8>;
+  if (!p.rel) return launch_tc_form<KBK, KBV, PAGED, NP, F8, F4, false>(mk, mv, mt, p, stream);
+  if (!palu::tc::rel_fits<Lay, NP>())
+    return fail(PALU_ERR_INVALID, "chunk-relative RoPE: this kernel layout has no room for the fixed table rows");
+  return launch_tc_form<KBK, KBV, PAGED, NP, F8, F4, true>(mk, mv, mt, p, stream);
 }
 
 int run_tc(const void* q, const void* k, const void* v, const void* u_k, int64_t u_k_ld, const void* cs_pairs,
