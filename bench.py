@@ -515,7 +515,7 @@ def run_layer(args, ws, rank, local):
             in_d.copy_(in_h, non_blocking=True)
             append(nk_d, nv_d, pos_d, L["k"], L["v"], **({"page_table": pt} if pt is not None else {}))
             fused.decode(q_d, L["k"], L["v"], L["u"], L["cs"], pos_d, u_v=L["u_v"], out=out, workspace=ws_buf,
-                         page_table=pt)
+                         page_table=pt, chunk_relative=rel)
             torch.mm(out.view(B, n_q * width), L["wo"].t(), out=y)
             y_h.copy_(y, non_blocking=True)
         graph_body()
