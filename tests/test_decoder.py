@@ -161,8 +161,8 @@ def _tp_rank(rank, world, port, out_q):
         tokens = torch.randint(0, cfg.vocab, (B, P), generator=torch.Generator().manual_seed(9))
         pre = m.prefill_logits(tokens)
         dec = m.decode_logits(pre.argmax(-1), torch.full((B,), P, dtype=torch.int32))
-        if rank == 0:
-            out_q.put((pre, dec))
+        if rank == 0:  # numpy arrays travel by value (a shared-memory tensor can race this process's exit)
+            out_q.put((pre.numpy(), dec.numpy()))
     finally:
         dist.destroy_process_group()
 
@@ -180,7 +180,7 @@ def test_two_rank_tensor_parallel_decoder_equals_one_rank():
     procs = [ctx.Process(target=_tp_rank, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    pre2, dec2 = q.get(timeout=180)
+    pre2, dec2 = (torch.from_numpy(a) for a in q.get(timeout=180))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0

@@ -70,8 +70,8 @@ def _rank_main(rank, world, port, grouped, out_q):
         o = _attend(x["q"], x["k_lat"], x["v_lat"], x["u_k"], x["u_v"], L["pos"], L["cos"], L["sin"],
                     len(sh.kv))
         part = all_reduce_layer_output(layer_output_partial(o, x["wo"]))
-        if rank == 0:
-            out_q.put(part)
+        if rank == 0:  # a numpy array travels by value (a shared-memory tensor can race this process's exit)
+            out_q.put(part.numpy())
     finally:
         dist.destroy_process_group()
 
@@ -86,7 +86,7 @@ def test_sharded_layer_equals_unsharded(grouped, world):
     procs = [ctx.Process(target=_rank_main, args=(r, world, port, grouped, q)) for r in range(world)]
     for p in procs:
         p.start()
-    got = q.get(timeout=90)
+    got = torch.from_numpy(q.get(timeout=90))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0

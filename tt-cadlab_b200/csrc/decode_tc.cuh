@@ -1254,7 +1254,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // head's query heads; the rest stay zero) x 128 dims in [even | odd] order: K-block 0 = even dims,
     // K-block 1 = odd dims (64 fp16 per 128-B row). Item (row, 16-byte chunk of 8 reordered dims); bf16
     // q is exact in fp16. The QK issuer waits for the buffer's barrier.
-    // Chunk-relative RoPE (`tile` >= 0): the q of the tile's row rotated by the tile's base position
+    // Chunk-relative RoPE (`rel`; `tile` is then the tile's index in its row, else -1): the q of the tile's
+    // row rotated by the tile's base position
     // p0 = 128 tile the other way, q' = R_{p0}^T q (q'(2f) = q(2f) cos + q(2f+1) sin, q'(2f+1) = q(2f+1) cos -
     // q(2f) sin, with the packed table's row p0), in fp32 and rounded once to fp16, so that
     // q' . R_j k = q . R_{p0 + j} k.
@@ -1266,7 +1267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                          16 * c8);
         const uint4 x0 = qr[0], x1 = qr[1];  // source dims 16 c8 .. + 15: (even, odd) of frequencies 8 c8 .. + 7
         uint32_t w[4];
-        if (tile >= 0) {
+        if (rel) {  // a constant of the instantiation: each body keeps one of the two paths
           // cosines of frequencies 8 c8 .. + 7 at p0: packed words 16 (c8 >> 1) + 4 (c8 & 1) .. + 3; sines 8 words on
           const uint4* tr = reinterpret_cast<const uint4*>(p.cs + (size_t)tile * kTile * 64 + 16 * (c8 >> 1) + 4 * (c8 & 1));
           const uint4 cw = __ldg(tr), sw = __ldg(tr + 2);
