@@ -6,7 +6,6 @@ directory. There is no fallback: if the library or a CUDA device is missing, eve
 from __future__ import annotations
 
 import ctypes
-import threading
 import os
 from pathlib import Path
 
@@ -196,17 +195,12 @@ def set_kernel(which: int) -> None:
     _KERNEL[0] = int(which)
 
 
-_ROPE = threading.local()
-
-
 def set_rope_mode(mode: int) -> None:
     """RoPE form of this thread's following decode calls (palu_set_rope_mode, thread-local in the library):
-    PALU_ROPE_ABSOLUTE (the reference op's Phase 1) or PALU_ROPE_CHUNK_RELATIVE (its Phase 2). The library
-    call is made only when the thread's mode changes."""
-    mode = int(mode)
-    if getattr(_ROPE, "mode", PALU_ROPE_ABSOLUTE) != mode:
-        check(load().palu_set_rope_mode(mode))
-        _ROPE.mode = mode
+    PALU_ROPE_ABSOLUTE (the reference op's Phase 1) or PALU_ROPE_CHUNK_RELATIVE (its Phase 2). Set on every
+    call rather than cached here, so a caller that also uses the C setter directly cannot leave the two out
+    of step (about 1 us of host time per decode call)."""
+    check(load().palu_set_rope_mode(int(mode)))
 
 
 def set_wait_limit(wait_ns: int = 0, starve_v: bool = False) -> None:

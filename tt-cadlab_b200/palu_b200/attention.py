@@ -144,8 +144,10 @@ class PaluAttention:
         self.cs_tab = fused.cs_table(cos, sin, tab_len)[None, None].to(dev, bf)           # [1, 1, S, 2hd]
         # The reference's PaluRuntime.cs_recurrence (convert.py:36; attention.py:74-75, 152): the op's Phase 2,
         # chunk-relative key angles with the query rotated per chunk, switched on by rot_step / trans_mat.
-        self.phase2 = ({"rot_step": fused.rot_step_table(cos, sin, min(128, tab_len - 1)).to(dev), "trans_mat": fused.trans_mat_tile()}
-                       if cs_recurrence else {})
+        self.phase2 = {}
+        if cs_recurrence:
+            self.phase2 = {"rot_step": fused.rot_step_table(cos, sin, min(128, tab_len - 1)).to(dev),
+                           "trans_mat": fused.trans_mat_tile()}
         if latent_dtype != "bf16":
             cls = fused.F4Latents if latent_dtype == "f4" else fused.F8Latents
             self.k_cache = cls.empty(max_batch, self.ng, max_seq, self.r_k, device=dev)
